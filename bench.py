@@ -1,0 +1,490 @@
+#!/usr/bin/env python
+"""Benchmark of the NVFP4 FFN path on B200: one FFN layer (d_model 1536, d_ff 8960,
+GELU-tanh, bias) over 7680 tokens per GPU, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
+
+A step is one pass of the FFN layer over a batch of 7680 synthetic tokens
+(two 48x80 latent frames, Student-t(4) x 0.5 activations, N(0, 0.02) weights,
+N(0, 0.01) biases; seeded).  Token rows are independent, so each rank runs
+its own batch with replicated weights and no collective in the step (weak
+scaling); the output all-gather the path uses after a stack is timed
+separately (`gather`).  Inputs rotate over 8 distinct (activation, weight)
+sets, 312 MB in all, so no step finds its operands in the 126 MB L2.
+
+Prints one JSON line (rank 0).  `value` is whole-job tokens/s with inputs
+resident in HBM; `e2e` is the same metric through the public module API with
+host buffers (pinned H2D of the input and D2H of the output inside the timed
+region); `roofline` describes the GEMM kernel; `cpu_baseline` times the
+reference arithmetic (the CPU oracle) on this host.
+
+`--impl reference` times the reference's NVFP4 FFN arithmetic on the host CPU
+(the oracle restatement; the reference itself needs FlashInfer on a GPU) with
+all host threads, on bounded samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+D_MODEL, D_FF = 1536, 8960
+TOKENS = 7680
+FLOP_PER_TOKEN = 2 * D_MODEL * D_FF * 2
+ROTATE = 8
+METRIC = "nvfp4_ffn_tokens_per_s"
+WORKLOAD = "ffn_layer_d1536_ff8960_gelu_tanh_bias_7680tok_per_gpu"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("native", "reference"), default="native")
+    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0,
+                    help="wall-time budget of the CPU baseline sample")
+    return ap.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the GPU is busy."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power)}
+
+
+# ---------------------------------------------------------------- CPU legs
+def cpu_ffn_tokens_per_s(steps: int, warmup: int, seconds: float, log=print) -> dict:
+    """Reference NVFP4 FFN arithmetic (the oracle, fp32 matmul) on host threads."""
+    from oracle import nvfp4_oracle as O
+    from flashvsr_optimizations_b200 import workloads as W
+    threads = os.cpu_count() or 1
+    w1, b1 = W.linear_params(D_FF, D_MODEL, seed=20, b_std=0.01)
+    w2, b2 = W.linear_params(D_MODEL, D_FF, seed=21, b_std=0.01)
+    l1, l2 = O.OracleQuantLinear(w1, b1), O.OracleQuantLinear(w2, b2)
+    # calibrate the per-step sample so the whole run fits the time budget
+    probe = W.student_t(64, D_MODEL, seed=1)
+    t0 = time.perf_counter()
+    O.ffn_forward(probe, l1, l2, fp32_matmul=True)
+    t0 = time.perf_counter()
+    O.ffn_forward(probe, l1, l2, fp32_matmul=True)
+    per_tok = (time.perf_counter() - t0) / 64
+    rows = int(seconds / max(1, steps + warmup) / max(per_tok, 1e-6))
+    rows = max(16, min(1024, rows // 16 * 16))
+    x_all = W.student_t(TOKENS, D_MODEL, seed=1)
+    for i in range(warmup):
+        O.ffn_forward(x_all[(i * rows) % (TOKENS - rows):][:rows], l1, l2, fp32_matmul=True)
+    times = []
+    for i in range(steps):
+        xs = x_all[(i * rows) % (TOKENS - rows):][:rows]
+        t = time.perf_counter()
+        O.ffn_forward(xs, l1, l2, fp32_matmul=True)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    return {"value": rows * steps / total, "unit": "tokens/s", "cores": threads,
+            "kind": "port", "rows_per_step": rows, "seconds": total,
+            "sample": (f"{steps} steps of {rows} tokens from the 7680-token layer workload; numpy oracle "
+                       f"(quantize, dequantize, fp32 BLAS matmul, bias, GELU-tanh, requantize); "
+                       f"weights quantized once outside the timing; {threads} host threads")}
+
+
+# ---------------------------------------------------------------- GPU setup
+def make_sets(torch, ops, dev, tokens, rank):
+    """ROTATE distinct (x, layer-1, layer-2) sets on the device, seeded per rank / set."""
+    sets = []
+    for i in range(ROTATE):
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1000 * rank + i + 1)
+        z = torch.randn(tokens, D_MODEL, device=dev, generator=gen)
+        chi = (torch.randn(4, tokens, D_MODEL, device=dev, generator=gen) ** 2).sum(0) / 4.0
+        x = (0.5 * z / chi.sqrt()).to(torch.bfloat16)          # Student-t(4) x 0.5
+        layers = []
+        for (n, k) in ((D_FF, D_MODEL), (D_MODEL, D_FF)):
+            w = (torch.randn(n, k, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+            b = (torch.randn(n, device=dev, generator=gen) * 0.01).to(torch.bfloat16)
+            g = ops.global_scale(w)
+            q, s = ops.nvfp4_quantize(w, g)
+            layers.append((q, s, g, b))
+        sets.append((x, layers))
+    return sets
+
+
+def fp4_library_peak(torch, dev) -> float | None:
+    """Dense NVFP4 throughput of cuBLASLt (torch._scaled_mm) at 8192^3, TFLOP/s, or None."""
+    try:
+        n = 8192
+        a = torch.randint(0, 256, (n, n // 2), dtype=torch.uint8, device=dev).view(torch.float4_e2m1fn_x2)
+        b = torch.randint(0, 256, (n, n // 2), dtype=torch.uint8, device=dev).view(torch.float4_e2m1fn_x2)
+        sa = torch.full((n * n // 16,), 0x38, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+        sb = torch.full((n * n // 16,), 0x38, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+        f = lambda: torch._scaled_mm(a, b.t(), sa, sb, out_dtype=torch.bfloat16)  # noqa: E731
+        for _ in range(3):
+            f()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(20):
+            f()
+        e.record()
+        e.synchronize()
+        return 2 * n ** 3 * 20 / (s.elapsed_time(e) * 1e-3) / 1e12
+    except Exception:
+        return None
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            pass
+    return {}
+
+
+def main():
+    args = parse()
+    rank, local_rank, world = env_rank()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    import flashvsr_optimizations_b200 as fvq
+    from flashvsr_optimizations_b200 import _lib, ops
+    from flashvsr_optimizations_b200.ffn_quantization import NVFP4FFN
+    lib = _lib.load()
+    tokens = args.tokens
+    sets = make_sets(torch, ops, dev, tokens, rank)
+    ws_bytes = lib.fvq_nvfp4_ffn_workspace_bytes(tokens, D_MODEL, D_FF)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    ys = [torch.empty(tokens, D_MODEL, dtype=torch.bfloat16, device=dev) for _ in range(ROTATE)]
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    # pre-bound C-ABI calls (fvq_nvfp4_ffn), one per rotating set
+    structs = []
+    for x, ((q1, s1, g1, b1), (q2, s2, g2, b2)) in sets:
+        l1 = _lib.FvqLinear(q1.data_ptr(), s1.data_ptr(), g1.data_ptr(), b1.data_ptr(), D_MODEL, D_FF)
+        l2 = _lib.FvqLinear(q2.data_ptr(), s2.data_ptr(), g2.data_ptr(), b2.data_ptr(), D_FF, D_MODEL)
+        structs.append((x, l1, l2))
+    ffn_call = lib.fvq_nvfp4_ffn
+
+    def step(i):
+        x, l1, l2 = structs[i % ROTATE]
+        rc = ffn_call(x.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2), ys[i % ROTATE].data_ptr(),
+                      ws.data_ptr(), ws_bytes, sptr)
+        if rc != 0:
+            raise RuntimeError(lib.fvq_last_error().decode())
+
+    def barrier_sync():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    barrier_sync()
+    gpu_uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    sampler = ClockSampler(gpu_uuid)
+    sampler.start()
+    time.sleep(0.15)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier_sync()
+    start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    end.record(stream)
+    barrier_sync()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total_tokens = tokens * args.steps * world
+    value = total_tokens / (ms * 1e-3)
+    tflops = value * FLOP_PER_TOKEN / 1e12
+
+    # ---- per-kernel timing (same kernels through the per-op C-ABI entry points)
+    kt = kernel_timing(torch, lib, _lib, sets, tokens, dev, stream, min(args.steps, 400))
+    if world > 1:
+        t = torch.tensor([kt["gemm_ms"], kt["quant_h_ms"]], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        kt["gemm_ms"], kt["quant_h_ms"] = (float(v) for v in t.tolist())
+
+    # ---- end to end through the public module API with host buffers
+    e2e = e2e_timing(torch, dist, fvq, NVFP4FFN, sets, tokens, dev, stream, world,
+                     min(args.steps, 500), args.warmup)
+
+    # ---- output gather (NCCL all_gather over NVLink) of one layer's output
+    gather = None
+    if world > 1:
+        out = torch.empty(world * tokens, D_MODEL, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            dist.all_gather_into_tensor(out, ys[0])
+        barrier_sync()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(20):
+            dist.all_gather_into_tensor(out, ys[0])
+        e.record(stream)
+        barrier_sync()
+        gms = s.elapsed_time(e) / 20
+        t = torch.tensor([gms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gms = float(t.item())
+        gather = {"ms": gms, "bytes": world * tokens * D_MODEL * 2,
+                  "busbw_GBps": (world - 1) * tokens * D_MODEL * 2 / (gms * 1e-3) / 1e9}
+
+    peaks = measured_peaks()
+    fp4_cublas = fp4_library_peak(torch, dev) if rank == 0 else None
+    bf16_burst = peaks.get("bf16_tflops")
+    if bf16_burst:
+        peak, peak_src = 4.0 * bf16_burst, "4 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json); dense FP4 runs at 4x bf16 on B200"
+    else:
+        peak, peak_src = 4.0 * 1590.0, "4 x fallback bf16 1.59 PFLOP/s"
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    gemm_flop = tokens * FLOP_PER_TOKEN
+    achieved = gemm_flop / (kt["gemm_ms"] * 1e-3) / 1e12
+    traffic = None
+    tp = ROOT / "profiles" / "gemm_traffic.json"
+    if tp.exists():
+        try:
+            traffic = json.loads(tp.read_text()).get("dram_bytes_per_gemm_pair")
+        except ValueError:
+            traffic = None
+    result = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4(e2m1+e4m3 scales), fp32 accumulate, bf16 io",
+        "data": "synthetic (seeded Student-t(4)x0.5 activations, N(0,0.02) weights, N(0,0.01) bias)",
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": tokens, "d_model": D_MODEL, "d_ff": D_FF,
+                   "layers": 1, "parallelism": f"token-row shards x{world}, replicated weights",
+                   "l2": f"inputs rotate over {ROTATE} distinct activation/weight sets (312 MB > 126 MB L2)"},
+        "tflops": tflops, "tflops_frac_of_fp4_peak": tflops / peak,
+        "gpu_launches": 5 * args.steps,
+        "roofline": {"bound": "tensor", "kernel": "nvfp4_gemm_kernel (GEMM1 + GEMM2 of the layer)",
+                     "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "algorithmic_flop_per_launch_pair": gemm_flop},
+        "quantize": {"kernel": "quantize_kernel on the 7680x8960 intermediate",
+                     "GBps": kt["quant_h_gbs"], "peak_GBps": hbm, "frac": kt["quant_h_gbs"] / hbm,
+                     "ms": kt["quant_h_ms"]},
+        "kernels_ms": kt,
+        "e2e": e2e,
+        "clocks": clocks,
+    }
+    if gather:
+        result["gather"] = gather
+    if fp4_cublas:
+        result["fp4_cublas_8192_tflops"] = fp4_cublas
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_ffn_tokens_per_s(5, 1, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def kernel_timing(torch, lib, _lib, sets, tokens, dev, stream, steps) -> dict:
+    """Per-kernel CUDA-event timing of the layer's five launches (GEMMs and H-quantize)."""
+    import ctypes as C
+    d, f = D_MODEL, D_FF
+    st = stream.cuda_stream
+    codes_x = torch.empty(tokens, d // 2, dtype=torch.uint8, device=dev)
+    sf_x = torch.empty((tokens + 127) // 128 * 128, d // 16, dtype=torch.uint8, device=dev)
+    h = torch.empty(tokens, f, dtype=torch.bfloat16, device=dev)
+    codes_h = torch.empty(tokens, f // 2, dtype=torch.uint8, device=dev)
+    sf_h = torch.empty((tokens + 127) // 128 * 128, f // 16, dtype=torch.uint8, device=dev)
+    y = torch.empty(tokens, d, dtype=torch.bfloat16, device=dev)
+    scal = torch.zeros(64, dtype=torch.float32, device=dev)
+    amax_ws = torch.zeros(lib.fvq_amax_workspace_bytes(), dtype=torch.uint8, device=dev)
+    gx, gh, amax_h = scal[0:1], scal[1:2], scal[2:3]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
+
+    def chk(rc):
+        if rc != 0:
+            raise RuntimeError(lib.fvq_last_error().decode())
+
+    def one(i, e):
+        x, ((q1, s1, g1, b1), (q2, s2, g2, b2)) = sets[i % ROTATE]
+        if e: e[0].record(stream)
+        chk(lib.fvq_amax(x.data_ptr(), x.numel(), None, gx.data_ptr(), amax_ws.data_ptr(),
+                         amax_ws.numel(), st))
+        chk(lib.fvq_nvfp4_quantize(x.data_ptr(), tokens, d, gx.data_ptr(), codes_x.data_ptr(),
+                                   sf_x.data_ptr(), st))
+        amax_h.zero_()
+        if e: e[1].record(stream)
+        chk(lib.fvq_nvfp4_gemm(codes_x.data_ptr(), sf_x.data_ptr(), gx.data_ptr(), q1.data_ptr(),
+                               s1.data_ptr(), g1.data_ptr(), b1.data_ptr(), h.data_ptr(), tokens, f, d,
+                               1, amax_h.data_ptr(), st))
+        if e: e[2].record(stream)
+        chk(lib.fvq_nvfp4_quantize_dynamic(h.data_ptr(), tokens, f, amax_h.data_ptr(), gh.data_ptr(),
+                                           codes_h.data_ptr(), sf_h.data_ptr(), None, 0, st))
+        if e: e[3].record(stream)
+        chk(lib.fvq_nvfp4_gemm(codes_h.data_ptr(), sf_h.data_ptr(), gh.data_ptr(), q2.data_ptr(),
+                               s2.data_ptr(), g2.data_ptr(), b2.data_ptr(), y.data_ptr(), tokens, d, f,
+                               0, None, st))
+        if e: e[4].record(stream)
+
+    for i in range(5):
+        one(i, None)
+    torch.cuda.synchronize(dev)
+    for i in range(steps):
+        one(i, ev[i])
+    torch.cuda.synchronize(dev)
+    qx = [e[0].elapsed_time(e[1]) for e in ev]
+    g1t = [e[1].elapsed_time(e[2]) for e in ev]
+    qh = [e[2].elapsed_time(e[3]) for e in ev]
+    g2t = [e[3].elapsed_time(e[4]) for e in ev]
+    mean = lambda v: sum(v) / len(v)  # noqa: E731
+    qh_bytes = tokens * f * 2 + tokens * f // 2 + (tokens + 127) // 128 * 128 * f // 16
+    return {"quant_x_ms": mean(qx), "gemm1_ms": mean(g1t), "quant_h_ms": mean(qh), "gemm2_ms": mean(g2t),
+            "gemm_ms": mean(g1t) + mean(g2t), "quant_h_gbs": qh_bytes / (mean(qh) * 1e-3) / 1e9,
+            "gemm1_tflops": tokens * 2 * d * f / (mean(g1t) * 1e-3) / 1e12,
+            "gemm2_tflops": tokens * 2 * d * f / (mean(g2t) * 1e-3) / 1e12, "steps": steps}
+
+
+def e2e_timing(torch, dist, fvq, NVFP4FFN, sets, tokens, dev, stream, world, steps, warmup) -> dict:
+    """Same metric through the public module (NVFP4FFN) with pinned host input/output."""
+    from flashvsr_optimizations_b200.ffn_quantization import QuantLinear
+    mods = []
+    for x, ((q1, s1, g1, b1), (q2, s2, g2, b2)) in sets:
+        l1 = QuantLinear.from_quantized(q1, s1, g1, b1, D_MODEL)
+        l2 = QuantLinear.from_quantized(q2, s2, g2, b2, D_FF)
+        mods.append(NVFP4FFN(l1, torch.nn.GELU(approximate="tanh"), l2))
+    xh = [x.cpu().pin_memory() for x, _ in sets]
+    yh = [torch.empty(tokens, D_MODEL, dtype=torch.bfloat16).pin_memory() for _ in range(ROTATE)]
+    xd = torch.empty(tokens, D_MODEL, dtype=torch.bfloat16, device=dev)
+
+    def step(i):
+        j = i % ROTATE
+        xd.copy_(xh[j], non_blocking=True)
+        y = mods[j](xd)
+        yh[j].copy_(y, non_blocking=True)
+
+    with torch.no_grad():
+        for i in range(max(3, warmup)):
+            step(i)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for i in range(steps):
+            step(i)
+        e.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = s.elapsed_time(e)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": tokens * steps * world / (ms * 1e-3), "unit": "tokens/s",
+            "h2d_bytes_per_step": tokens * D_MODEL * 2, "d2h_bytes_per_step": tokens * D_MODEL * 2,
+            "steps": steps, "ms_per_step": ms / steps,
+            "api": "NVFP4FFN.forward (install_ffn's fused module) via torch custom op fvq::nvfp4_ffn"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    res = cpu_ffn_tokens_per_s(args.steps, args.warmup, seconds=60.0)
+    ms_per_step = res["seconds"] / args.steps * 1e3
+    line = {"metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "nvfp4 emulated (fp32 dequantized matmul)", "data": "synthetic (seeded)",
+            "config": {"workload": WORKLOAD, "tokens_per_step": res["rows_per_step"],
+                       "d_model": D_MODEL, "d_ff": D_FF, "layers": 1, "parallelism": "host CPU"},
+            "impl": "reference",
+            "cpu_baseline": {"value": res["value"], "unit": "tokens/s", "cores": res["cores"],
+                             "kind": res["kind"], "sample": res["sample"]},
+            "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,349 @@
+// fvq_api.cu -- the extern "C" boundary (include/fvq.h): argument checks,
+// status codes, per-thread error text, workspace carving and the call
+// sequences of QuantLinear.forward and the FFN.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/fvq.h"
+#include "fvq_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+uint64_t g_wait_limit = fvq::kDefaultWaitLimit;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(FVQ_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_device() {
+  static int ok_cache[64] = {0};  // 0 unknown, 1 ok, -1 bad
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev >= 0 && dev < 64 && ok_cache[dev] == 1) return FVQ_OK;
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0) {
+    return fail(FVQ_EDEVICE, "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev,
+                major, minor);
+  }
+  if (dev >= 0 && dev < 64) ok_cache[dev] = 1;
+  return FVQ_OK;
+}
+
+constexpr size_t kAlign = 256;
+size_t round_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Workspace carving shared by linear and ffn.
+struct Carve {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carve(void* b) : base(static_cast<uint8_t*>(b)) {}
+  uint8_t* take(size_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off += round_up(bytes);
+    return p;
+  }
+};
+
+constexpr size_t kScalarBytes = 256;  // g_x, g_h, amax_h, spare
+
+int check_quant_shape(int64_t rows, int64_t k, const char* who) {
+  if (rows <= 0) return fail(FVQ_EINVAL, "%s: rows must be > 0 (got %lld)", who, (long long)rows);
+  if (k <= 0 || k % 64 != 0)
+    return fail(FVQ_EINVAL, "%s: k must be a positive multiple of 64 (got %lld)", who,
+                (long long)k);
+  if (rows > (int64_t(1) << 31) || k > (int64_t(1) << 24))
+    return fail(FVQ_EINVAL, "%s: shape too large", who);
+  return FVQ_OK;
+}
+
+int check_gemm_shape(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || m > (int64_t(1) << 30))
+    return fail(FVQ_EINVAL, "fvq_nvfp4_gemm: m must be in [1, 2^30] (got %lld)", (long long)m);
+  if (n <= 0 || n % 256 != 0)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_gemm: n must be a positive multiple of 256 (got %lld)",
+                (long long)n);
+  if (k <= 0 || k % 256 != 0)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_gemm: k must be a positive multiple of 256 (got %lld)",
+                (long long)k);
+  if (n * k / 2 > (int64_t(1) << 31) || m * (k / 2) > (int64_t(1) << 40))
+    return fail(FVQ_EINVAL, "fvq_nvfp4_gemm: operand too large");
+  return FVQ_OK;
+}
+
+int gemm_impl(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
+              const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w, const float* alpha,
+              const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k, int epilogue,
+              float* amax_out, cudaStream_t st) {
+  const char* why = nullptr;
+  cudaError_t e = fvq::launch_gemm(a_codes, a_sf, g_a, w_codes, w_sf, g_w, alpha, bias, out, m, n, k,
+                                   epilogue, amax_out, g_wait_limit, st, &why);
+  if (e != cudaSuccess) {
+    if (why) return fail(FVQ_ECUDA, "fvq_nvfp4_gemm: %s", why);
+    return cuda_fail(e, "fvq_nvfp4_gemm launch");
+  }
+  return FVQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fvq_version(void) { return 100; }
+
+const char* fvq_last_error(void) { return g_last_error.c_str(); }
+
+size_t fvq_amax_workspace_bytes(void) { return round_up(fvq::kAmaxWorkspaceBytes); }
+
+int fvq_amax(const uint16_t* x, int64_t numel, float* amax_out, float* g_out, void* workspace,
+             size_t workspace_bytes, void* stream) {
+  if (numel < 0) return fail(FVQ_EINVAL, "fvq_amax: numel < 0");
+  if (numel > 0 && x == nullptr) return fail(FVQ_EINVAL, "fvq_amax: x is NULL");
+  if (workspace == nullptr) return fail(FVQ_EINVAL, "fvq_amax: workspace is NULL");
+  if (workspace_bytes < fvq_amax_workspace_bytes())
+    return fail(FVQ_EWORKSPACE, "fvq_amax: workspace needs %zu bytes, got %zu",
+                fvq_amax_workspace_bytes(), workspace_bytes);
+  if (!aligned16(x) || !aligned16(workspace))
+    return fail(FVQ_EALIGN, "fvq_amax: x and workspace must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  cudaError_t e = fvq::launch_amax(x, numel, amax_out, g_out, static_cast<uint32_t*>(workspace),
+                                   nullptr, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_amax launch");
+  return FVQ_OK;
+}
+
+int fvq_nvfp4_quantize(const uint16_t* x, int64_t rows, int64_t k, const float* g,
+                       uint8_t* codes, uint8_t* sf, void* stream) {
+  if (int rc = check_quant_shape(rows, k, "fvq_nvfp4_quantize")) return rc;
+  if (!x || !g || !codes || !sf) return fail(FVQ_EINVAL, "fvq_nvfp4_quantize: NULL pointer");
+  if (!aligned16(x) || !aligned16(codes) || !aligned16(sf))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_quantize: x, codes and sf must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  cudaError_t e = fvq::launch_quantize(x, rows, k, g, nullptr, nullptr, codes, sf, nullptr,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_quantize launch");
+  return FVQ_OK;
+}
+
+int fvq_nvfp4_quantize_dynamic(const uint16_t* x, int64_t rows, int64_t k, const float* amax_in,
+                               float* g_out, uint8_t* codes, uint8_t* sf, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (int rc = check_quant_shape(rows, k, "fvq_nvfp4_quantize_dynamic")) return rc;
+  if (!x || !codes || !sf) return fail(FVQ_EINVAL, "fvq_nvfp4_quantize_dynamic: NULL pointer");
+  if (!aligned16(x) || !aligned16(codes) || !aligned16(sf))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_quantize_dynamic: x, codes and sf must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float* amax = amax_in;
+  if (amax == nullptr) {
+    if (workspace == nullptr || workspace_bytes < fvq_amax_workspace_bytes())
+      return fail(FVQ_EWORKSPACE, "fvq_nvfp4_quantize_dynamic: workspace needs %zu bytes",
+                  fvq_amax_workspace_bytes());
+    if (!aligned16(workspace))
+      return fail(FVQ_EALIGN, "fvq_nvfp4_quantize_dynamic: workspace must be 16-byte aligned");
+    uint32_t* ws = static_cast<uint32_t*>(workspace);
+    cudaError_t e = fvq::launch_amax(x, rows * k, nullptr, nullptr, ws, nullptr, st);
+    if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_quantize_dynamic amax launch");
+    amax = reinterpret_cast<const float*>(ws + 2);
+  }
+  cudaError_t e = fvq::launch_quantize(x, rows, k, nullptr, amax, g_out, codes, sf, nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_quantize_dynamic launch");
+  return FVQ_OK;
+}
+
+int fvq_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
+                   const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
+                   const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
+                   int epilogue, float* amax_out, void* stream) {
+  if (int rc = check_gemm_shape(m, n, k)) return rc;
+  if (!a_codes || !a_sf || !g_a || !w_codes || !w_sf || !g_w || !out)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_gemm: NULL pointer");
+  if (epilogue != FVQ_EPI_BF16 && epilogue != FVQ_EPI_GELU_AMAX)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_gemm: unknown epilogue %d", epilogue);
+  if (epilogue == FVQ_EPI_GELU_AMAX && amax_out == nullptr)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_gemm: FVQ_EPI_GELU_AMAX needs amax_out");
+  if (!aligned16(a_codes) || !aligned16(a_sf) || !aligned16(w_codes) || !aligned16(w_sf) ||
+      !aligned16(out) || !aligned16(bias))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_gemm: operands, scales, bias and out must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  return gemm_impl(a_codes, a_sf, g_a, w_codes, w_sf, g_w, nullptr, bias, out, m, n, k, epilogue,
+                   amax_out, static_cast<cudaStream_t>(stream));
+}
+
+int fvq_nvfp4_mm(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* w_codes,
+                 const uint8_t* w_sf, const float* alpha, const uint16_t* bias, uint16_t* out,
+                 int64_t m, int64_t n, int64_t k, void* stream) {
+  if (int rc = check_gemm_shape(m, n, k)) return rc;
+  if (!a_codes || !a_sf || !w_codes || !w_sf || !alpha || !out)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_mm: NULL pointer");
+  if (!aligned16(a_codes) || !aligned16(a_sf) || !aligned16(w_codes) || !aligned16(w_sf) ||
+      !aligned16(out) || !aligned16(bias))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_mm: operands, scales, bias and out must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  return gemm_impl(a_codes, a_sf, nullptr, w_codes, w_sf, nullptr, alpha, bias, out, m, n, k,
+                   FVQ_EPI_BF16, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+size_t fvq_nvfp4_linear_workspace_bytes(int64_t rows, int64_t in_features) {
+  if (rows <= 0 || in_features <= 0) return 0;
+  Carve c(nullptr);
+  c.take(fvq::kAmaxWorkspaceBytes);
+  c.take(kScalarBytes);
+  c.take(static_cast<size_t>(rows * in_features / 2));
+  c.take(fvq::sf_bytes(rows, in_features));
+  return c.off;
+}
+
+static int check_linear(const fvq_linear* lin, const char* who) {
+  if (lin == nullptr) return fail(FVQ_EINVAL, "%s: linear descriptor is NULL", who);
+  if (!lin->qweight || !lin->scale || !lin->global_sf)
+    return fail(FVQ_EINVAL, "%s: qweight, scale and global_sf are required", who);
+  if (lin->in_features <= 0 || lin->in_features % 256 != 0 || lin->out_features <= 0 ||
+      lin->out_features % 256 != 0)
+    return fail(FVQ_EINVAL, "%s: in/out features must be positive multiples of 256 (got %lld, %lld)",
+                who, (long long)lin->in_features, (long long)lin->out_features);
+  if (!aligned16(lin->qweight) || !aligned16(lin->scale) || !aligned16(lin->bias))
+    return fail(FVQ_EALIGN, "%s: weight buffers must be 16-byte aligned", who);
+  return FVQ_OK;
+}
+
+int fvq_nvfp4_linear(const uint16_t* x, int64_t rows, const fvq_linear* lin, uint16_t* y,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_linear(lin, "fvq_nvfp4_linear")) return rc;
+  if (int rc = check_quant_shape(rows, lin->in_features, "fvq_nvfp4_linear")) return rc;
+  if (!x || !y || !workspace) return fail(FVQ_EINVAL, "fvq_nvfp4_linear: NULL pointer");
+  const size_t need = fvq_nvfp4_linear_workspace_bytes(rows, lin->in_features);
+  if (workspace_bytes < need)
+    return fail(FVQ_EWORKSPACE, "fvq_nvfp4_linear: workspace needs %zu bytes, got %zu", need,
+                workspace_bytes);
+  if (!aligned16(x) || !aligned16(y) || !aligned16(workspace))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_linear: x, y and workspace must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t k = lin->in_features;
+  Carve c(workspace);
+  uint32_t* amax_ws = reinterpret_cast<uint32_t*>(c.take(fvq::kAmaxWorkspaceBytes));
+  float* scalars = reinterpret_cast<float*>(c.take(kScalarBytes));
+  uint8_t* codes = c.take(static_cast<size_t>(rows * k / 2));
+  uint8_t* sf = c.take(fvq::sf_bytes(rows, k));
+  cudaError_t e = fvq::launch_amax(x, rows * k, nullptr, &scalars[0], amax_ws, nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_linear amax launch");
+  e = fvq::launch_quantize(x, rows, k, &scalars[0], nullptr, nullptr, codes, sf, nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_linear quantize launch");
+  return gemm_impl(codes, sf, &scalars[0], lin->qweight, lin->scale, lin->global_sf, nullptr,
+                   lin->bias, y,
+                   rows, lin->out_features, k, FVQ_EPI_BF16, nullptr, st);
+}
+
+size_t fvq_nvfp4_ffn_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff) {
+  if (rows <= 0 || d_model <= 0 || d_ff <= 0) return 0;
+  Carve c(nullptr);
+  c.take(fvq::kAmaxWorkspaceBytes);
+  c.take(kScalarBytes);
+  c.take(static_cast<size_t>(rows * d_model / 2));
+  c.take(fvq::sf_bytes(rows, d_model));
+  c.take(static_cast<size_t>(rows * d_ff * 2));
+  c.take(static_cast<size_t>(rows * d_ff / 2));
+  c.take(fvq::sf_bytes(rows, d_ff));
+  return c.off;
+}
+
+int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
+                  uint16_t* y, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_linear(lin1, "fvq_nvfp4_ffn (linear 1)")) return rc;
+  if (int rc = check_linear(lin2, "fvq_nvfp4_ffn (linear 2)")) return rc;
+  if (lin1->out_features != lin2->in_features || lin2->out_features != lin1->in_features)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn: linear shapes do not chain (%lld->%lld, %lld->%lld)",
+                (long long)lin1->in_features, (long long)lin1->out_features,
+                (long long)lin2->in_features, (long long)lin2->out_features);
+  if (int rc = check_quant_shape(rows, lin1->in_features, "fvq_nvfp4_ffn")) return rc;
+  if (!x || !y || !workspace) return fail(FVQ_EINVAL, "fvq_nvfp4_ffn: NULL pointer");
+  const int64_t d = lin1->in_features, f = lin1->out_features;
+  const size_t need = fvq_nvfp4_ffn_workspace_bytes(rows, d, f);
+  if (workspace_bytes < need)
+    return fail(FVQ_EWORKSPACE, "fvq_nvfp4_ffn: workspace needs %zu bytes, got %zu", need,
+                workspace_bytes);
+  if (!aligned16(x) || !aligned16(y) || !aligned16(workspace))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_ffn: x, y and workspace must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c(workspace);
+  uint32_t* amax_ws = reinterpret_cast<uint32_t*>(c.take(fvq::kAmaxWorkspaceBytes));
+  float* scalars = reinterpret_cast<float*>(c.take(kScalarBytes));
+  uint8_t* codes_x = c.take(static_cast<size_t>(rows * d / 2));
+  uint8_t* sf_x = c.take(fvq::sf_bytes(rows, d));
+  uint16_t* h = reinterpret_cast<uint16_t*>(c.take(static_cast<size_t>(rows * f * 2)));
+  uint8_t* codes_h = c.take(static_cast<size_t>(rows * f / 2));
+  uint8_t* sf_h = c.take(fvq::sf_bytes(rows, f));
+  float* g_x = &scalars[0];
+  float* g_h = &scalars[1];
+  float* amax_h = &scalars[2];
+  // 1. amax(x) -> g_x; also zeroes amax_h before GEMM1 accumulates into it
+  cudaError_t e = fvq::launch_amax(x, rows * d, nullptr, g_x, amax_ws, amax_h, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn amax launch");
+  // 2. x -> NVFP4
+  e = fvq::launch_quantize(x, rows, d, g_x, nullptr, nullptr, codes_x, sf_x, nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(x) launch");
+  // 3. h = bf16(gelu(bf16(bf16(alpha1 * acc) + b1))), amax_h = max |h|
+  if (int rc = gemm_impl(codes_x, sf_x, g_x, lin1->qweight, lin1->scale, lin1->global_sf, nullptr,
+                         lin1->bias, h, rows, f, d, FVQ_EPI_GELU_AMAX, amax_h, st))
+    return rc;
+  // 4. h -> NVFP4 with g_h = 2688 / max(amax_h, 1e-12)
+  e = fvq::launch_quantize(h, rows, f, nullptr, amax_h, g_h, codes_h, sf_h, nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(h) launch");
+  // 5. y = bf16(bf16(alpha2 * acc) + b2)
+  return gemm_impl(codes_h, sf_h, g_h, lin2->qweight, lin2->scale, lin2->global_sf, nullptr,
+                   lin2->bias, y,
+                   rows, d, f, FVQ_EPI_BF16, nullptr, st);
+}
+
+int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream) {
+  if (n < 0 || (n > 0 && (!in || !out))) return fail(FVQ_EINVAL, "fvq_rcp_approx_probe: bad args");
+  if (int rc = check_device()) return rc;
+  cudaError_t e = fvq::launch_rcp_probe(in, out, n, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_rcp_approx_probe launch");
+  return FVQ_OK;
+}
+
+int fvq_set_wait_limit(uint64_t nanoseconds) {
+  g_wait_limit = nanoseconds == 0 ? fvq::kDefaultWaitLimit : nanoseconds;
+  return FVQ_OK;
+}
+
+int fvq_read_device_error(void* stream, uint32_t* flags) {
+  if (flags == nullptr) return fail(FVQ_EINVAL, "fvq_read_device_error: flags is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  cudaError_t e = fvq::read_error_word(&v, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_read_device_error");
+  *flags = v;
+  if (v != 0) {
+    e = fvq::set_error_word(0, st);
+    if (e != cudaSuccess) return cuda_fail(e, "fvq_read_device_error clear");
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "fvq_read_device_error clear");
+  }
+  return FVQ_OK;
+}
+
+}  // extern "C"

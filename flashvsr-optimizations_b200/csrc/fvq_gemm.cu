@@ -1,0 +1,403 @@
+// fvq_gemm.cu -- block-scaled NVFP4 GEMM on sm_100a tensor cores.
+//
+//   out[m, n] = epilogue(alpha * sum_k A[m, k] W[n, k]),  alpha = 1 / (g_a * g_w)
+//
+// Replaces flashinfer.mm_fp4(..., backend='cutlass') plus the bias add that
+// follows it (reference ffn_quantization.py:65-69).  Design:
+//   * persistent CTAs (one per SM), 128 x 256 output tile, 256-deep K tiles;
+//   * warp 0: TMA producer (A and W codes through 128B-swizzled tensor maps,
+//     the scale factors as contiguous 2 KB bulk copies -- the 128x4 swizzled
+//     layout keeps a 128-row x 256-K scale tile contiguous);
+//   * warp 1: owns TMEM (512 columns: fp32 accumulator in 0-255, A scales in
+//     256-271, W scales in 272-303), moves scales smem -> TMEM with
+//     tcgen05.cp and issues tcgen05.mma.kind::mxf4nvf4 (K = 64 per MMA);
+//   * warps 2-9: epilogue; each thread owns one accumulator row and 128
+//     columns, pulls them into registers, frees the accumulator for the next
+//     tile and then applies alpha / bias / GELU and stores bf16 while the
+//     next tile's MMAs run.
+// No TMA multicast: every CTA loads its own tiles.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "fvq_internal.h"
+#include "fvq_ptx.cuh"
+
+namespace fvq {
+
+__device__ uint32_t g_device_error = 0;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 256;
+constexpr int BKB = BK / 2;                      // bytes of codes per row per K tile
+constexpr int kStages = 4;
+constexpr int kABytes = BM * BKB;                // 16 KB
+constexpr int kBBytes = BN * BKB;                // 32 KB
+constexpr int kSfaBytes = BM * (BK / 16);        // 2 KB
+constexpr int kSfbBytes = BN * (BK / 16);        // 4 KB
+constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // 54 KB
+constexpr int kNumThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSfaCol = 256;
+constexpr uint32_t kSfbCol = 272;
+constexpr int kBarrierBytes = 256;
+constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+
+// Instruction descriptor, kind::mxf4nvf4: A/B E2M1 (1), UE4M3 scales (0),
+// K-major A and B, N = 256 (>>3 at bit 17), M = 128 (>>4 at bit 24).
+constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                            (static_cast<uint32_t>(BM >> 4) << 24);
+
+struct Barriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full;
+  uint64_t acc_empty;
+  uint64_t teardown;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Barriers) <= kBarrierBytes, "barrier area");
+
+__device__ __forceinline__ void flag_error(Barriers* bars, uint32_t bit) {
+  atomicOr(&g_device_error, bit);
+  *reinterpret_cast<volatile int*>(&bars->abort_flag) = 1;
+}
+
+__device__ __forceinline__ bool aborted(Barriers* bars) {
+  return *reinterpret_cast<volatile int*>(&bars->abort_flag) != 0;
+}
+
+__device__ __forceinline__ float bf16_round(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+  return a | (b << 16);
+}
+
+// GELU, tanh approximation, evaluated in fp32 as torch does for bf16 inputs.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
+  const float kKappa = 0.044715f;
+  const float x_cube = x * x * x;
+  const float inner = kBeta * (x + kKappa * x_cube);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                      const __grid_constant__ CUtensorMap tmap_b, const uint8_t* __restrict__ a_sf,
+                      const uint8_t* __restrict__ w_sf, const float* __restrict__ g_a,
+                      const float* __restrict__ g_w, const float* __restrict__ alpha_in,
+                      const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m, int n,
+                      int k, float* amax_out, uint64_t wait_limit) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m_blocks = (m + BM - 1) / BM;
+  const int num_n_blocks = n / BN;
+  const int num_tiles = num_m_blocks * num_n_blocks;
+  const int num_k_tiles = k / BK;
+  const int64_t sf_tile_stride = static_cast<int64_t>(k / 64) * 512;  // bytes per 128-row block
+  const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, kEpiWarps);
+    mbar_init(&bars->teardown, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    uint32_t armed[kStages];
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) armed[s] = 0;
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted(bars); tile += gridDim.x) {
+        const int mb = tile % num_m_blocks;
+        const int nb = tile / num_m_blocks;
+        for (int kt = 0; kt < num_k_tiles; ++kt) {
+          if (!mbar_wait_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
+            flag_error(bars, kErrWaitProducer);
+            break;
+          }
+          uint8_t* sa = smem + stage * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          uint8_t* ssfa = sb + kBBytes;
+          uint8_t* ssfb = ssfa + kSfaBytes;
+          mbar_arrive_expect_tx(&bars->full[stage], kStageBytes);
+          tma_load_2d(sa, &tmap_a, &bars->full[stage], kt * BKB, mb * BM);
+          tma_load_2d(sb, &tmap_b, &bars->full[stage], kt * BKB, nb * BN);
+          bulk_load(ssfa, a_sf + mb * sf_tile_stride + kt * 2048, kSfaBytes, &bars->full[stage]);
+          bulk_load(ssfb, w_sf + (2 * nb) * sf_tile_stride + kt * 2048, 2048, &bars->full[stage]);
+          bulk_load(ssfb + 2048, w_sf + (2 * nb + 1) * sf_tile_stride + kt * 2048, 2048,
+                    &bars->full[stage]);
+          armed[stage] += 1;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // every armed stage must have landed before shared memory goes away;
+      // this wait keeps the default limit even when a short one was requested
+      for (int s = 0; s < kStages; ++s) {
+        if (armed[s] > 0 &&
+            !mbar_wait_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit)) {
+          flag_error(bars, kErrWaitTeardown);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool issued_any = false;
+      const uint32_t acc = tmem;
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted(bars);
+           tile += gridDim.x, ++local) {
+        if (!mbar_wait_bounded(&bars->acc_empty, (static_cast<uint32_t>(local) & 1u) ^ 1u,
+                               wait_limit)) {
+          flag_error(bars, kErrWaitMma);
+          break;
+        }
+        tc_fence_after();
+        bool ok = true;
+        for (int kt = 0; kt < num_k_tiles; ++kt) {
+          if (!mbar_wait_bounded(&bars->full[stage], phase, wait_limit)) {
+            flag_error(bars, kErrWaitMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* sa = smem + stage * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          uint8_t* ssfa = sb + kBBytes;
+          uint8_t* ssfb = ssfa + kSfaBytes;
+          // scales: one 512-byte atom (32 rows x 16 B) per 64-deep K step
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            tmem_cp_32x128b_x4(tmem + kSfaCol + 4 * j,
+                               make_smem_desc(smem_u32(ssfa + 512 * j), 16, 128, 0));
+            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j,
+                               make_smem_desc(smem_u32(ssfb + 512 * j), 16, 128, 0));
+            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j + 4,
+                               make_smem_desc(smem_u32(ssfb + 2048 + 512 * j), 16, 128, 0));
+          }
+          const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
+          const uint64_t bdesc = make_smem_desc(smem_u32(sb), 16, 1024, 2);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            mma_nvf4(acc, adesc + static_cast<uint64_t>(2 * j), bdesc + static_cast<uint64_t>(2 * j),
+                     kIdesc, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j,
+                     (kt > 0 || j > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          tc_commit(&bars->empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&bars->acc_full);
+      }
+      if (aborted(bars) && issued_any) {
+        tc_commit(&bars->teardown);
+        if (!mbar_wait_bounded(&bars->teardown, 0, teardown_limit))
+          flag_error(bars, kErrWaitTeardown);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;             // TMEM lane quadrant this warp may read
+    const int half = (warp - 2) >> 2;      // column half: 0 -> 0..127, 1 -> 128..255
+    // alpha = 1 / (g_a * g_w): torch's reciprocal of the product, IEEE rounded
+    const float alpha = alpha_in != nullptr ? *alpha_in : __frcp_rn(__fmul_rn(*g_a, *g_w));
+    float amax = 0.0f;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      if (!mbar_wait_bounded(&bars->acc_full, static_cast<uint32_t>(local) & 1u, wait_limit)) {
+        flag_error(bars, kErrWaitEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const int mb = tile % num_m_blocks;
+      const int nb = tile / num_m_blocks;
+      uint32_t r[128];
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 128;
+      tmem_ld_32x32b_x32(taddr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld_32x32b_x32(taddr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+      tmem_ld_32x32b_x32(taddr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty);
+
+      const int row = mb * BM + quad * 32 + lane;
+      const int col0 = nb * BN + half * 128;
+      uint16_t* dst = out + static_cast<int64_t>(row) * n + col0;
+#pragma unroll
+      for (int c = 0; c < 128; c += 8) {
+        uint4 bv = make_uint4(0, 0, 0, 0);
+        if (bias != nullptr) bv = __ldg(reinterpret_cast<const uint4*>(bias + col0 + c));
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float v0 = bf16_round(__fmul_rn(__uint_as_float(r[c + 2 * j]), alpha));
+          float v1 = bf16_round(__fmul_rn(__uint_as_float(r[c + 2 * j + 1]), alpha));
+          if (bias != nullptr) {
+            v0 = bf16_round(v0 + __uint_as_float(bw[j] << 16));
+            v1 = bf16_round(v1 + __uint_as_float(bw[j] & 0xFFFF0000u));
+          }
+          if (kEpi == 1) {
+            v0 = bf16_round(gelu_tanh(v0));
+            v1 = bf16_round(gelu_tanh(v1));
+            amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
+          }
+          o[j] = pack_bf16x2(v0, v1);
+        }
+        if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    if (kEpi == 1) {
+      const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, __float_as_uint(amax));
+      if (lane == 0 && bits != 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), bits);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+
+// 2-D map over an FP4 code matrix [rows, k/2 bytes], box = box_rows x 128 bytes, 128B swizzle.
+bool make_code_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t k,
+                   uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k / 2), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k / 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BKB), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int kEpi>
+cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const uint8_t* a_sf,
+                          const uint8_t* w_sf, const float* g_a, const float* g_w,
+                          const float* alpha, const uint16_t* bias, uint16_t* out, int m, int n,
+                          int k, float* amax_out, uint64_t wait_limit, cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_kernel<kEpi>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int tiles = ((m + BM - 1) / BM) * (n / BN);
+  int grid = sm_count();
+  if (grid > tiles) grid = tiles;
+  nvfp4_gemm_kernel<kEpi><<<grid, kNumThreads, kSmemBytes, st>>>(
+      ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
+                        const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
+                        const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
+                        int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
+                        const char** why) {
+  alignas(64) CUtensorMap ma;
+  alignas(64) CUtensorMap mb;
+  if (!make_code_map(&ma, a_codes, m, k, BM) || !make_code_map(&mb, w_codes, n, k, BN)) {
+    if (why) *why = "cuTensorMapEncodeTiled failed for the code matrices";
+    return cudaErrorInvalidValue;
+  }
+  if (epilogue == 1) {
+    return launch_gemm_t<1>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, static_cast<int>(m),
+                            static_cast<int>(n), static_cast<int>(k), amax_out, wait_limit, st);
+  }
+  return launch_gemm_t<0>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, static_cast<int>(m),
+                          static_cast<int>(n), static_cast<int>(k), amax_out, wait_limit, st);
+}
+
+cudaError_t set_error_word(uint32_t v, cudaStream_t st) {
+  return cudaMemcpyToSymbolAsync(g_device_error, &v, sizeof(v), 0, cudaMemcpyHostToDevice, st);
+}
+
+cudaError_t read_error_word(uint32_t* v, cudaStream_t st) {
+  cudaError_t e = cudaMemcpyFromSymbolAsync(v, g_device_error, sizeof(*v), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) return e;
+  return cudaStreamSynchronize(st);
+}
+
+}  // namespace fvq

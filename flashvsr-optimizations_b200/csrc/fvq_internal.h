@@ -1,0 +1,47 @@
+// fvq_internal.h -- launchers shared between the kernel files and the C ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace fvq {
+
+// Bits of the device error word.
+constexpr uint32_t kErrWaitProducer = 1u << 0;  // producer gave up on an empty stage
+constexpr uint32_t kErrWaitMma = 1u << 1;       // MMA warp gave up on a full stage / accumulator
+constexpr uint32_t kErrWaitEpilogue = 1u << 2;  // epilogue gave up on the accumulator
+constexpr uint32_t kErrWaitTeardown = 1u << 3;  // teardown gave up on in-flight work
+
+// Bound on any single pipeline wait inside a kernel (wall time, ns).
+constexpr uint64_t kDefaultWaitLimit = 2000000000ull;
+
+// amax workspace: [0] arrival counter, [2] amax bits, partials from byte 64.
+constexpr int kAmaxMaxBlocks = 2048;
+constexpr size_t kAmaxWorkspaceBytes = 64 + kAmaxMaxBlocks * 4;
+
+inline int64_t pad_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+inline size_t sf_bytes(int64_t rows, int64_t k) {
+  return static_cast<size_t>(pad_up(rows, 128) * pad_up(k / 16, 4));
+}
+
+int sm_count();
+
+// Kernels (fvq_quant.cu)
+cudaError_t launch_amax(const uint16_t* x, int64_t numel, float* amax_out, float* g_out,
+                        uint32_t* ws, float* zero_word, cudaStream_t st);
+cudaError_t launch_quantize(const uint16_t* x, int64_t rows, int64_t k, const float* g,
+                            const float* amax, float* g_out, uint8_t* codes, uint8_t* sf,
+                            float* zero_word, cudaStream_t st);
+cudaError_t launch_rcp_probe(const float* in, float* out, int64_t n, cudaStream_t st);
+
+// GEMM (fvq_gemm.cu)
+cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
+                        const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
+                        const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
+                        int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
+                        const char** why);
+cudaError_t set_error_word(uint32_t v, cudaStream_t st);
+cudaError_t read_error_word(uint32_t* v, cudaStream_t st);
+
+}  // namespace fvq

@@ -1,0 +1,237 @@
+// fvq_quant.cu -- HBM-bound kernels of the activation quantizer.
+//
+//   amax kernel     : max |x| over a bf16 tensor, then g = 2688 / max(amax, 1e-12)
+//                     (reference ffn_quantization.py:15-19, :29-32).
+//   quantize kernel : NVFP4 codes + 128x4-swizzled E4M3 block scales
+//                     (reference: flashinfer.nvfp4_quantize, ffn_quantization.py:47, :64).
+//
+// Both stream the input once with 16-byte non-allocating loads, several loads in
+// flight per thread, on a grid of (SM count x 8) CTAs of 256 threads.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "fvq_internal.h"
+#include "fvq_ptx.cuh"
+
+namespace fvq {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// max of |bf16| over the 8 values of a uint4, as a bf16 bit pattern in the low 16 bits.
+__device__ __forceinline__ uint32_t absmax8(uint4 v) {
+  uint32_t m = __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
+                        __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
+  return max(m & 0xFFFFu, m >> 16);
+}
+
+__device__ __forceinline__ int64_t pad_up_dev(int64_t r) { return (r + 127) / 128 * 128; }
+
+// g = reciprocal(max(amax, 1e-12)) * 2688 with IEEE rounding at each step,
+// as torch evaluates 2688. / t on a device tensor.
+__device__ __forceinline__ float encode_scale(float amax) {
+  float m = fmaxf(amax, 1e-12f);
+  return __fmul_rn(__frcp_rn(m), 2688.0f);
+}
+
+// ---------------------------------------------------------------- amax
+__global__ void __launch_bounds__(kThreads) amax_kernel(const uint16_t* __restrict__ x,
+                                                        int64_t numel, float* amax_out,
+                                                        float* g_out, uint32_t* ws,
+                                                        float* zero_word) {
+  __shared__ uint32_t warp_max[kThreads / 32];
+  __shared__ bool is_last;
+  if (zero_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *zero_word = 0.0f;
+
+  const int64_t nvec = numel / 8;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kThreads;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  uint32_t m = 0;
+  int64_t i = tid;
+  for (; i + (kUnroll - 1) * nthreads < nvec; i += kUnroll * nthreads) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = ld_stream(xv + i + u * nthreads);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) m = max(m, absmax8(v[u]));
+  }
+  for (; i < nvec; i += nthreads) m = max(m, absmax8(ld_stream(xv + i)));
+  // ragged tail (numel % 8)
+  for (int64_t t = nvec * 8 + tid; t < numel; t += nthreads) m = max(m, x[t] & 0x7FFFu);
+
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t bm = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) bm = max(bm, warp_max[w]);
+    ws[16 + blockIdx.x] = bm;
+    __threadfence();
+    uint32_t prev = atomicAdd(&ws[0], 1u);
+    is_last = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  // last CTA: reduce the per-CTA maxima, publish, and re-arm the counter.
+  __threadfence();
+  uint32_t bm = 0;
+  for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += kThreads)
+    bm = max(bm, __ldcg(&ws[16 + b]));
+  bm = __reduce_max_sync(0xFFFFFFFFu, bm);
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = bm;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t r = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) r = max(r, warp_max[w]);
+    const float amax = __uint_as_float(r << 16);
+    ws[2] = __float_as_uint(amax);
+    if (amax_out) *amax_out = amax;
+    if (g_out) *g_out = encode_scale(amax);
+    ws[0] = 0;
+  }
+}
+
+// ---------------------------------------------------------------- quantize
+// Work unit: a "group" = 64 consecutive elements of one row = 4 scale blocks =
+// one 32-bit word of the swizzled scale layout.  8 threads share a group, 8
+// elements (one 16-byte load) each; a warp covers 4 consecutive groups.
+// Groups past the last row up to pad128(rows) only write zero scale words.
+__global__ void __launch_bounds__(kThreads) quantize_kernel(
+    const uint16_t* __restrict__ x, int64_t rows, int64_t k, const float* __restrict__ g_ptr,
+    const float* __restrict__ amax_ptr, float* g_out, uint8_t* __restrict__ codes,
+    uint8_t* __restrict__ sf, float* zero_word) {
+  const float g = amax_ptr != nullptr ? encode_scale(*amax_ptr) : *g_ptr;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (g_out != nullptr) *g_out = g;
+    if (zero_word != nullptr) *zero_word = 0.0f;
+  }
+  const float r6 = rcp_approx_ftz(6.0f);
+  const float rg = rcp_approx_ftz(g);
+
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & 7;        // 8-element slice within the group
+  const int gsel = lane >> 3;      // which of the warp's 4 groups
+  const int64_t gpr = k / 64;      // groups per row
+  const int64_t n_real = rows * gpr;
+  const int64_t n_all = pad_up_dev(rows) * gpr;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
+  const int64_t stride = nwarps * 4;
+
+  for (int64_t base = warp * 4; base < n_all; base += stride * kUnroll) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t gi = base + u * stride + gsel;
+      v[u] = make_uint4(0, 0, 0, 0);
+      if (gi < n_real) v[u] = ld_stream(x + gi * 64 + sub * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t gi = base + u * stride + gsel;
+      // pair max -> the 16-element block maximum (exact, bf16 bits)
+      uint32_t bm = absmax8(v[u]);
+      bm = max(bm, __shfl_xor_sync(0xFFFFFFFFu, bm, 1));
+      const float vmax = __uint_as_float(bm << 16);
+      const float sfv_raw = mul_ftz(g, mul_ftz(vmax, r6));
+      const uint32_t s8 = f32_to_e4m3(sfv_raw);
+      const float sfv = e4m3_to_f32(s8);
+      // vmax != 0 under flush-to-zero: a subnormal maximum counts as zero
+      const float os = (bm >= 0x0080u) ? rcp_approx_ftz(mul_ftz(sfv, rg)) : 0.0f;
+      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      uint32_t packed = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = mul_ftz(__uint_as_float(w[j] << 16), os);
+        const float hi = mul_ftz(__uint_as_float(w[j] & 0xFFFF0000u), os);
+        packed |= f32x2_to_e2m1x2(lo, hi) << (8 * j);
+      }
+      // gather the group's 4 scale bytes (held by subs 0,2,4,6) into sub 0
+      const int lead = lane & ~7;
+      const uint32_t s1 = __shfl_sync(0xFFFFFFFFu, s8, lead + 2);
+      const uint32_t s2 = __shfl_sync(0xFFFFFFFFu, s8, lead + 4);
+      const uint32_t s3 = __shfl_sync(0xFFFFFFFFu, s8, lead + 6);
+      if (gi < n_real) {
+        reinterpret_cast<uint32_t*>(codes)[gi * 8 + sub] = packed;
+      }
+      if (sub == 0 && gi < n_all) {
+        const int64_t row = gi / gpr;
+        const int64_t kc = gi - row * gpr;
+        const uint32_t word = (gi < n_real) ? (s8 | (s1 << 8) | (s2 << 16) | (s3 << 24)) : 0u;
+        const int64_t off = (row >> 7) * (gpr * 512) + kc * 512 + (row & 31) * 16 +
+                            ((row & 127) >> 5) * 4;
+        *reinterpret_cast<uint32_t*>(sf + off) = word;
+      }
+    }
+  }
+}
+
+__global__ void rcp_probe_kernel(const float* in, float* out, int64_t n) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = rcp_approx_ftz(in[i]);
+}
+
+}  // namespace
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+cudaError_t launch_amax(const uint16_t* x, int64_t numel, float* amax_out, float* g_out,
+                        uint32_t* ws, float* zero_word, cudaStream_t st) {
+  const int64_t nvec = numel / 8 + 1;
+  int64_t blocks = (nvec + kThreads * kUnroll - 1) / (kThreads * kUnroll);
+  blocks = blocks < 1 ? 1 : blocks;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks > kAmaxMaxBlocks) blocks = kAmaxMaxBlocks;
+  amax_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(x, numel, amax_out, g_out, ws,
+                                                                  zero_word);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize(const uint16_t* x, int64_t rows, int64_t k, const float* g,
+                            const float* amax, float* g_out, uint8_t* codes, uint8_t* sf,
+                            float* zero_word, cudaStream_t st) {
+  const int64_t n_all = pad_up(rows, 128) * (k / 64);
+  const int64_t warps_needed = (n_all + 4 * kUnroll - 1) / (4 * kUnroll);
+  int64_t blocks = (warps_needed + (kThreads / 32) - 1) / (kThreads / 32);
+  blocks = blocks < 1 ? 1 : blocks;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  quantize_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(x, rows, k, g, amax, g_out,
+                                                                      codes, sf, zero_word);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rcp_probe(const float* in, float* out, int64_t n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t blocks = (n + 255) / 256;
+  rcp_probe_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(in, out, n);
+  return cudaGetLastError();
+}
+
+}  // namespace fvq

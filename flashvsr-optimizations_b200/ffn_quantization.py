@@ -1,0 +1,146 @@
+"""Drop-in replacement of the reference's ``ffn_quantization.py`` NVFP4 path.
+
+Same plugin API as the reference (ffn_quantization.py:35-86):
+
+* ``global_scale(x)`` -> fp32 [1] encode scale ``2688 / max(amax(x), 1e-12)``;
+* ``QuantLinear(linear, mode)`` with buffers ``qweight``, ``scale``,
+  ``global_sf``, ``bias`` and attribute ``out_features``; ``forward`` maps
+  bf16 ``[..., K]`` -> bf16 ``[..., N]`` on the current CUDA stream, without a
+  host synchronisation;
+* ``install_ffn(pipe, mode)`` swaps ``pipe.dit.blocks[i].ffn[0]`` and
+  ``ffn[2]`` and returns the same metadata dict.
+
+Additionally ``install_ffn`` (``fused=True``, the default) replaces each
+block's ``ffn`` ``nn.Sequential`` by :class:`NVFP4FFN`, a subclass that keeps
+the same children (``[0]`` and ``[2]`` are the ``QuantLinear`` modules, ``[1]``
+the GELU) but runs the whole Linear-GELU-Linear chain as one call into the
+library, with GELU and the intermediate's amax computed in GEMM1's epilogue.
+Its result follows the reference's roundings and global scales exactly.
+
+Modes: ``'nvfp4'`` (this path), ``'bf16'`` (no swap).  ``'fp8'`` is the
+reference's W8A8 adapter, which this library does not implement: it raises
+``NotImplementedError``.  Any other mode raises ``ValueError(mode)`` like the
+reference (ffn_quantization.py:50).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+__all__ = ["global_scale", "QuantLinear", "NVFP4FFN", "install_ffn"]
+
+
+def global_scale(x: torch.Tensor) -> torch.Tensor:
+    """ffn_quantization.py:29-32."""
+    return ops.global_scale(x.contiguous())
+
+
+def _quantize_weight(w: torch.Tensor):
+    w = w.detach().to(torch.bfloat16).contiguous()
+    g = ops.global_scale(w)
+    q, s = ops.nvfp4_quantize(w, g)
+    return q, s, g
+
+
+class QuantLinear(torch.nn.Module):
+    """NVFP4 W4A4 replacement of one ``nn.Linear`` (ffn_quantization.py:35-70)."""
+
+    def __init__(self, linear: torch.nn.Linear, mode: str):
+        super().__init__()
+        self.mode = mode
+        self.out_features = linear.out_features
+        self.in_features = linear.in_features
+        bias = linear.bias.detach().clone().to(torch.bfloat16) if linear.bias is not None else None
+        self.register_buffer("bias", bias)
+        if mode == "fp8":
+            raise NotImplementedError(
+                "QuantLinear(mode='fp8') (the reference's W8A8 adapter) is not implemented by "
+                "this NVFP4 library")
+        if mode != "nvfp4":
+            raise ValueError(mode)
+        w = linear.weight
+        if not w.is_cuda:
+            raise RuntimeError("QuantLinear: the weight must be on a CUDA device (no CPU path)")
+        q, s, g = _quantize_weight(w)
+        self.register_buffer("global_sf", g)
+        self.register_buffer("qweight", q)
+        self.register_buffer("scale", s)
+
+    @classmethod
+    def from_quantized(cls, qweight: torch.Tensor, scale: torch.Tensor, global_sf: torch.Tensor,
+                       bias: torch.Tensor | None, in_features: int) -> "QuantLinear":
+        """Build from already-quantized buffers (e.g. a saved state dict), no re-quantization."""
+        self = cls.__new__(cls)
+        torch.nn.Module.__init__(self)
+        self.mode = "nvfp4"
+        self.in_features = in_features
+        self.out_features = qweight.shape[0]
+        if qweight.shape[1] * 2 != in_features:
+            raise ValueError("QuantLinear.from_quantized: qweight does not match in_features")
+        self.register_buffer("bias", bias)
+        self.register_buffer("global_sf", global_sf)
+        self.register_buffer("qweight", qweight)
+        self.register_buffer("scale", scale)
+        return self
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        out = ops.nvfp4_linear(x2, self.qweight, self.scale, self.global_sf, self.bias)
+        return out.reshape(*shape[:-1], self.out_features)
+
+    def extra_repr(self) -> str:
+        return f"in_features={self.in_features}, out_features={self.out_features}, mode={self.mode}"
+
+
+class NVFP4FFN(torch.nn.Sequential):
+    """``nn.Sequential(QuantLinear, GELU(tanh), QuantLinear)`` run as one fused call.
+
+    Indexing, iteration and state-dict keys are those of the Sequential it
+    replaces; ``forward`` computes exactly what the Sequential of QuantLinear
+    modules would, in five kernel launches.
+    """
+
+    def __init__(self, lin1: QuantLinear, act: torch.nn.Module, lin2: QuantLinear):
+        super().__init__(lin1, act, lin2)
+        if lin1.out_features != lin2.in_features or lin2.out_features != lin1.in_features:
+            raise ValueError("NVFP4FFN: linear shapes do not chain")
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        l1, l2 = self[0], self[2]
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        y = ops.nvfp4_ffn(x2, l1.qweight, l1.scale, l1.global_sf, l1.bias,
+                          l2.qweight, l2.scale, l2.global_sf, l2.bias)
+        return y.reshape(*shape[:-1], l2.out_features)
+
+
+def _is_gelu_tanh(m: torch.nn.Module) -> bool:
+    return isinstance(m, torch.nn.GELU) and getattr(m, "approximate", "none") == "tanh"
+
+
+def install_ffn(pipe, mode: str, fused: bool = True) -> dict:
+    """ffn_quantization.py:73-86, plus the fused whole-FFN module when ``fused``."""
+    count = 0
+    before = sum(p.numel() * p.element_size() for b in pipe.dit.blocks for p in b.ffn.parameters())
+    fused_blocks = 0
+    if mode != "bf16":
+        for block in pipe.dit.blocks:
+            for idx in (0, 2):
+                block.ffn[idx] = QuantLinear(block.ffn[idx], mode)
+                count += 1
+            if fused and mode == "nvfp4" and len(block.ffn) == 3 and _is_gelu_tanh(block.ffn[1]):
+                block.ffn = NVFP4FFN(block.ffn[0], block.ffn[1], block.ffn[2])
+                fused_blocks += 1
+    after = sum(t.numel() * t.element_size() for b in pipe.dit.blocks
+                for t in list(b.ffn.parameters()) + list(b.ffn.buffers()))
+    return {
+        "mode": mode, "quantized_linears": count, "ffn_bytes_before": before,
+        "ffn_bytes_after": after,
+        "fp8": "E4M3 per-row W8A8; torch._scaled_mm; FP32 accumulation; BF16 output",
+        "nvfp4": ("E2M1 W4A4; 16-element E4M3 scales + dynamic tensor FP32 scale; sm_100a "
+                  "tcgen05 block-scaled GEMM (libfvq); BF16 output"),
+        "scope": "Only dit.blocks.*.ffn.{0,2}; GELU, bias, attention, conditioning, decoder remain BF16",
+        "fused_ffn_blocks": fused_blocks,
+    }

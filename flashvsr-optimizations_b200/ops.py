@@ -1,0 +1,270 @@
+"""torch-facing NVFP4 operators over the C ABI (libfvq.so).
+
+Each function mirrors one call of the reference path and is registered as a
+``torch.library`` custom op (namespace ``fvq``) with a fake implementation, so
+it can sit inside traced / compiled graphs.  All work runs on the current
+CUDA stream of the input's device; no host synchronisation happens.  There is
+no CPU fallback: a non-CUDA tensor raises.
+
+Layouts are the reference's (flashinfer's): codes uint8 [rows, k/2]; scale
+factors uint8 [pad128(rows), k/16] in the 128x4 swizzled order; global scales
+fp32 [1] on the device.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "amax", "global_scale", "nvfp4_quantize", "mm_fp4", "nvfp4_gemm",
+    "nvfp4_linear", "nvfp4_ffn", "rcp_approx_probe", "sf_rows", "read_device_error",
+]
+
+
+def sf_rows(rows: int) -> int:
+    return (rows + 127) // 128 * 128
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _check_cuda(name: str, *ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{name}: expected CUDA tensors (there is no CPU path)")
+
+
+def _check_bf16(name: str, x: torch.Tensor) -> None:
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"{name}: expected bfloat16 input, got {x.dtype}")
+
+
+# ---------------------------------------------------------------- workspaces
+class _Workspaces:
+    """Zero-initialised scratch buffers, one per (device, stream), grown on demand.
+
+    The amax counter region of a workspace must start at zero and every call
+    leaves it zero again, so a buffer is zeroed only when it is created.
+    """
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self._bufs: dict[tuple[int, int], torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.index if device.index is not None else torch.cuda.current_device(),
+               torch.cuda.current_stream(device).cuda_stream)
+        with self._lock:
+            buf = self._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+                self._bufs[key] = buf
+            return buf
+
+
+_WS = _Workspaces()
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    return _WS.get(device, nbytes)
+
+
+# ---------------------------------------------------------------- custom ops
+@torch.library.custom_op("fvq::amax", mutates_args=())
+def amax(x: torch.Tensor) -> torch.Tensor:
+    """max |x| (fp32 [1]) of a bf16 tensor."""
+    _check_cuda("amax", x)
+    _check_bf16("amax", x)
+    x = x.contiguous()
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    ws = workspace(x.device, lib.fvq_amax_workspace_bytes())
+    _lib.call("fvq_amax", _ptr(x), x.numel(), _ptr(out), None, _ptr(ws), ws.numel(), _stream(x))
+    return out
+
+
+@amax.register_fake
+def _(x):
+    return x.new_empty(1, dtype=torch.float32)
+
+
+@torch.library.custom_op("fvq::global_scale", mutates_args=())
+def global_scale(x: torch.Tensor) -> torch.Tensor:
+    """``2688 / max(amax(x), 1e-12)`` as fp32 [1] -- ffn_quantization.py:29-32."""
+    _check_cuda("global_scale", x)
+    _check_bf16("global_scale", x)
+    if x.numel() == 0:
+        raise RuntimeError("global_scale: empty tensor (the reference's amax of no partials fails)")
+    x = x.contiguous()
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    ws = workspace(x.device, lib.fvq_amax_workspace_bytes())
+    _lib.call("fvq_amax", _ptr(x), x.numel(), None, _ptr(out), _ptr(ws), ws.numel(), _stream(x))
+    return out
+
+
+@global_scale.register_fake
+def _(x):
+    return x.new_empty(1, dtype=torch.float32)
+
+
+@torch.library.custom_op("fvq::nvfp4_quantize", mutates_args=())
+def nvfp4_quantize(x: torch.Tensor, g: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(codes uint8 [M, K/2], scales uint8 [pad128(M), K/16]) -- flashinfer.nvfp4_quantize(x, g)."""
+    _check_cuda("nvfp4_quantize", x, g)
+    _check_bf16("nvfp4_quantize", x)
+    if x.dim() != 2:
+        raise ValueError("nvfp4_quantize: expected a 2-D [M, K] tensor")
+    m, k = x.shape
+    x = x.contiguous()
+    g = g.to(torch.float32).contiguous()
+    codes = torch.empty((m, k // 2), dtype=torch.uint8, device=x.device)
+    sf = torch.empty((sf_rows(m), k // 16), dtype=torch.uint8, device=x.device)
+    _lib.call("fvq_nvfp4_quantize", _ptr(x), m, k, _ptr(g), _ptr(codes), _ptr(sf), _stream(x))
+    return codes, sf
+
+
+@nvfp4_quantize.register_fake
+def _(x, g):
+    m, k = x.shape
+    return (x.new_empty((m, k // 2), dtype=torch.uint8),
+            x.new_empty((sf_rows(m), k // 16), dtype=torch.uint8))
+
+
+@torch.library.custom_op("fvq::mm_fp4", mutates_args=())
+def mm_fp4(a: torch.Tensor, a_sf: torch.Tensor, w: torch.Tensor, w_sf: torch.Tensor,
+           alpha: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16(alpha * A @ W^T) [+ bias], operands in NVFP4.
+
+    The reference passes ``qweight.t()`` / ``scale.t()`` to flashinfer.mm_fp4
+    (ffn_quantization.py:65-67); here W is given in its stored [N, K/2] layout.
+    """
+    _check_cuda("mm_fp4", a, a_sf, w, w_sf, alpha, bias)
+    m, kh = a.shape
+    n = w.shape[0]
+    if w.shape[1] != kh:
+        raise ValueError(f"mm_fp4: K mismatch ({2 * kh} vs {2 * w.shape[1]})")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    _lib.call("fvq_nvfp4_mm", _ptr(a.contiguous()), _ptr(a_sf.contiguous()), _ptr(w.contiguous()),
+              _ptr(w_sf.contiguous()), _ptr(alpha.to(torch.float32).contiguous()),
+              _ptr(None if bias is None else bias.contiguous()), _ptr(out), m, n, 2 * kh,
+              _stream(a))
+    return out
+
+
+@mm_fp4.register_fake
+def _(a, a_sf, w, w_sf, alpha, bias=None):
+    return a.new_empty((a.shape[0], w.shape[0]), dtype=torch.bfloat16)
+
+
+@torch.library.custom_op("fvq::nvfp4_gemm", mutates_args=())
+def nvfp4_gemm(a: torch.Tensor, a_sf: torch.Tensor, g_a: torch.Tensor, w: torch.Tensor,
+               w_sf: torch.Tensor, g_w: torch.Tensor, bias: torch.Tensor | None = None,
+               gelu: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """GEMM with alpha = 1/(g_a*g_w); with gelu=True also GELU-tanh and amax of the result."""
+    _check_cuda("nvfp4_gemm", a, a_sf, g_a, w, w_sf, g_w, bias)
+    m, kh = a.shape
+    n = w.shape[0]
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    amax_out = torch.zeros(1, dtype=torch.float32, device=a.device)
+    _lib.call("fvq_nvfp4_gemm", _ptr(a.contiguous()), _ptr(a_sf.contiguous()), _ptr(g_a),
+              _ptr(w.contiguous()), _ptr(w_sf.contiguous()), _ptr(g_w),
+              _ptr(None if bias is None else bias.contiguous()), _ptr(out), m, n, 2 * kh,
+              _lib.EPI_GELU_AMAX if gelu else _lib.EPI_BF16, _ptr(amax_out) if gelu else None,
+              _stream(a))
+    return out, amax_out
+
+
+@nvfp4_gemm.register_fake
+def _(a, a_sf, g_a, w, w_sf, g_w, bias=None, gelu=False):
+    return (a.new_empty((a.shape[0], w.shape[0]), dtype=torch.bfloat16),
+            a.new_empty(1, dtype=torch.float32))
+
+
+def _linear_struct(qweight, scale, global_sf, bias, in_f, out_f) -> _lib.FvqLinear:
+    return _lib.FvqLinear(_ptr(qweight), _ptr(scale), _ptr(global_sf), _ptr(bias), in_f, out_f)
+
+
+@torch.library.custom_op("fvq::nvfp4_linear", mutates_args=())
+def nvfp4_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor,
+                 global_sf: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """QuantLinear.forward (ffn_quantization.py:54-70) on a 2-D bf16 input."""
+    _check_cuda("nvfp4_linear", x, qweight, scale, global_sf, bias)
+    _check_bf16("nvfp4_linear", x)
+    m, k = x.shape
+    n = qweight.shape[0]
+    if m == 0:
+        raise RuntimeError("nvfp4_linear: empty input (the reference's global_scale fails on it)")
+    x = x.contiguous()
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    lib = _lib.load()
+    ws = workspace(x.device, lib.fvq_nvfp4_linear_workspace_bytes(m, k))
+    lin = _linear_struct(qweight, scale, global_sf, bias, k, n)
+    _lib.call("fvq_nvfp4_linear", _ptr(x), m, ctypes.byref(lin), _ptr(y), _ptr(ws), ws.numel(),
+              _stream(x))
+    return y
+
+
+@nvfp4_linear.register_fake
+def _(x, qweight, scale, global_sf, bias=None):
+    return x.new_empty((x.shape[0], qweight.shape[0]), dtype=torch.bfloat16)
+
+
+@torch.library.custom_op("fvq::nvfp4_ffn", mutates_args=())
+def nvfp4_ffn(x: torch.Tensor, q1: torch.Tensor, s1: torch.Tensor, g1: torch.Tensor,
+              b1: torch.Tensor | None, q2: torch.Tensor, s2: torch.Tensor, g2: torch.Tensor,
+              b2: torch.Tensor | None) -> torch.Tensor:
+    """QuantLinear -> GELU-tanh -> QuantLinear on a 2-D bf16 input, as the reference computes it."""
+    _check_cuda("nvfp4_ffn", x, q1, s1, g1, b1, q2, s2, g2, b2)
+    _check_bf16("nvfp4_ffn", x)
+    m, d = x.shape
+    f = q1.shape[0]
+    if m == 0:
+        raise RuntimeError("nvfp4_ffn: empty input (the reference's global_scale fails on it)")
+    x = x.contiguous()
+    y = torch.empty((m, d), dtype=torch.bfloat16, device=x.device)
+    lib = _lib.load()
+    ws = workspace(x.device, lib.fvq_nvfp4_ffn_workspace_bytes(m, d, f))
+    l1 = _linear_struct(q1, s1, g1, b1, d, f)
+    l2 = _linear_struct(q2, s2, g2, b2, f, d)
+    _lib.call("fvq_nvfp4_ffn", _ptr(x), m, ctypes.byref(l1), ctypes.byref(l2), _ptr(y), _ptr(ws),
+              ws.numel(), _stream(x))
+    return y
+
+
+@nvfp4_ffn.register_fake
+def _(x, q1, s1, g1, b1, q2, s2, g2, b2):
+    return x.new_empty(x.shape, dtype=torch.bfloat16)
+
+
+# ---------------------------------------------------------------- support
+def rcp_approx_probe(values: torch.Tensor) -> torch.Tensor:
+    """rcp.approx.ftz.f32 of each fp32 value, computed on the GPU (test support)."""
+    _check_cuda("rcp_approx_probe", values)
+    v = values.to(torch.float32).contiguous()
+    out = torch.empty_like(v)
+    _lib.call("fvq_rcp_approx_probe", _ptr(v), _ptr(out), v.numel(), _stream(v))
+    return out
+
+
+def read_device_error(device: torch.device | None = None) -> int:
+    """Synchronise and return (and clear) the library's device error word."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    flags = ctypes.c_uint32(0)
+    _lib.call("fvq_read_device_error", torch.cuda.current_stream(dev).cuda_stream,
+              ctypes.byref(flags))
+    return int(flags.value)
+
+
+def set_wait_limit(nanoseconds: int) -> None:
+    """Bound (wall time per wait) on the GEMM's pipeline waits; 0 restores the 2 s default."""
+    _lib.call("fvq_set_wait_limit", nanoseconds)

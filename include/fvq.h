@@ -1,0 +1,165 @@
+/*
+ * fvq.h -- C ABI of the B200 (sm_100a) NVFP4 transformer-FFN library (libfvq.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as void*.  Nothing allocates: outputs and workspaces belong to the
+ * caller.  Work is enqueued on the given stream; no entry point synchronises
+ * the host (except fvq_read_device_error).  Return value: FVQ_OK (0) or a
+ * negative FVQ_E* status; fvq_last_error() gives a message for the calling
+ * host thread.
+ *
+ * Tensor conventions (the reference's, so buffers are interchangeable):
+ *   bf16 tensors are uint16_t bit patterns, row-major.
+ *   NVFP4 codes: uint8 [rows, k/2], element 2j in the low nibble of byte j.
+ *   Scale factors: E4M3 bytes, one per 16 elements, in the 128x4 swizzled
+ *     layout [pad128(rows)/128][k/64][32][4][4] (pad128(rows) * k/16 bytes);
+ *     rows past `rows` hold zero.
+ *   Global scales: device fp32 scalars, g = 2688 / max(amax, 1e-12) computed
+ *     as reciprocal(amax) * 2688 (two fp32 roundings).
+ *
+ * Shape limits: k % 64 == 0 for the quantizer; the GEMM needs k % 256 == 0
+ * and n % 256 == 0 (d_model 1536 and d_ff 8960 both qualify).
+ */
+#ifndef FVQ_H_
+#define FVQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FVQ_OK 0
+#define FVQ_EINVAL (-1)     /* bad shape, null pointer or bad mode */
+#define FVQ_EALIGN (-2)     /* pointer not 16-byte aligned */
+#define FVQ_ECUDA (-3)      /* CUDA runtime / driver error */
+#define FVQ_EDEVICE (-4)    /* device is not sm_100 */
+#define FVQ_EWORKSPACE (-5) /* workspace too small */
+#define FVQ_ETIMEOUT (-6)   /* a bounded device wait gave up (fvq_read_device_error) */
+
+/* GEMM epilogues */
+#define FVQ_EPI_BF16 0      /* y = bf16(alpha*acc), then y = bf16(y + bias) if bias */
+#define FVQ_EPI_GELU_AMAX 1 /* FVQ_EPI_BF16, then h = bf16(gelu_tanh(y)) and
+                               atomic max of |h| into *amax_out (fp32 bits) */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int fvq_version(void);
+
+/* Message for the last failing call made by this host thread. */
+const char* fvq_last_error(void);
+
+/*
+ * Bytes of workspace fvq_amax needs.  The workspace must be zeroed once
+ * before its first use; every call leaves it zeroed again.
+ */
+size_t fvq_amax_workspace_bytes(void);
+
+/*
+ * amax = max |x| over `numel` bf16 values; g = 2688 / max(amax, 1e-12).
+ * Replaces the reference's global_scale() -- the Triton _partial_amax
+ * kernel and its torch tail (ffn_quantization.py:15-19, :29-32).
+ * Either output may be NULL.  numel == 0 gives amax = 0.
+ */
+int fvq_amax(const uint16_t* x, int64_t numel, float* amax_out, float* g_out,
+             void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * NVFP4 quantization with a given global scale: codes and swizzled E4M3
+ * scale factors.  Replaces flashinfer.nvfp4_quantize(x, g) with its default
+ * 128x4 layout as called at ffn_quantization.py:47 and :64.
+ * `g` points to the fp32 encode scale on the device.
+ */
+int fvq_nvfp4_quantize(const uint16_t* x, int64_t rows, int64_t k, const float* g,
+                       uint8_t* codes, uint8_t* sf, void* stream);
+
+/*
+ * global_scale + nvfp4_quantize in one call (ffn_quantization.py:63-64):
+ * g_out receives the encode scale it used.  `amax_in` may be NULL (then the
+ * amax pass runs first, using `workspace`); if not NULL it must hold
+ * max |x| already (e.g. from an FVQ_EPI_GELU_AMAX epilogue) and no amax
+ * pass runs.
+ */
+int fvq_nvfp4_quantize_dynamic(const uint16_t* x, int64_t rows, int64_t k,
+                               const float* amax_in, float* g_out,
+                               uint8_t* codes, uint8_t* sf,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Block-scaled NVFP4 GEMM on tcgen05 tensor cores:
+ *   out[m, n] = epilogue(alpha * sum_k A[m,k] * W[n,k]),  alpha = 1 / (g_a * g_w)
+ * A: codes [m, k/2] + swizzled sf; W: codes [n, k/2] + swizzled sf (the
+ * nn.Linear weight layout).  Replaces flashinfer.mm_fp4(q, qweight.t(), s,
+ * scale.t(), alpha=1./(g*global_sf), out_dtype=bf16, backend='cutlass')
+ * followed by `out + self.bias` (ffn_quantization.py:65-69), with the bias
+ * add's double rounding kept.  `bias` may be NULL.  `amax_out` is required
+ * for FVQ_EPI_GELU_AMAX (the caller zeroes it before the first tile runs).
+ */
+int fvq_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
+                   const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
+                   const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
+                   int epilogue, float* amax_out, void* stream);
+
+/*
+ * The same GEMM with a precomputed device alpha (fp32 scalar) instead of the
+ * two global scales: the exact argument list of flashinfer.mm_fp4 as the
+ * reference calls it (ffn_quantization.py:65-67), plus the optional bias of
+ * :68-69.  FVQ_EPI_BF16 epilogue.
+ */
+int fvq_nvfp4_mm(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* w_codes,
+                 const uint8_t* w_sf, const float* alpha, const uint16_t* bias, uint16_t* out,
+                 int64_t m, int64_t n, int64_t k, void* stream);
+
+/* One nn.Linear replaced by QuantLinear (ffn_quantization.py:54-70). */
+typedef struct fvq_linear {
+  const uint8_t* qweight;   /* [out_features, in_features/2] */
+  const uint8_t* scale;     /* swizzled, pad128(out_features) * in_features/16 */
+  const float* global_sf;   /* device fp32 scalar */
+  const uint16_t* bias;     /* bf16 [out_features] or NULL */
+  int64_t in_features;
+  int64_t out_features;
+} fvq_linear;
+
+/* Bytes of workspace fvq_nvfp4_linear needs for `rows` rows. */
+size_t fvq_nvfp4_linear_workspace_bytes(int64_t rows, int64_t in_features);
+
+/* QuantLinear.forward: y = bias + mm_fp4(nvfp4_quantize(x, global_scale(x)), W). */
+int fvq_nvfp4_linear(const uint16_t* x, int64_t rows, const fvq_linear* lin, uint16_t* y,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace fvq_nvfp4_ffn needs for `rows` tokens. */
+size_t fvq_nvfp4_ffn_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff);
+
+/*
+ * The whole FFN the reference installs into (ffn_quantization.py:77-80 swaps
+ * ffn[0] and ffn[2] of nn.Sequential(Linear, GELU(tanh), Linear)):
+ *   y = QuantLinear2(bf16(gelu_tanh(QuantLinear1(x))))
+ * with the same global scales and roundings as the reference.  GELU and the
+ * amax of the intermediate are computed in GEMM1's epilogue.
+ * The workspace must be zeroed once before its first use.
+ */
+int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
+                  uint16_t* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Test support: out[i] = rcp.approx.ftz.f32(in[i]) on the device, the
+ * reciprocal the quantizer uses (so a CPU checker can use measured values).
+ */
+int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream);
+
+/*
+ * Bounded device waits: a GEMM whose pipeline wait exceeds the limit sets a
+ * device error word and returns early (after letting its own copies and MMAs
+ * drain).  fvq_set_wait_limit changes the limit, in nanoseconds of wall time
+ * per wait (0 restores the default of 2 s), for later launches.
+ * fvq_read_device_error synchronises `stream`, returns the error word
+ * (0 = none) in *flags and clears it.
+ */
+int fvq_set_wait_limit(uint64_t nanoseconds);
+int fvq_read_device_error(void* stream, uint32_t* flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FVQ_H_ */

@@ -1,0 +1,143 @@
+"""Block-scaled NVFP4 GEMM (tcgen05) on the GPU.
+
+The GEMM is checked against the oracle's dequantise-and-multiply on random
+codes and scale bytes (this exercises the operand, scale-factor and TMEM
+layouts independently of the quantizer), against the reference's own
+QuantLinear output (golden, flashinfer.mm_fp4 on a B200), and the GELU/amax
+epilogue against the oracle's GELU.
+Tolerance: the GPU accumulates in fp32 in its own order while the oracle sums
+in float64, so outputs agree to within one bf16 rounding: relative Frobenius
+error <= 2e-3 and every element within 2 bf16 ulps (+ a tiny absolute slack).
+"""
+import numpy as np
+import pytest
+import torch
+
+from flashvsr_optimizations_b200 import ops, workloads as W
+from flashvsr_optimizations_b200.ffn_quantization import QuantLinear
+from helpers import bits_to_dev, dev_to_bits, f32_from_bits, golden, golden_meta
+from oracle import nvfp4_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+REL_FRO_TOL = 2e-3
+
+
+def _random_operand(rows, k, rng, sf_lo=0x30, sf_hi=0x48):
+    """Random E2M1 codes and E4M3 scale bytes in a moderate range (swizzled layout)."""
+    codes = rng.integers(0, 256, size=(rows, k // 2), dtype=np.uint8)
+    sf_un = rng.integers(sf_lo, sf_hi, size=(rows, k // 16), dtype=np.uint8)
+    sf = np.zeros(O.sf_swizzled_size(rows, k), dtype=np.uint8)
+    sf[O.sf_swizzled_offsets(rows, k // 16)] = sf_un
+    return codes, sf
+
+
+def _close_bf16(got_bits, ref_f32, ulps=2):
+    got = O.bf16_bits_to_f32(got_bits).astype(np.float64)
+    ref = np.asarray(ref_f32, dtype=np.float64)
+    rel = O.frobenius_rel(got, ref)
+    ulp = np.maximum(np.abs(ref), 1e-30) * 2.0 ** -8
+    worst = np.max(np.abs(got - ref) / (ulp + 1e-6 * np.abs(ref).max()))
+    return rel, worst
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 256), (200, 512, 512), (300, 256, 1536),
+                                   (1, 256, 256), (513, 768, 768)])
+def test_gemm_random_operands_vs_oracle(m, n, k):
+    rng = np.random.default_rng(m * 7 + n + k)
+    a, a_sf = _random_operand(m, k, rng)
+    w, w_sf = _random_operand(n, k, rng)
+    g_a = torch.tensor([1.5], device="cuda")
+    g_w = torch.tensor([0.75], device="cuda")
+    out, _ = ops.nvfp4_gemm(torch.from_numpy(a).cuda(), torch.from_numpy(a_sf).cuda(), g_a,
+                            torch.from_numpy(w).cuda(), torch.from_numpy(w_sf).cuda(), g_w)
+    alpha = O.gemm_alpha(np.float32(1.5), np.float32(0.75))
+    ref = alpha * (O.dequantize(a, a_sf, m, k).astype(np.float64)
+                   @ O.dequantize(w, w_sf, n, k).astype(np.float64).T)
+    rel, worst = _close_bf16(dev_to_bits(out), ref)
+    assert rel <= REL_FRO_TOL, rel
+    assert worst <= 2.0, worst
+
+
+def test_gemm_scale_placement_one_hot():
+    """Unit codes, all scales 1 except one block per operand: pins the scale layout."""
+    m, n, k = 256, 256, 512
+    one = 0x22  # two E2M1 codes of 1.0
+    a = np.full((m, k // 2), one, dtype=np.uint8)
+    w = np.full((n, k // 2), one, dtype=np.uint8)
+    sf_one = 0x38  # E4M3 1.0
+    a_un = np.full((m, k // 16), sf_one, dtype=np.uint8)
+    w_un = np.full((n, k // 16), sf_one, dtype=np.uint8)
+    a_un[77, 19] = 0x40  # 2.0
+    w_un[201, 5] = 0x48  # 4.0
+    a_sf = np.zeros(O.sf_swizzled_size(m, k), dtype=np.uint8)
+    w_sf = np.zeros(O.sf_swizzled_size(n, k), dtype=np.uint8)
+    a_sf[O.sf_swizzled_offsets(m, k // 16)] = a_un
+    w_sf[O.sf_swizzled_offsets(n, k // 16)] = w_un
+    g1 = torch.ones(1, device="cuda")
+    out, _ = ops.nvfp4_gemm(torch.from_numpy(a).cuda(), torch.from_numpy(a_sf).cuda(), g1,
+                            torch.from_numpy(w).cuda(), torch.from_numpy(w_sf).cuda(), g1)
+    got = O.bf16_bits_to_f32(dev_to_bits(out))
+    ref = O.dequantize(a, a_sf, m, k).astype(np.float64) @ O.dequantize(w, w_sf, n, k).astype(np.float64).T
+    assert np.array_equal(got, O.round_bf16(ref.astype(np.float32)))
+
+
+def test_gemm_bias_and_gelu_epilogue_vs_oracle():
+    m, n, k = 200, 512, 768
+    rng = np.random.default_rng(3)
+    a, a_sf = _random_operand(m, k, rng, 0x28, 0x38)
+    w, w_sf = _random_operand(n, k, rng, 0x28, 0x38)
+    bias = W.f32_to_bf16_bits(rng.standard_normal(n).astype(np.float32) * np.float32(0.1))
+    g = torch.tensor([2.0], device="cuda")
+    args = (torch.from_numpy(a).cuda(), torch.from_numpy(a_sf).cuda(), g,
+            torch.from_numpy(w).cuda(), torch.from_numpy(w_sf).cuda(), g, bits_to_dev(bias))
+    y, _ = ops.nvfp4_gemm(*args, gelu=False)
+    h, amax = ops.nvfp4_gemm(*args, gelu=True)
+    alpha = O.gemm_alpha(np.float32(2.0), np.float32(2.0))
+    acc = (O.dequantize(a, a_sf, m, k).astype(np.float64) @ O.dequantize(w, w_sf, n, k).astype(np.float64).T)
+    y_ref = O.bias_add_bf16(O.round_bf16((alpha * acc).astype(np.float32)), bias)
+    rel, worst = _close_bf16(dev_to_bits(y), y_ref)
+    assert rel <= REL_FRO_TOL and worst <= 2.0
+    # GELU applied to the GPU's own pre-activation: differences come only from tanh
+    h_ref = O.gelu_tanh_bf16(O.bf16_bits_to_f32(dev_to_bits(y)))
+    rel, worst = _close_bf16(dev_to_bits(h), h_ref)
+    assert rel <= 1e-3 and worst <= 2.0
+    h_bits = dev_to_bits(h)
+    assert np.float32(amax.item()) == np.abs(O.bf16_bits_to_f32(h_bits)).max()
+
+
+def test_quant_linear_matches_reference_golden():
+    meta = golden_meta()["cases"]["lin_200x1536x256"]
+    fix = golden("lin_200x1536x256")
+    wb, bb = W.linear_params(256, 1536, seed=30, b_std=0.01)
+    xb = W.gaussian(200, 1536, seed=31)
+    lin = torch.nn.Linear(1536, 256, bias=True).cuda()
+    with torch.no_grad():
+        lin.weight.copy_(bits_to_dev(wb).float())
+        lin.bias.copy_(bits_to_dev(bb).float())
+    ql = QuantLinear(lin, "nvfp4")
+    import hashlib
+    assert hashlib.sha256(ql.qweight.cpu().numpy().tobytes()).hexdigest() == meta["qweight_sha256"]
+    assert hashlib.sha256(ql.scale.cpu().numpy().tobytes()).hexdigest() == meta["scale_sha256"]
+    assert np.uint32(ql.global_sf.cpu().numpy().view(np.uint32)[0]) == fix["gw_bits"][0]
+    y = ql(bits_to_dev(xb))
+    got = dev_to_bits(y)
+    ref = O.bf16_bits_to_f32(fix["y"])
+    rel, worst = _close_bf16(got, ref)
+    assert rel <= REL_FRO_TOL and worst <= 2.0
+    # report how often the two fp32 accumulation orders round to the same bf16
+    same = np.mean(got == fix["y"])
+    assert same >= 0.95, same
+
+
+def test_mm_fp4_device_alpha_equals_gscales():
+    rng = np.random.default_rng(11)
+    m, n, k = 130, 256, 512
+    a, a_sf = _random_operand(m, k, rng)
+    w, w_sf = _random_operand(n, k, rng)
+    ga = torch.tensor([3.0], device="cuda")
+    gw = torch.tensor([0.3], device="cuda")
+    ta, tas, tw, tws = (torch.from_numpy(v).cuda() for v in (a, a_sf, w, w_sf))
+    y1, _ = ops.nvfp4_gemm(ta, tas, ga, tw, tws, gw)
+    y2 = ops.mm_fp4(ta, tas, tw, tws, 1. / (ga * gw))
+    assert torch.equal(y1, y2)

@@ -1,0 +1,86 @@
+"""The C-ABI library on a machine without a GPU: it loads, exports every entry
+point include/fvq.h declares, and its host-side checks reject bad arguments
+with the documented status codes before any device work."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+from flashvsr_optimizations_b200 import _lib
+
+
+def _declared():
+    text = (ROOT / "include" / "fvq.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(fvq_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = _declared()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with include/fvq.h"
+
+
+def test_version_and_workspace_sizes():
+    lib = _lib.load()
+    assert lib.fvq_version() == 100
+    assert lib.fvq_amax_workspace_bytes() >= 64 + 4 * 148 * 8
+    ws = lib.fvq_nvfp4_ffn_workspace_bytes(7680, 1536, 8960)
+    # codes + scales of x, bf16 intermediate, codes + scales of the intermediate
+    need = 7680 * 768 + 7680 * 96 + 7680 * 8960 * 2 + 7680 * 4480 + 7680 * 560
+    assert need <= ws <= need + 64 * 1024
+    assert lib.fvq_nvfp4_ffn_workspace_bytes(0, 1536, 8960) == 0
+
+
+def _rc(name, *args):
+    return getattr(_lib.load(), name)(*args)
+
+
+def test_quantize_rejects_bad_shapes_and_alignment():
+    buf = ctypes.create_string_buffer(4096 + 16)
+    base = (ctypes.addressof(buf) + 15) // 16 * 16
+    assert _rc("fvq_nvfp4_quantize", base, 4, 100, base, base, base, None) == _lib.FVQ_EINVAL
+    assert b"multiple of 64" in _lib.load().fvq_last_error()
+    assert _rc("fvq_nvfp4_quantize", base, 0, 64, base, base, base, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_nvfp4_quantize", None, 4, 64, base, base, base, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_nvfp4_quantize", base + 2, 4, 64, base, base, base, None) == _lib.FVQ_EALIGN
+
+
+def test_gemm_rejects_bad_shapes_and_epilogue():
+    buf = ctypes.create_string_buffer(4096 + 16)
+    b = (ctypes.addressof(buf) + 15) // 16 * 16
+    gemm = lambda m, n, k, epi=0, amax=None: _rc(  # noqa: E731
+        "fvq_nvfp4_gemm", b, b, b, b, b, b, None, b, m, n, k, epi, amax, None)
+    assert gemm(128, 200, 256) == _lib.FVQ_EINVAL
+    assert gemm(128, 256, 100) == _lib.FVQ_EINVAL
+    assert gemm(0, 256, 256) == _lib.FVQ_EINVAL
+    assert gemm(128, 256, 256, epi=7) == _lib.FVQ_EINVAL
+    assert gemm(128, 256, 256, epi=1, amax=None) == _lib.FVQ_EINVAL
+
+
+def test_linear_and_ffn_check_descriptors():
+    lin_bad = _lib.FvqLinear(None, None, None, None, 1536, 8960)
+    assert _rc("fvq_nvfp4_linear", 16, 4, ctypes.byref(lin_bad), 16, 16, 1 << 20, None) == _lib.FVQ_EINVAL
+    buf = ctypes.create_string_buffer(64)
+    b = (ctypes.addressof(buf) + 15) // 16 * 16
+    l1 = _lib.FvqLinear(b, b, b, None, 1536, 8960)
+    l2 = _lib.FvqLinear(b, b, b, None, 8960, 1024)   # does not chain back to 1536
+    assert _rc("fvq_nvfp4_ffn", b, 4, ctypes.byref(l1), ctypes.byref(l2), b, b, 1 << 30,
+               None) == _lib.FVQ_EINVAL
+    l2 = _lib.FvqLinear(b, b, b, None, 8960, 1536)
+    assert _rc("fvq_nvfp4_ffn", b, 4, ctypes.byref(l1), ctypes.byref(l2), b, b, 16,
+               None) == _lib.FVQ_EWORKSPACE
+
+
+def test_valid_call_without_gpu_fails_loudly():
+    """A well-formed call on a machine without a usable GPU returns an error, never computes on CPU."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    buf = ctypes.create_string_buffer(4096 + 16)
+    b = (ctypes.addressof(buf) + 15) // 16 * 16
+    rc = _rc("fvq_nvfp4_quantize", b, 4, 64, b, b, b, None)
+    assert rc in (_lib.FVQ_ECUDA, _lib.FVQ_EDEVICE)
