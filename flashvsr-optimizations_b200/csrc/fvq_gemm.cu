@@ -11,10 +11,12 @@
 //   * warp 1: owns TMEM (512 columns: fp32 accumulator in 0-255, A scales in
 //     256-271, W scales in 272-303), moves scales smem -> TMEM with
 //     tcgen05.cp and issues tcgen05.mma.kind::mxf4nvf4 (K = 64 per MMA);
-//   * warps 2-9: epilogue; each thread owns one accumulator row and 128
-//     columns, pulls them into registers, frees the accumulator for the next
-//     tile and then applies alpha / bias / GELU and stores bf16 while the
-//     next tile's MMAs run.
+//   * warps 2-17: epilogue; each thread owns one accumulator row and 64
+//     columns, pulls them into registers, forms bf16(alpha*acc), frees the
+//     accumulator for the next tile, then (GEMM1) stages the bf16 tile in
+//     shared memory and applies bias / GELU row by row with coalesced
+//     128-byte stores, or (GEMM2) adds the bias and stores from registers,
+//     while the next tile's MMAs run.
 // No TMA multicast: every CTA loads its own tiles.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -36,25 +38,37 @@ constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 256;
 constexpr int BKB = BK / 2;                      // bytes of codes per row per K tile
-constexpr int kStages = 4;
 constexpr int kABytes = BM * BKB;                // 16 KB
 constexpr int kBBytes = BN * BKB;                // 32 KB
 constexpr int kSfaBytes = BM * (BK / 16);        // 2 KB
 constexpr int kSfbBytes = BN * (BK / 16);        // 4 KB
 constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // 54 KB
-constexpr int kNumThreads = 320;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;                    // 4 per TMEM lane quadrant, 64 columns each
+constexpr int kNumThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfaCol = 256;
 constexpr uint32_t kSfbCol = 272;
 constexpr int kBarrierBytes = 256;
-constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+constexpr int kStagingBytes = BM * BN * 2;       // bf16 tile staged for coalesced stores
+
+// Shared memory plan per epilogue kind: GEMM1 (GELU) keeps 3 operand stages
+// and a 64 KB bf16 staging tile; GEMM2 (plain) keeps 4 stages and stores
+// straight from registers.
+template <int kEpi>
+struct Plan {
+  static constexpr int kStages = kEpi == 1 ? 3 : 4;
+  static constexpr bool kStaged = kEpi == 1;
+  static constexpr int kStagingOff = kStages * kStageBytes;
+  static constexpr int kBarrierOff = kStagingOff + (kStaged ? kStagingBytes : 0);
+  static constexpr int kSmemBytes = kBarrierOff + kBarrierBytes;
+};
 
 // Instruction descriptor, kind::mxf4nvf4: A/B E2M1 (1), UE4M3 scales (0),
 // K-major A and B, N = 256 (>>3 at bit 17), M = 128 (>>4 at bit 24).
 constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
                             (static_cast<uint32_t>(BM >> 4) << 24);
 
+template <int kStages>
 struct Barriers {
   uint64_t full[kStages];
   uint64_t empty[kStages];
@@ -64,14 +78,16 @@ struct Barriers {
   uint32_t tmem_base;
   int abort_flag;
 };
-static_assert(sizeof(Barriers) <= kBarrierBytes, "barrier area");
+static_assert(sizeof(Barriers<4>) <= kBarrierBytes, "barrier area");
 
-__device__ __forceinline__ void flag_error(Barriers* bars, uint32_t bit) {
+template <class B>
+__device__ __forceinline__ void flag_error(B* bars, uint32_t bit) {
   atomicOr(&g_device_error, bit);
   *reinterpret_cast<volatile int*>(&bars->abort_flag) = 1;
 }
 
-__device__ __forceinline__ bool aborted(Barriers* bars) {
+template <class B>
+__device__ __forceinline__ bool aborted(B* bars) {
   return *reinterpret_cast<volatile int*>(&bars->abort_flag) != 0;
 }
 
@@ -84,6 +100,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
   return a | (b << 16);
 }
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // GELU, tanh approximation, evaluated in fp32 as torch does for bf16 inputs.
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -102,10 +121,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                       const float* __restrict__ g_w, const float* __restrict__ alpha_in,
                       const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m, int n,
                       int k, float* amax_out, uint64_t wait_limit) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes);
+  using P = Plan<kEpi>;
+  constexpr int kStages = P::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023u) != 0) {  // the 128B-swizzled tiles need 1024-byte alignment
+    if (threadIdx.x == 0) atomicOr(&g_device_error, kErrSmemAlign);
+    return;
+  }
+  auto* bars = reinterpret_cast<Barriers<kStages>*>(smem + P::kBarrierOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -141,10 +165,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    uint32_t armed[kStages];
-#pragma unroll
-    for (int s = 0; s < kStages; ++s) armed[s] = 0;
     if (lane == 0) {
+      uint32_t armed[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) armed[s] = 0;
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !aborted(bars); tile += gridDim.x) {
@@ -246,10 +270,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;             // TMEM lane quadrant this warp may read
-    const int half = (warp - 2) >> 2;      // column half: 0 -> 0..127, 1 -> 128..255
+    // Warp w reads TMEM lanes 32*(w%4).. (its quadrant) and columns
+    // [64*q, 64*q+64), q = (w-2)/4.  Phase 1 pulls the accumulator slice into
+    // registers, forms the mm_fp4 output bf16(alpha*acc) and frees TMEM for
+    // the next tile; phase 2 adds the bias (and GELU) and stores.
+    const int quad = warp & 3;
+    const int quarter = (warp - 2) >> 2;
+    const int col_base = quarter * 64;
+    const int trow = quad * 32 + lane;
     // alpha = 1 / (g_a * g_w): torch's reciprocal of the product, IEEE rounded
     const float alpha = alpha_in != nullptr ? *alpha_in : __frcp_rn(__fmul_rn(*g_a, *g_w));
+    uint8_t* staging = smem + P::kStagingOff;
     float amax = 0.0f;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -260,42 +291,89 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       tc_fence_after();
       const int mb = tile % num_m_blocks;
       const int nb = tile / num_m_blocks;
-      uint32_t r[128];
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + half * 128;
+      uint32_t r[64];
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + col_base;
       tmem_ld_32x32b_x32(taddr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
       tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_ld_32x32b_x32(taddr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-      tmem_ld_32x32b_x32(taddr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->acc_empty);
-
-      const int row = mb * BM + quad * 32 + lane;
-      const int col0 = nb * BN + half * 128;
-      uint16_t* dst = out + static_cast<int64_t>(row) * n + col0;
+      // mm_fp4's output: bf16(alpha * acc), packed in pairs
+      uint32_t y[32];
 #pragma unroll
-      for (int c = 0; c < 128; c += 8) {
-        uint4 bv = make_uint4(0, 0, 0, 0);
-        if (bias != nullptr) bv = __ldg(reinterpret_cast<const uint4*>(bias + col0 + c));
-        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-        uint32_t o[4];
+      for (int j = 0; j < 32; ++j) {
+        y[j] = pack_bf16x2(__fmul_rn(__uint_as_float(r[2 * j]), alpha),
+                           __fmul_rn(__uint_as_float(r[2 * j + 1]), alpha));
+      }
+      const int col0 = nb * BN + col_base;
+      if constexpr (P::kStaged) {
+        // stage row `trow` (64 bf16 = 8 chunks of 16 B), chunk index XOR-swizzled by row
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float v0 = bf16_round(__fmul_rn(__uint_as_float(r[c + 2 * j]), alpha));
-          float v1 = bf16_round(__fmul_rn(__uint_as_float(r[c + 2 * j + 1]), alpha));
+        for (int q = 0; q < 8; ++q) {
+          const int phys = quarter * 8 + (q ^ (trow & 7));
+          *reinterpret_cast<uint4*>(staging + trow * (BN * 2) + phys * 16) =
+              make_uint4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+        }
+        __syncwarp();
+        // phase 2: lane handles columns col0 + 2*lane, +1 of each of the warp's 32 rows
+        float b0 = 0.0f, b1 = 0.0f;
+        if (bias != nullptr) {
+          const uint32_t bw = __ldg(reinterpret_cast<const uint32_t*>(bias + col0) + lane);
+          b0 = bf16_lo(bw);
+          b1 = bf16_hi(bw);
+        }
+        const int rchunk = quarter * 8;
+        const int lchunk = lane >> 2;
+        const int lword = (lane & 3) * 4;
+#pragma unroll 4
+        for (int rr = 0; rr < 32; ++rr) {
+          const int row_t = quad * 32 + rr;
+          const int grow = mb * BM + row_t;
+          const uint32_t hv = *reinterpret_cast<const uint32_t*>(
+              staging + row_t * (BN * 2) + (rchunk + (lchunk ^ (row_t & 7))) * 16 + lword);
+          float v0 = bf16_lo(hv), v1 = bf16_hi(hv);
           if (bias != nullptr) {
-            v0 = bf16_round(v0 + __uint_as_float(bw[j] << 16));
-            v1 = bf16_round(v1 + __uint_as_float(bw[j] & 0xFFFF0000u));
+            v0 = bf16_round(v0 + b0);
+            v1 = bf16_round(v1 + b1);
           }
           if (kEpi == 1) {
             v0 = bf16_round(gelu_tanh(v0));
             v1 = bf16_round(gelu_tanh(v1));
-            amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
+            if (grow < m) amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
           }
-          o[j] = pack_bf16x2(v0, v1);
+          if (grow < m) {
+            *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(grow) * n + col0 + 2 * lane) =
+                pack_bf16x2(v0, v1);
+          }
         }
-        if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+        __syncwarp();
+      } else {
+        const int row = mb * BM + trow;
+        uint16_t* dst = out + static_cast<int64_t>(row) * n + col0;
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          uint4 bv = make_uint4(0, 0, 0, 0);
+          if (bias != nullptr) bv = __ldg(reinterpret_cast<const uint4*>(bias + col0 + c));
+          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t w = y[c / 2 + j];
+            float v0 = bf16_lo(w), v1 = bf16_hi(w);
+            if (bias != nullptr) {
+              v0 = bf16_round(v0 + bf16_lo(bw[j]));
+              v1 = bf16_round(v1 + bf16_hi(bw[j]));
+            }
+            if (kEpi == 1) {
+              v0 = bf16_round(gelu_tanh(v0));
+              v1 = bf16_round(gelu_tanh(v1));
+              if (row < m) amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
+            }
+            o[j] = pack_bf16x2(v0, v1);
+          }
+          if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
       }
     }
     if (kEpi == 1) {
@@ -352,6 +430,7 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const ui
                           const float* alpha, const uint16_t* bias, uint16_t* out, int m, int n,
                           int k, float* amax_out, uint64_t wait_limit, cudaStream_t st) {
   static bool attr_set[64] = {false};
+  constexpr int kSmemBytes = Plan<kEpi>::kSmemBytes;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {

@@ -12,6 +12,7 @@ constexpr uint32_t kErrWaitProducer = 1u << 0;  // producer gave up on an empty 
 constexpr uint32_t kErrWaitMma = 1u << 1;       // MMA warp gave up on a full stage / accumulator
 constexpr uint32_t kErrWaitEpilogue = 1u << 2;  // epilogue gave up on the accumulator
 constexpr uint32_t kErrWaitTeardown = 1u << 3;  // teardown gave up on in-flight work
+constexpr uint32_t kErrSmemAlign = 1u << 4;     // dynamic shared memory not 1024-byte aligned
 
 // Bound on any single pipeline wait inside a kernel (wall time, ns).
 constexpr uint64_t kDefaultWaitLimit = 2000000000ull;

@@ -129,7 +129,7 @@ def test_quantize_dynamic_uses_amax():
     assert g.item() == g2.item()
     assert torch.equal(q.cpu(), torch.from_numpy(q2))
     assert np.array_equal(s.cpu().numpy().reshape(-1), s2)
-    assert not ws.any(), "amax workspace must be left zeroed"
+    assert not ws[:4].any(), "the amax arrival counter must be re-armed (zero) after each call"
 
 
 @pytest.mark.parametrize("numel", [1, 7, 8, 9, 4095, 4096 * 3 + 5, 1 << 20])
