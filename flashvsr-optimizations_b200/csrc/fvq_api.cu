@@ -32,6 +32,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// the quantizer reads bf16 inputs in 32-byte vectors
+bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
 int check_device() {
   static int ok_cache[64] = {0};  // 0 unknown, 1 ok, -1 bad
@@ -136,8 +138,8 @@ int fvq_nvfp4_quantize(const uint16_t* x, int64_t rows, int64_t k, const float* 
                        uint8_t* codes, uint8_t* sf, void* stream) {
   if (int rc = check_quant_shape(rows, k, "fvq_nvfp4_quantize")) return rc;
   if (!x || !g || !codes || !sf) return fail(FVQ_EINVAL, "fvq_nvfp4_quantize: NULL pointer");
-  if (!aligned16(x) || !aligned16(codes) || !aligned16(sf))
-    return fail(FVQ_EALIGN, "fvq_nvfp4_quantize: x, codes and sf must be 16-byte aligned");
+  if (!aligned32(x) || !aligned16(codes) || !aligned16(sf))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_quantize: x must be 32-byte aligned, codes and sf 16-byte");
   if (int rc = check_device()) return rc;
   cudaError_t e = fvq::launch_quantize(x, rows, k, g, nullptr, nullptr, codes, sf, nullptr,
                                        static_cast<cudaStream_t>(stream));
@@ -150,8 +152,9 @@ int fvq_nvfp4_quantize_dynamic(const uint16_t* x, int64_t rows, int64_t k, const
                                size_t workspace_bytes, void* stream) {
   if (int rc = check_quant_shape(rows, k, "fvq_nvfp4_quantize_dynamic")) return rc;
   if (!x || !codes || !sf) return fail(FVQ_EINVAL, "fvq_nvfp4_quantize_dynamic: NULL pointer");
-  if (!aligned16(x) || !aligned16(codes) || !aligned16(sf))
-    return fail(FVQ_EALIGN, "fvq_nvfp4_quantize_dynamic: x, codes and sf must be 16-byte aligned");
+  if (!aligned32(x) || !aligned16(codes) || !aligned16(sf))
+    return fail(FVQ_EALIGN,
+                "fvq_nvfp4_quantize_dynamic: x must be 32-byte aligned, codes and sf 16-byte");
   if (int rc = check_device()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const float* amax = amax_in;
@@ -236,8 +239,8 @@ int fvq_nvfp4_linear(const uint16_t* x, int64_t rows, const fvq_linear* lin, uin
   if (workspace_bytes < need)
     return fail(FVQ_EWORKSPACE, "fvq_nvfp4_linear: workspace needs %zu bytes, got %zu", need,
                 workspace_bytes);
-  if (!aligned16(x) || !aligned16(y) || !aligned16(workspace))
-    return fail(FVQ_EALIGN, "fvq_nvfp4_linear: x, y and workspace must be 16-byte aligned");
+  if (!aligned32(x) || !aligned16(y) || !aligned16(workspace))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_linear: x must be 32-byte aligned, y and workspace 16-byte");
   if (int rc = check_device()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t k = lin->in_features;
@@ -283,8 +286,8 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
   if (workspace_bytes < need)
     return fail(FVQ_EWORKSPACE, "fvq_nvfp4_ffn: workspace needs %zu bytes, got %zu", need,
                 workspace_bytes);
-  if (!aligned16(x) || !aligned16(y) || !aligned16(workspace))
-    return fail(FVQ_EALIGN, "fvq_nvfp4_ffn: x, y and workspace must be 16-byte aligned");
+  if (!aligned32(x) || !aligned16(y) || !aligned16(workspace))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_ffn: x must be 32-byte aligned, y and workspace 16-byte");
   if (int rc = check_device()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carve c(workspace);
@@ -322,6 +325,15 @@ int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream) {
   if (int rc = check_device()) return rc;
   cudaError_t e = fvq::launch_rcp_probe(in, out, n, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "fvq_rcp_approx_probe launch");
+  return FVQ_OK;
+}
+
+int fvq_gelu_bf16_probe(const uint16_t* in, uint16_t* out, int64_t count, void* stream) {
+  if (count < 0 || (count > 0 && (!in || !out)))
+    return fail(FVQ_EINVAL, "fvq_gelu_bf16_probe: bad args");
+  if (int rc = check_device()) return rc;
+  cudaError_t e = fvq::launch_gelu_probe(in, out, count, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_gelu_bf16_probe launch");
   return FVQ_OK;
 }
 

@@ -42,26 +42,40 @@ constexpr int kABytes = BM * BKB;                // 16 KB
 constexpr int kBBytes = BN * BKB;                // 32 KB
 constexpr int kSfaBytes = BM * (BK / 16);        // 2 KB
 constexpr int kSfbBytes = BN * (BK / 16);        // 4 KB
-constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;  // 54 KB
 constexpr int kEpiWarps = 16;                    // 4 per TMEM lane quadrant, 64 columns each
-constexpr int kNumThreads = 64 + 32 * kEpiWarps;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kNumThreads = 64 + kEpiThreads;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSfaCol = 256;
-constexpr uint32_t kSfbCol = 272;
+constexpr uint32_t kSfaCol = 256;                // A scales: 16 columns (4 K-steps x 4)
+constexpr uint32_t kSfbCol = 272;                // W scales: 8 columns per K-step
+constexpr int kMaxResidentKSteps = (512 - 272) / 8;  // W scales of up to K = 1920 stay in TMEM
 constexpr int kBarrierBytes = 256;
 constexpr int kStagingBytes = BM * BN * 2;       // bf16 tile staged for coalesced stores
 
-// Shared memory plan per epilogue kind: GEMM1 (GELU) keeps 3 operand stages
-// and a 64 KB bf16 staging tile; GEMM2 (plain) keeps 4 stages and stores
-// straight from registers.
-template <int kEpi>
+// GELU of a bf16 input is a function of 16 bits.  Inputs with exponent field
+// in [115, 130) (|x| in [2^-12, 8)) are tabulated per CTA in shared memory
+// (computed with the exact fp32 formula at kernel start); all other inputs
+// take the exact formula directly.  Entry: sign * 1920 + (bits & 0x7FFF) - 14720.
+constexpr uint32_t kGeluTabLo = 115u << 7;       // 14720
+constexpr uint32_t kGeluTabSpan = 15u << 7;      // 1920
+constexpr int kGeluTabEntries = 2 * kGeluTabSpan;
+constexpr int kGeluTabBytes = kGeluTabEntries * 2;
+
+// Shared-memory plan.  kResident: the W scales of the CTA's single N block
+// are loaded into TMEM once (K <= 1920), so stages carry only A, W and A scales.
+template <int kEpi, bool kResident>
 struct Plan {
-  static constexpr int kStages = kEpi == 1 ? 3 : 4;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + (kResident ? 0 : kSfbBytes);
+  static constexpr int kStages = kEpi == 0 ? 4 : (kResident ? 3 : 2);
   static constexpr bool kStaged = kEpi == 1;
   static constexpr int kStagingOff = kStages * kStageBytes;
-  static constexpr int kBarrierOff = kStagingOff + (kStaged ? kStagingBytes : 0);
+  static constexpr int kTableOff = kStagingOff + (kStaged ? kStagingBytes : 0);
+  static constexpr int kBarrierOff = kTableOff + (kEpi == 1 ? kGeluTabBytes : 0);
   static constexpr int kSmemBytes = kBarrierOff + kBarrierBytes;
 };
+static_assert(Plan<1, true>::kSmemBytes <= 232448, "GEMM1 resident plan exceeds shared memory");
+static_assert(Plan<1, false>::kSmemBytes <= 232448, "GEMM1 streaming plan exceeds shared memory");
+static_assert(Plan<0, false>::kSmemBytes <= 232448, "GEMM2 plan exceeds shared memory");
 
 // Instruction descriptor, kind::mxf4nvf4: A/B E2M1 (1), UE4M3 scales (0),
 // K-major A and B, N = 256 (>>3 at bit 17), M = 128 (>>4 at bit 24).
@@ -75,6 +89,7 @@ struct Barriers {
   uint64_t acc_full;
   uint64_t acc_empty;
   uint64_t teardown;
+  uint64_t sfb_full;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -95,10 +110,11 @@ __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
 
+// Two floats -> two bf16 (round to nearest even) in one cvt.rn.bf16x2.f32.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
-  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
-  return a | (b << 16);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
@@ -113,7 +129,73 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanhf(inner));
 }
 
-template <int kEpi>
+__device__ __noinline__ uint32_t gelu_bf16_exact(uint32_t x_bits) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(gelu_tanh(__uint_as_float(x_bits << 16))));
+}
+
+__device__ __forceinline__ void gelu_table_init(uint16_t* tab, int tid, int nthreads) {
+  for (int i = tid; i < kGeluTabEntries; i += nthreads) {
+    const uint32_t sign = i >= static_cast<int>(kGeluTabSpan) ? 0x8000u : 0u;
+    const uint32_t off = static_cast<uint32_t>(i) - (sign ? kGeluTabSpan : 0u);
+    tab[i] = static_cast<uint16_t>(gelu_bf16_exact(sign | (kGeluTabLo + off)));
+  }
+}
+
+// bf16(gelu(x)) for a bf16 input, bit-identical to the exact formula.
+__device__ __forceinline__ uint32_t gelu_bf16(uint32_t x_bits, const uint16_t* tab) {
+  const uint32_t off = (x_bits & 0x7FFFu) - kGeluTabLo;
+  if (off < kGeluTabSpan) return tab[off + ((x_bits & 0x8000u) ? kGeluTabSpan : 0u)];
+  return gelu_bf16_exact(x_bits);
+}
+
+// Both halves of a bf16x2 word at once: table indices are formed with 16-bit
+// SIMD ops; a half outside the table range takes the exact formula.
+__device__ __forceinline__ uint32_t gelu_bf16x2(uint32_t hv, const uint16_t* tab) {
+  const uint32_t a2 = hv & 0x7FFF7FFFu;
+  const uint32_t off2 = __vsub2(a2, (kGeluTabLo << 16) | kGeluTabLo);
+  const uint32_t in2 = __vcmpltu2(off2, (kGeluTabSpan << 16) | kGeluTabSpan);  // 0xFFFF per half
+  const uint32_t idx2 = off2 + ((hv >> 15) & 0x00010001u) * kGeluTabSpan;
+  if (in2 == 0xFFFFFFFFu) {
+    const uint32_t lo = tab[idx2 & 0xFFFFu];
+    const uint32_t hi = tab[idx2 >> 16];
+    return lo | (hi << 16);
+  }
+  return gelu_bf16(hv & 0xFFFFu, tab) | (gelu_bf16(hv >> 16, tab) << 16);
+}
+
+// Tiles of one CTA.  Streaming: tile t = blockIdx + i*grid, M-block fastest.
+// Resident: the CTA keeps one N block (blockIdx % NB) and strides over M blocks.
+template <bool kResident>
+struct TileSeq {
+  int count, nb_fixed, mb0, mb_step, num_m_blocks;
+  __device__ TileSeq(int num_m, int num_n) : num_m_blocks(num_m) {
+    const int c = blockIdx.x, g = gridDim.x;
+    if (kResident) {
+      nb_fixed = c % num_n;
+      mb0 = c / num_n;
+      mb_step = (g - 1 - nb_fixed) / num_n + 1;
+      count = mb0 < num_m ? (num_m - 1 - mb0) / mb_step + 1 : 0;
+    } else {
+      const int tiles = num_m * num_n;
+      nb_fixed = 0;
+      mb0 = 0;
+      mb_step = 0;
+      count = c < tiles ? (tiles - 1 - c) / g + 1 : 0;
+    }
+  }
+  __device__ void at(int i, int& mb, int& nb) const {
+    if (kResident) {
+      mb = mb0 + i * mb_step;
+      nb = nb_fixed;
+    } else {
+      const int t = blockIdx.x + i * gridDim.x;
+      mb = t % num_m_blocks;
+      nb = t / num_m_blocks;
+    }
+  }
+};
+
+template <int kEpi, bool kResident>
 __global__ void __launch_bounds__(kNumThreads, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b, const uint8_t* __restrict__ a_sf,
@@ -121,8 +203,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                       const float* __restrict__ g_w, const float* __restrict__ alpha_in,
                       const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m, int n,
                       int k, float* amax_out, uint64_t wait_limit) {
-  using P = Plan<kEpi>;
+  using P = Plan<kEpi, kResident>;
   constexpr int kStages = P::kStages;
+  constexpr int kStageBytes = P::kStageBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
   if ((smem_u32(smem) & 1023u) != 0) {  // the 128B-swizzled tiles need 1024-byte alignment
@@ -130,15 +213,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     return;
   }
   auto* bars = reinterpret_cast<Barriers<kStages>*>(smem + P::kBarrierOff);
+  uint8_t* staging = smem + P::kStagingOff;
+  uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + P::kTableOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_m_blocks = (m + BM - 1) / BM;
   const int num_n_blocks = n / BN;
-  const int num_tiles = num_m_blocks * num_n_blocks;
   const int num_k_tiles = k / BK;
   const int64_t sf_tile_stride = static_cast<int64_t>(k / 64) * 512;  // bytes per 128-row block
   const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
+  const TileSeq<kResident> seq(num_m_blocks, num_n_blocks);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -148,6 +233,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     mbar_init(&bars->acc_full, 1);
     mbar_init(&bars->acc_empty, kEpiWarps);
     mbar_init(&bars->teardown, 1);
+    mbar_init(&bars->sfb_full, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -165,15 +251,25 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    if (lane == 0 && seq.count > 0) {
+      bool sfb_armed = false;
+      if (kResident) {
+        // the W scales of this CTA's N block, all K: two contiguous 128-row runs
+        mbar_arrive_expect_tx(&bars->sfb_full, static_cast<uint32_t>(2 * sf_tile_stride));
+        bulk_load(staging, w_sf + (2 * seq.nb_fixed) * sf_tile_stride,
+                  static_cast<uint32_t>(sf_tile_stride), &bars->sfb_full);
+        bulk_load(staging + sf_tile_stride, w_sf + (2 * seq.nb_fixed + 1) * sf_tile_stride,
+                  static_cast<uint32_t>(sf_tile_stride), &bars->sfb_full);
+        sfb_armed = true;
+      }
       uint32_t armed[kStages];
 #pragma unroll
       for (int s = 0; s < kStages; ++s) armed[s] = 0;
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !aborted(bars); tile += gridDim.x) {
-        const int mb = tile % num_m_blocks;
-        const int nb = tile / num_m_blocks;
+      for (int i = 0; i < seq.count && !aborted(bars); ++i) {
+        int mb, nb;
+        seq.at(i, mb, nb);
         for (int kt = 0; kt < num_k_tiles; ++kt) {
           if (!mbar_wait_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
             flag_error(bars, kErrWaitProducer);
@@ -182,14 +278,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sa = smem + stage * kStageBytes;
           uint8_t* sb = sa + kABytes;
           uint8_t* ssfa = sb + kBBytes;
-          uint8_t* ssfb = ssfa + kSfaBytes;
           mbar_arrive_expect_tx(&bars->full[stage], kStageBytes);
           tma_load_2d(sa, &tmap_a, &bars->full[stage], kt * BKB, mb * BM);
           tma_load_2d(sb, &tmap_b, &bars->full[stage], kt * BKB, nb * BN);
           bulk_load(ssfa, a_sf + mb * sf_tile_stride + kt * 2048, kSfaBytes, &bars->full[stage]);
-          bulk_load(ssfb, w_sf + (2 * nb) * sf_tile_stride + kt * 2048, 2048, &bars->full[stage]);
-          bulk_load(ssfb + 2048, w_sf + (2 * nb + 1) * sf_tile_stride + kt * 2048, 2048,
-                    &bars->full[stage]);
+          if (!kResident) {
+            uint8_t* ssfb = ssfa + kSfaBytes;
+            bulk_load(ssfb, w_sf + (2 * nb) * sf_tile_stride + kt * 2048, 2048, &bars->full[stage]);
+            bulk_load(ssfb + 2048, w_sf + (2 * nb + 1) * sf_tile_stride + kt * 2048, 2048,
+                      &bars->full[stage]);
+          }
           armed[stage] += 1;
           if (++stage == kStages) {
             stage = 0;
@@ -197,32 +295,48 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
         }
       }
-      // every armed stage must have landed before shared memory goes away;
-      // this wait keeps the default limit even when a short one was requested
+      // everything armed must have landed before shared memory goes away;
+      // these waits keep the default limit even when a short one was requested
       for (int s = 0; s < kStages; ++s) {
         if (armed[s] > 0 &&
             !mbar_wait_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit)) {
           flag_error(bars, kErrWaitTeardown);
         }
       }
+      if (sfb_armed && !mbar_wait_bounded(&bars->sfb_full, 0, teardown_limit))
+        flag_error(bars, kErrWaitTeardown);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && seq.count > 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int local = 0;
       bool issued_any = false;
+      bool ok = true;
       const uint32_t acc = tmem;
-      for (int tile = blockIdx.x; tile < num_tiles && !aborted(bars);
-           tile += gridDim.x, ++local) {
-        if (!mbar_wait_bounded(&bars->acc_empty, (static_cast<uint32_t>(local) & 1u) ^ 1u,
+      if (kResident) {
+        if (!mbar_wait_bounded(&bars->sfb_full, 0, wait_limit)) {
+          flag_error(bars, kErrWaitMma);
+          ok = false;
+        } else {
+          tc_fence_after();
+          for (int s = 0; s < k / 64; ++s) {
+            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * s,
+                               make_smem_desc(smem_u32(staging + 512 * s), 16, 128, 0));
+            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * s + 4,
+                               make_smem_desc(smem_u32(staging + sf_tile_stride + 512 * s), 16, 128,
+                                              0));
+          }
+          issued_any = true;
+        }
+      }
+      for (int i = 0; ok && i < seq.count && !aborted(bars); ++i) {
+        if (!mbar_wait_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
                                wait_limit)) {
           flag_error(bars, kErrWaitMma);
           break;
         }
         tc_fence_after();
-        bool ok = true;
         for (int kt = 0; kt < num_k_tiles; ++kt) {
           if (!mbar_wait_bounded(&bars->full[stage], phase, wait_limit)) {
             flag_error(bars, kErrWaitMma);
@@ -233,24 +347,26 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sa = smem + stage * kStageBytes;
           uint8_t* sb = sa + kABytes;
           uint8_t* ssfa = sb + kBBytes;
-          uint8_t* ssfb = ssfa + kSfaBytes;
           // scales: one 512-byte atom (32 rows x 16 B) per 64-deep K step
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             tmem_cp_32x128b_x4(tmem + kSfaCol + 4 * j,
                                make_smem_desc(smem_u32(ssfa + 512 * j), 16, 128, 0));
-            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j,
-                               make_smem_desc(smem_u32(ssfb + 512 * j), 16, 128, 0));
-            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j + 4,
-                               make_smem_desc(smem_u32(ssfb + 2048 + 512 * j), 16, 128, 0));
+            if (!kResident) {
+              uint8_t* ssfb = ssfa + kSfaBytes;
+              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j,
+                                 make_smem_desc(smem_u32(ssfb + 512 * j), 16, 128, 0));
+              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j + 4,
+                                 make_smem_desc(smem_u32(ssfb + 2048 + 512 * j), 16, 128, 0));
+            }
           }
           const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
           const uint64_t bdesc = make_smem_desc(smem_u32(sb), 16, 1024, 2);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
+            const uint32_t sfb = tmem + kSfbCol + 8 * (kResident ? kt * 4 + j : j);
             mma_nvf4(acc, adesc + static_cast<uint64_t>(2 * j), bdesc + static_cast<uint64_t>(2 * j),
-                     kIdesc, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j,
-                     (kt > 0 || j > 0) ? 1u : 0u);
+                     kIdesc, tmem + kSfaCol + 4 * j, sfb, (kt > 0 || j > 0) ? 1u : 0u);
           }
           issued_any = true;
           tc_commit(&bars->empty[stage]);
@@ -278,19 +394,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int quarter = (warp - 2) >> 2;
     const int col_base = quarter * 64;
     const int trow = quad * 32 + lane;
+    if constexpr (kEpi == 1) {
+      gelu_table_init(gelu_tab, threadIdx.x - 64, kEpiThreads);
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+    }
     // alpha = 1 / (g_a * g_w): torch's reciprocal of the product, IEEE rounded
     const float alpha = alpha_in != nullptr ? *alpha_in : __frcp_rn(__fmul_rn(*g_a, *g_w));
-    uint8_t* staging = smem + P::kStagingOff;
-    float amax = 0.0f;
-    int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      if (!mbar_wait_bounded(&bars->acc_full, static_cast<uint32_t>(local) & 1u, wait_limit)) {
+    uint32_t amax2 = 0;  // max |h| as two bf16 bit patterns
+    for (int i = 0; i < seq.count; ++i) {
+      if (!mbar_wait_bounded(&bars->acc_full, static_cast<uint32_t>(i) & 1u, wait_limit)) {
         flag_error(bars, kErrWaitEpilogue);
         break;
       }
       tc_fence_after();
-      const int mb = tile % num_m_blocks;
-      const int nb = tile / num_m_blocks;
+      int mb, nb;
+      seq.at(i, mb, nb);
       uint32_t r[64];
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + col_base;
       tmem_ld_32x32b_x32(taddr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
@@ -323,28 +441,35 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           b0 = bf16_lo(bw);
           b1 = bf16_hi(bw);
         }
-        const int rchunk = quarter * 8;
+        // chunk offsets of this lane's word in each row class (row & 7)
         const int lchunk = lane >> 2;
-        const int lword = (lane & 3) * 4;
-#pragma unroll 4
-        for (int rr = 0; rr < 32; ++rr) {
-          const int row_t = quad * 32 + rr;
-          const int grow = mb * BM + row_t;
-          const uint32_t hv = *reinterpret_cast<const uint32_t*>(
-              staging + row_t * (BN * 2) + (rchunk + (lchunk ^ (row_t & 7))) * 16 + lword);
-          float v0 = bf16_lo(hv), v1 = bf16_hi(hv);
-          if (bias != nullptr) {
-            v0 = bf16_round(v0 + b0);
-            v1 = bf16_round(v1 + b1);
+        uint32_t xoff[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          xoff[c] = static_cast<uint32_t>((quarter * 8 + (lchunk ^ c)) * 16 + (lane & 3) * 4);
+        const uint8_t* srow = staging + quad * 32 * (BN * 2);
+        uint16_t* orow = out + static_cast<int64_t>(mb * BM + quad * 32) * n + col0 + 2 * lane;
+        const int rows_here = min(32, m - (mb * BM + quad * 32));
+        auto row_word = [&](int rr, uint32_t xo) -> uint32_t {
+          uint32_t hv = *reinterpret_cast<const uint32_t*>(srow + rr * (BN * 2) + xo);
+          if (bias != nullptr) hv = pack_bf16x2(bf16_lo(hv) + b0, bf16_hi(hv) + b1);
+          if (kEpi == 1) hv = gelu_bf16x2(hv, gelu_tab);
+          return hv;
+        };
+        if (rows_here >= 32) {
+#pragma unroll 8
+          for (int rr = 0; rr < 32; ++rr) {
+            const uint32_t hv = row_word(rr, xoff[rr & 7]);
+            if (kEpi == 1) amax2 = __vmaxu2(amax2, hv & 0x7FFF7FFFu);
+            *reinterpret_cast<uint32_t*>(orow + static_cast<int64_t>(rr) * n) = hv;
           }
-          if (kEpi == 1) {
-            v0 = bf16_round(gelu_tanh(v0));
-            v1 = bf16_round(gelu_tanh(v1));
-            if (grow < m) amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
-          }
-          if (grow < m) {
-            *reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(grow) * n + col0 + 2 * lane) =
-                pack_bf16x2(v0, v1);
+        } else {
+          for (int rr = 0; rr < rows_here; ++rr) {
+            const uint32_t xo =
+                static_cast<uint32_t>((quarter * 8 + (lchunk ^ (rr & 7))) * 16 + (lane & 3) * 4);
+            const uint32_t hv = row_word(rr, xo);
+            if (kEpi == 1) amax2 = __vmaxu2(amax2, hv & 0x7FFF7FFFu);
+            *reinterpret_cast<uint32_t*>(orow + static_cast<int64_t>(rr) * n) = hv;
           }
         }
         __syncwarp();
@@ -359,25 +484,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint32_t o[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t w = y[c / 2 + j];
-            float v0 = bf16_lo(w), v1 = bf16_hi(w);
-            if (bias != nullptr) {
-              v0 = bf16_round(v0 + bf16_lo(bw[j]));
-              v1 = bf16_round(v1 + bf16_hi(bw[j]));
-            }
+            uint32_t w = y[c / 2 + j];
+            if (bias != nullptr) w = pack_bf16x2(bf16_lo(w) + bf16_lo(bw[j]), bf16_hi(w) + bf16_hi(bw[j]));
             if (kEpi == 1) {
-              v0 = bf16_round(gelu_tanh(v0));
-              v1 = bf16_round(gelu_tanh(v1));
-              if (row < m) amax = fmaxf(amax, fmaxf(fabsf(v0), fabsf(v1)));
+              w = gelu_bf16_exact(w & 0xFFFFu) | (gelu_bf16_exact(w >> 16) << 16);
+              if (row < m) amax2 = __vmaxu2(amax2, w & 0x7FFF7FFFu);
             }
-            o[j] = pack_bf16x2(v0, v1);
+            o[j] = w;
           }
           if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
     }
     if (kEpi == 1) {
-      const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, __float_as_uint(amax));
+      const uint32_t hmax = max(amax2 & 0xFFFFu, amax2 >> 16);
+      const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, hmax << 16);
       if (lane == 0 && bits != 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), bits);
     }
   }
@@ -386,6 +507,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// GELU of bf16 values through the epilogue's table-plus-exact path (test support).
+__global__ void __launch_bounds__(256) gelu_probe_kernel(const uint16_t* in, uint16_t* out,
+                                                         int64_t count) {
+  __shared__ uint16_t tab[kGeluTabEntries];
+  gelu_table_init(tab, threadIdx.x, blockDim.x);
+  __syncthreads();
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = static_cast<uint16_t>(gelu_bf16(in[i], tab));
 }
 
 // ---------------------------------------------------------------- host side
@@ -424,17 +556,17 @@ bool make_code_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t 
   return r == CUDA_SUCCESS;
 }
 
-template <int kEpi>
+template <int kEpi, bool kResident>
 cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const uint8_t* a_sf,
                           const uint8_t* w_sf, const float* g_a, const float* g_w,
                           const float* alpha, const uint16_t* bias, uint16_t* out, int m, int n,
                           int k, float* amax_out, uint64_t wait_limit, cudaStream_t st) {
   static bool attr_set[64] = {false};
-  constexpr int kSmemBytes = Plan<kEpi>::kSmemBytes;
+  constexpr int kSmemBytes = Plan<kEpi, kResident>::kSmemBytes;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_kernel<kEpi>,
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_kernel<kEpi, kResident>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
@@ -442,7 +574,7 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const ui
   const int tiles = ((m + BM - 1) / BM) * (n / BN);
   int grid = sm_count();
   if (grid > tiles) grid = tiles;
-  nvfp4_gemm_kernel<kEpi><<<grid, kNumThreads, kSmemBytes, st>>>(
+  nvfp4_gemm_kernel<kEpi, kResident><<<grid, kNumThreads, kSmemBytes, st>>>(
       ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit);
   return cudaGetLastError();
 }
@@ -460,12 +592,26 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
     if (why) *why = "cuTensorMapEncodeTiled failed for the code matrices";
     return cudaErrorInvalidValue;
   }
+  const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
   if (epilogue == 1) {
-    return launch_gemm_t<1>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, static_cast<int>(m),
-                            static_cast<int>(n), static_cast<int>(k), amax_out, wait_limit, st);
+    // W scales stay in TMEM when they fit and every N block gets a CTA
+    const bool resident = (k / 64) <= kMaxResidentKSteps && (n / BN) <= sm_count();
+    if (resident)
+      return launch_gemm_t<1, true>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
+                                    amax_out, wait_limit, st);
+    return launch_gemm_t<1, false>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
+                                   amax_out, wait_limit, st);
   }
-  return launch_gemm_t<0>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, static_cast<int>(m),
-                          static_cast<int>(n), static_cast<int>(k), amax_out, wait_limit, st);
+  return launch_gemm_t<0, false>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
+                                 amax_out, wait_limit, st);
+}
+
+cudaError_t launch_gelu_probe(const uint16_t* in, uint16_t* out, int64_t count, cudaStream_t st) {
+  if (count <= 0) return cudaSuccess;
+  int64_t blocks = (count + 255) / 256;
+  if (blocks > 1024) blocks = 1024;
+  gelu_probe_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(in, out, count);
+  return cudaGetLastError();
 }
 
 cudaError_t set_error_word(uint32_t v, cudaStream_t st) {

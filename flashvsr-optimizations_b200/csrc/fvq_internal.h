@@ -42,6 +42,7 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                         const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
                         int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
                         const char** why);
+cudaError_t launch_gelu_probe(const uint16_t* in, uint16_t* out, int64_t count, cudaStream_t st);
 cudaError_t set_error_word(uint32_t v, cudaStream_t st);
 cudaError_t read_error_word(uint32_t* v, cudaStream_t st);
 

@@ -5,8 +5,8 @@
 //   quantize kernel : NVFP4 codes + 128x4-swizzled E4M3 block scales
 //                     (reference: flashinfer.nvfp4_quantize, ffn_quantization.py:47, :64).
 //
-// Both stream the input once with 16-byte non-allocating loads, several loads in
-// flight per thread, on a grid of (SM count x 8) CTAs of 256 threads.
+// Both stream the input once with wide non-allocating loads, several in flight
+// per thread, on a grid of up to (SM count x 8) CTAs of 256 threads.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -19,7 +19,7 @@ namespace fvq {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 8;   // 16-byte loads in flight per thread in the amax pass
 
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
   uint4 v;
@@ -106,10 +106,31 @@ __global__ void __launch_bounds__(kThreads) amax_kernel(const uint16_t* __restri
 }
 
 // ---------------------------------------------------------------- quantize
-// Work unit: a "group" = 64 consecutive elements of one row = 4 scale blocks =
-// one 32-bit word of the swizzled scale layout.  8 threads share a group, 8
-// elements (one 16-byte load) each; a warp covers 4 consecutive groups.
-// Groups past the last row up to pad128(rows) only write zero scale words.
+// One thread per 16-element scale block (a 32-byte load); consecutive threads
+// take consecutive blocks, so a warp streams 1 KB per load instruction and
+// writes 256 contiguous code bytes.  The four scale bytes of a 64-column group
+// (held by 4 consecutive lanes) are gathered into one 32-bit store.  Blocks
+// past the last row, up to pad128(rows), only write zero scale words.
+__device__ __forceinline__ void ld_stream_v8(const void* p, uint32_t (&r)[8]) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "l"(p));
+}
+
+// (lo, hi) * s with flush-to-zero, as one packed f32x2 multiply.
+__device__ __forceinline__ void mul2_ftz(float lo, float hi, float s, float& olo, float& ohi) {
+  asm("{\n\t.reg .b64 a, b, c;\n\t"
+      "mov.b64 a, {%2, %3};\n\t"
+      "mov.b64 b, {%4, %4};\n\t"
+      "mul.rn.ftz.f32x2 c, a, b;\n\t"
+      "mov.b64 {%0, %1}, c;\n\t}"
+      : "=f"(olo), "=f"(ohi)
+      : "f"(lo), "f"(hi), "f"(s));
+}
+
+constexpr int kQuantUnroll = 2;
+
 __global__ void __launch_bounds__(kThreads) quantize_kernel(
     const uint16_t* __restrict__ x, int64_t rows, int64_t k, const float* __restrict__ g_ptr,
     const float* __restrict__ amax_ptr, float* g_out, uint8_t* __restrict__ codes,
@@ -123,55 +144,64 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(
   const float rg = rcp_approx_ftz(g);
 
   const int lane = threadIdx.x & 31;
-  const int sub = lane & 7;        // 8-element slice within the group
-  const int gsel = lane >> 3;      // which of the warp's 4 groups
-  const int64_t gpr = k / 64;      // groups per row
-  const int64_t n_real = rows * gpr;
-  const int64_t n_all = pad_up_dev(rows) * gpr;
-  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
-  const int64_t stride = nwarps * 4;
+  const int64_t bpr = k / 16;                      // scale blocks per row
+  const int64_t gpr = k / 64;                      // 64-column groups per row
+  const int64_t n_real = rows * bpr;
+  const int64_t n_all = pad_up_dev(rows) * bpr;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  const uint32_t* xw = reinterpret_cast<const uint32_t*>(x);
 
-  for (int64_t base = warp * 4; base < n_all; base += stride * kUnroll) {
-    uint4 v[kUnroll];
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; base - lane < n_all;
+       base += stride * kQuantUnroll) {
+    uint32_t v[kQuantUnroll][8];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t gi = base + u * stride + gsel;
-      v[u] = make_uint4(0, 0, 0, 0);
-      if (gi < n_real) v[u] = ld_stream(x + gi * 64 + sub * 8);
+    for (int u = 0; u < kQuantUnroll; ++u) {
+      const int64_t b = base + u * stride;
+      if (b < n_real) {
+        ld_stream_v8(xw + b * 8, v[u]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[u][j] = 0;
+      }
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t gi = base + u * stride + gsel;
-      // pair max -> the 16-element block maximum (exact, bf16 bits)
-      uint32_t bm = absmax8(v[u]);
-      bm = max(bm, __shfl_xor_sync(0xFFFFFFFFu, bm, 1));
+    for (int u = 0; u < kQuantUnroll; ++u) {
+      const int64_t b = base + u * stride;
+      // warp-uniform exit: the warp's blocks are consecutive
+      if (b - lane >= n_all) break;
+      const uint32_t* w = v[u];
+      const uint32_t m2 = __vmaxu2(
+          __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                   __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)),
+          __vmaxu2(__vmaxu2(w[4] & 0x7FFF7FFFu, w[5] & 0x7FFF7FFFu),
+                   __vmaxu2(w[6] & 0x7FFF7FFFu, w[7] & 0x7FFF7FFFu)));
+      const uint32_t bm = max(m2 & 0xFFFFu, m2 >> 16);   // block max |x|, bf16 bits (exact)
       const float vmax = __uint_as_float(bm << 16);
-      const float sfv_raw = mul_ftz(g, mul_ftz(vmax, r6));
-      const uint32_t s8 = f32_to_e4m3(sfv_raw);
+      const uint32_t s8 = f32_to_e4m3(mul_ftz(g, mul_ftz(vmax, r6)));
       const float sfv = e4m3_to_f32(s8);
       // vmax != 0 under flush-to-zero: a subnormal maximum counts as zero
       const float os = (bm >= 0x0080u) ? rcp_approx_ftz(mul_ftz(sfv, rg)) : 0.0f;
-      const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-      uint32_t packed = 0;
+      uint32_t byte[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float lo = mul_ftz(__uint_as_float(w[j] << 16), os);
-        const float hi = mul_ftz(__uint_as_float(w[j] & 0xFFFF0000u), os);
-        packed |= f32x2_to_e2m1x2(lo, hi) << (8 * j);
+      for (int j = 0; j < 8; ++j) {
+        float lo, hi;
+        mul2_ftz(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u), os, lo, hi);
+        byte[j] = f32x2_to_e2m1x2(lo, hi);
       }
-      // gather the group's 4 scale bytes (held by subs 0,2,4,6) into sub 0
-      const int lead = lane & ~7;
-      const uint32_t s1 = __shfl_sync(0xFFFFFFFFu, s8, lead + 2);
-      const uint32_t s2 = __shfl_sync(0xFFFFFFFFu, s8, lead + 4);
-      const uint32_t s3 = __shfl_sync(0xFFFFFFFFu, s8, lead + 6);
-      if (gi < n_real) {
-        reinterpret_cast<uint32_t*>(codes)[gi * 8 + sub] = packed;
+      const uint32_t c0 = byte[0] | (byte[1] << 8) | (byte[2] << 16) | (byte[3] << 24);
+      const uint32_t c1 = byte[4] | (byte[5] << 8) | (byte[6] << 16) | (byte[7] << 24);
+      // gather the group's 4 scale bytes into its first lane (b % 4 == lane % 4)
+      const int lead = lane & ~3;
+      const uint32_t s1 = __shfl_sync(0xFFFFFFFFu, s8, lead + 1);
+      const uint32_t s2 = __shfl_sync(0xFFFFFFFFu, s8, lead + 2);
+      const uint32_t s3 = __shfl_sync(0xFFFFFFFFu, s8, lead + 3);
+      if (b < n_real) {
+        *reinterpret_cast<uint2*>(codes + b * 8) = make_uint2(c0, c1);
       }
-      if (sub == 0 && gi < n_all) {
-        const int64_t row = gi / gpr;
-        const int64_t kc = gi - row * gpr;
-        const uint32_t word = (gi < n_real) ? (s8 | (s1 << 8) | (s2 << 16) | (s3 << 24)) : 0u;
+      if ((lane & 3) == 0 && b < n_all) {
+        const int64_t row = b / bpr;
+        const int64_t kc = (b - row * bpr) >> 2;
+        const uint32_t word = (b < n_real) ? (s8 | (s1 << 8) | (s2 << 16) | (s3 << 24)) : 0u;
         const int64_t off = (row >> 7) * (gpr * 512) + kc * 512 + (row & 31) * 16 +
                             ((row & 127) >> 5) * 4;
         *reinterpret_cast<uint32_t*>(sf + off) = word;
@@ -216,9 +246,8 @@ cudaError_t launch_amax(const uint16_t* x, int64_t numel, float* amax_out, float
 cudaError_t launch_quantize(const uint16_t* x, int64_t rows, int64_t k, const float* g,
                             const float* amax, float* g_out, uint8_t* codes, uint8_t* sf,
                             float* zero_word, cudaStream_t st) {
-  const int64_t n_all = pad_up(rows, 128) * (k / 64);
-  const int64_t warps_needed = (n_all + 4 * kUnroll - 1) / (4 * kUnroll);
-  int64_t blocks = (warps_needed + (kThreads / 32) - 1) / (kThreads / 32);
+  const int64_t n_all = pad_up(rows, 128) * (k / 16);
+  int64_t blocks = (n_all + kThreads * kQuantUnroll - 1) / (kThreads * kQuantUnroll);
   blocks = blocks < 1 ? 1 : blocks;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;

@@ -48,6 +48,13 @@ def _check_bf16(name: str, x: torch.Tensor) -> None:
         raise TypeError(f"{name}: expected bfloat16 input, got {x.dtype}")
 
 
+def _aligned32(x: torch.Tensor) -> torch.Tensor:
+    """The quantizer reads its bf16 input in 32-byte vectors: re-home a
+    contiguous tensor whose storage offset breaks that alignment."""
+    x = x.contiguous()
+    return x if x.data_ptr() % 32 == 0 else x.clone()
+
+
 # ---------------------------------------------------------------- workspaces
 class _Workspaces:
     """Zero-initialised scratch buffers, one per (device, stream), grown on demand.
@@ -125,7 +132,7 @@ def nvfp4_quantize(x: torch.Tensor, g: torch.Tensor) -> tuple[torch.Tensor, torc
     if x.dim() != 2:
         raise ValueError("nvfp4_quantize: expected a 2-D [M, K] tensor")
     m, k = x.shape
-    x = x.contiguous()
+    x = _aligned32(x)
     g = g.to(torch.float32).contiguous()
     codes = torch.empty((m, k // 2), dtype=torch.uint8, device=x.device)
     sf = torch.empty((sf_rows(m), k // 16), dtype=torch.uint8, device=x.device)
@@ -204,7 +211,7 @@ def nvfp4_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor,
     n = qweight.shape[0]
     if m == 0:
         raise RuntimeError("nvfp4_linear: empty input (the reference's global_scale fails on it)")
-    x = x.contiguous()
+    x = _aligned32(x)
     y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     lib = _lib.load()
     ws = workspace(x.device, lib.fvq_nvfp4_linear_workspace_bytes(m, k))
@@ -230,7 +237,7 @@ def nvfp4_ffn(x: torch.Tensor, q1: torch.Tensor, s1: torch.Tensor, g1: torch.Ten
     f = q1.shape[0]
     if m == 0:
         raise RuntimeError("nvfp4_ffn: empty input (the reference's global_scale fails on it)")
-    x = x.contiguous()
+    x = _aligned32(x)
     y = torch.empty((m, d), dtype=torch.bfloat16, device=x.device)
     lib = _lib.load()
     ws = workspace(x.device, lib.fvq_nvfp4_ffn_workspace_bytes(m, d, f))

@@ -19,6 +19,8 @@
  *
  * Shape limits: k % 64 == 0 for the quantizer; the GEMM needs k % 256 == 0
  * and n % 256 == 0 (d_model 1536 and d_ff 8960 both qualify).
+ * Alignment: bf16 inputs of the quantizer (and of linear / ffn) 32 bytes,
+ * every other pointer 16 bytes.
  */
 #ifndef FVQ_H_
 #define FVQ_H_
@@ -146,6 +148,13 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
  * reciprocal the quantizer uses (so a CPU checker can use measured values).
  */
 int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream);
+
+/*
+ * Test support: out[i] = bf16(gelu_tanh(in[i])) through the GEMM epilogue's
+ * GELU path (a per-CTA table over |x| in [2^-12, 8) plus the exact fp32
+ * formula elsewhere), so it can be compared with torch over all 65536 inputs.
+ */
+int fvq_gelu_bf16_probe(const uint16_t* in, uint16_t* out, int64_t count, void* stream);
 
 /*
  * Bounded device waits: a GEMM whose pipeline wait exceeds the limit sets a

@@ -141,3 +141,20 @@ def test_mm_fp4_device_alpha_equals_gscales():
     y1, _ = ops.nvfp4_gemm(ta, tas, ga, tw, tws, gw)
     y2 = ops.mm_fp4(ta, tas, tw, tws, 1. / (ga * gw))
     assert torch.equal(y1, y2)
+
+
+def test_epilogue_gelu_matches_torch_on_every_bf16_input():
+    """The GELU epilogue (shared-memory table plus exact formula) equals torch's
+    GELU(approximate='tanh') on all 65536 bf16 inputs, NaNs compared as NaN."""
+    from flashvsr_optimizations_b200 import _lib
+    bits = torch.arange(0, 1 << 16, dtype=torch.int32).to(torch.int16).cuda()
+    x = bits.view(torch.bfloat16)
+    out = torch.empty_like(bits)
+    _lib.call("fvq_gelu_bf16_probe", bits.data_ptr(), out.data_ptr(), bits.numel(),
+              torch.cuda.current_stream().cuda_stream)
+    ref = torch.nn.functional.gelu(x, approximate="tanh")
+    got = out.view(torch.bfloat16)
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(got), nan)
+    mismatch = (got.view(torch.int16) != ref.view(torch.int16)) & ~nan
+    assert int(mismatch.sum()) == 0, bits[mismatch][:10].tolist()

@@ -47,6 +47,7 @@ def test_quantize_rejects_bad_shapes_and_alignment():
     assert _rc("fvq_nvfp4_quantize", base, 0, 64, base, base, base, None) == _lib.FVQ_EINVAL
     assert _rc("fvq_nvfp4_quantize", None, 4, 64, base, base, base, None) == _lib.FVQ_EINVAL
     assert _rc("fvq_nvfp4_quantize", base + 2, 4, 64, base, base, base, None) == _lib.FVQ_EALIGN
+    assert _rc("fvq_nvfp4_quantize", base + 16 if base % 32 == 0 else base, 4, 64, base, base, base, None) == _lib.FVQ_EALIGN
 
 
 def test_gemm_rejects_bad_shapes_and_epilogue():
@@ -80,7 +81,7 @@ def test_valid_call_without_gpu_fails_loudly():
     import torch
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
-    buf = ctypes.create_string_buffer(4096 + 16)
-    b = (ctypes.addressof(buf) + 15) // 16 * 16
+    buf = ctypes.create_string_buffer(4096 + 32)
+    b = (ctypes.addressof(buf) + 31) // 32 * 32
     rc = _rc("fvq_nvfp4_quantize", b, 4, 64, b, b, b, None)
     assert rc in (_lib.FVQ_ECUDA, _lib.FVQ_EDEVICE)
