@@ -74,8 +74,10 @@ int check_quant_shape(int64_t rows, int64_t k, const char* who) {
   if (k <= 0 || k % 64 != 0)
     return fail(FVQ_EINVAL, "%s: k must be a positive multiple of 64 (got %lld)", who,
                 (long long)k);
-  if (rows > (int64_t(1) << 31) || k > (int64_t(1) << 24))
-    return fail(FVQ_EINVAL, "%s: shape too large", who);
+  if (rows > (int64_t(1) << 31) || k > (int64_t(1) << 24) ||
+      (rows + 128) * (k / 16) >= (int64_t(1) << 31))
+    return fail(FVQ_EINVAL, "%s: shape too large (pad128(rows) * k / 16 must stay below 2^31)",
+                who);
   return FVQ_OK;
 }
 

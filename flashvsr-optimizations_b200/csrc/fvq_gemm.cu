@@ -148,19 +148,27 @@ __device__ __forceinline__ uint32_t gelu_bf16(uint32_t x_bits, const uint16_t* t
   return gelu_bf16_exact(x_bits);
 }
 
-// Both halves of a bf16x2 word at once: table indices are formed with 16-bit
-// SIMD ops; a half outside the table range takes the exact formula.
+// Both halves of a bf16x2 word; a half outside the table range takes the
+// exact formula.
 __device__ __forceinline__ uint32_t gelu_bf16x2(uint32_t hv, const uint16_t* tab) {
-  const uint32_t a2 = hv & 0x7FFF7FFFu;
-  const uint32_t off2 = __vsub2(a2, (kGeluTabLo << 16) | kGeluTabLo);
-  const uint32_t in2 = __vcmpltu2(off2, (kGeluTabSpan << 16) | kGeluTabSpan);  // 0xFFFF per half
-  const uint32_t idx2 = off2 + ((hv >> 15) & 0x00010001u) * kGeluTabSpan;
-  if (in2 == 0xFFFFFFFFu) {
-    const uint32_t lo = tab[idx2 & 0xFFFFu];
-    const uint32_t hi = tab[idx2 >> 16];
-    return lo | (hi << 16);
+  const uint32_t lo = hv & 0xFFFFu, hi = hv >> 16;
+  const uint32_t off_lo = (lo & 0x7FFFu) - kGeluTabLo;
+  const uint32_t off_hi = (hi & 0x7FFFu) - kGeluTabLo;
+  if (off_lo < kGeluTabSpan && off_hi < kGeluTabSpan) {
+    const uint32_t r_lo = tab[off_lo + (lo >> 15) * kGeluTabSpan];
+    const uint32_t r_hi = tab[off_hi + (hi >> 15) * kGeluTabSpan];
+    return r_lo | (r_hi << 16);
   }
-  return gelu_bf16(hv & 0xFFFFu, tab) | (gelu_bf16(hv >> 16, tab) << 16);
+  return gelu_bf16(lo, tab) | (gelu_bf16(hi, tab) << 16);
+}
+
+// bf16x2 add, one rounding of the exact sum.  For two bf16 operands this equals
+// torch's fp32 add followed by a bf16 rounding: the fp32 sum is exact unless
+// the exponents differ by more than 16, and then it lies far from a bf16 tie.
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
 }
 
 // Tiles of one CTA.  Streaming: tile t = blockIdx + i*grid, M-block fastest.
@@ -400,7 +408,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     // alpha = 1 / (g_a * g_w): torch's reciprocal of the product, IEEE rounded
     const float alpha = alpha_in != nullptr ? *alpha_in : __frcp_rn(__fmul_rn(*g_a, *g_w));
-    uint32_t amax2 = 0;  // max |h| as two bf16 bit patterns
+    uint32_t amax2 = 0;  // max |h| as a bf16 bit pattern
     for (int i = 0; i < seq.count; ++i) {
       if (!mbar_wait_bounded(&bars->acc_full, static_cast<uint32_t>(i) & 1u, wait_limit)) {
         flag_error(bars, kErrWaitEpilogue);
@@ -435,12 +443,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         __syncwarp();
         // phase 2: lane handles columns col0 + 2*lane, +1 of each of the warp's 32 rows
-        float b0 = 0.0f, b1 = 0.0f;
-        if (bias != nullptr) {
-          const uint32_t bw = __ldg(reinterpret_cast<const uint32_t*>(bias + col0) + lane);
-          b0 = bf16_lo(bw);
-          b1 = bf16_hi(bw);
-        }
+        const uint32_t bias2 =
+            bias != nullptr ? __ldg(reinterpret_cast<const uint32_t*>(bias + col0) + lane) : 0u;
         // chunk offsets of this lane's word in each row class (row & 7)
         const int lchunk = lane >> 2;
         uint32_t xoff[8];
@@ -452,7 +456,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int rows_here = min(32, m - (mb * BM + quad * 32));
         auto row_word = [&](int rr, uint32_t xo) -> uint32_t {
           uint32_t hv = *reinterpret_cast<const uint32_t*>(srow + rr * (BN * 2) + xo);
-          if (bias != nullptr) hv = pack_bf16x2(bf16_lo(hv) + b0, bf16_hi(hv) + b1);
+          if (bias != nullptr) hv = add_bf16x2(hv, bias2);
           if (kEpi == 1) hv = gelu_bf16x2(hv, gelu_tab);
           return hv;
         };
@@ -460,7 +464,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll 8
           for (int rr = 0; rr < 32; ++rr) {
             const uint32_t hv = row_word(rr, xoff[rr & 7]);
-            if (kEpi == 1) amax2 = __vmaxu2(amax2, hv & 0x7FFF7FFFu);
+            if (kEpi == 1) amax2 = max(amax2, max(hv & 0x7FFFu, (hv >> 16) & 0x7FFFu));
             *reinterpret_cast<uint32_t*>(orow + static_cast<int64_t>(rr) * n) = hv;
           }
         } else {
@@ -468,7 +472,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             const uint32_t xo =
                 static_cast<uint32_t>((quarter * 8 + (lchunk ^ (rr & 7))) * 16 + (lane & 3) * 4);
             const uint32_t hv = row_word(rr, xo);
-            if (kEpi == 1) amax2 = __vmaxu2(amax2, hv & 0x7FFF7FFFu);
+            if (kEpi == 1) amax2 = max(amax2, max(hv & 0x7FFFu, (hv >> 16) & 0x7FFFu));
             *reinterpret_cast<uint32_t*>(orow + static_cast<int64_t>(rr) * n) = hv;
           }
         }
@@ -485,10 +489,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             uint32_t w = y[c / 2 + j];
-            if (bias != nullptr) w = pack_bf16x2(bf16_lo(w) + bf16_lo(bw[j]), bf16_hi(w) + bf16_hi(bw[j]));
+            if (bias != nullptr) w = add_bf16x2(w, bw[j]);
             if (kEpi == 1) {
               w = gelu_bf16_exact(w & 0xFFFFu) | (gelu_bf16_exact(w >> 16) << 16);
-              if (row < m) amax2 = __vmaxu2(amax2, w & 0x7FFF7FFFu);
+              if (row < m) amax2 = max(amax2, max(w & 0x7FFFu, (w >> 16) & 0x7FFFu));
             }
             o[j] = w;
           }
@@ -497,8 +501,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
     if (kEpi == 1) {
-      const uint32_t hmax = max(amax2 & 0xFFFFu, amax2 >> 16);
-      const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, hmax << 16);
+      const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, amax2 << 16);
       if (lane == 0 && bits != 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), bits);
     }
   }

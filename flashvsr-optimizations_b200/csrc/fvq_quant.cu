@@ -29,11 +29,28 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
   return v;
 }
 
+// Packed bf16 maximum (max.bf16x2); on non-negative non-NaN values it orders
+// exactly like the bit patterns.
+__device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 // max of |bf16| over the 8 values of a uint4, as a bf16 bit pattern in the low 16 bits.
 __device__ __forceinline__ uint32_t absmax8(uint4 v) {
-  uint32_t m = __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
-                        __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
+  const uint32_t m = bmax2(bmax2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
+                           bmax2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
   return max(m & 0xFFFFu, m >> 16);
+}
+
+// four bytes (low 8 bits of each argument) -> one word, b0 lowest
+__device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
+  uint32_t lo, hi, r;
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(lo) : "r"(b0), "r"(b1));
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(hi) : "r"(b2), "r"(b3));
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(r) : "r"(lo), "r"(hi));
+  return r;
 }
 
 __device__ __forceinline__ int64_t pad_up_dev(int64_t r) { return (r + 127) / 128 * 128; }
@@ -118,17 +135,6 @@ __device__ __forceinline__ void ld_stream_v8(const void* p, uint32_t (&r)[8]) {
                : "l"(p));
 }
 
-// (lo, hi) * s with flush-to-zero, as one packed f32x2 multiply.
-__device__ __forceinline__ void mul2_ftz(float lo, float hi, float s, float& olo, float& ohi) {
-  asm("{\n\t.reg .b64 a, b, c;\n\t"
-      "mov.b64 a, {%2, %3};\n\t"
-      "mov.b64 b, {%4, %4};\n\t"
-      "mul.rn.ftz.f32x2 c, a, b;\n\t"
-      "mov.b64 {%0, %1}, c;\n\t}"
-      : "=f"(olo), "=f"(ohi)
-      : "f"(lo), "f"(hi), "f"(s));
-}
-
 constexpr int kQuantUnroll = 2;
 
 __global__ void __launch_bounds__(kThreads) quantize_kernel(
@@ -170,11 +176,10 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(
       // warp-uniform exit: the warp's blocks are consecutive
       if (b - lane >= n_all) break;
       const uint32_t* w = v[u];
-      const uint32_t m2 = __vmaxu2(
-          __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
-                   __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)),
-          __vmaxu2(__vmaxu2(w[4] & 0x7FFF7FFFu, w[5] & 0x7FFF7FFFu),
-                   __vmaxu2(w[6] & 0x7FFF7FFFu, w[7] & 0x7FFF7FFFu)));
+      const uint32_t m2 = bmax2(bmax2(bmax2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                                      bmax2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)),
+                                bmax2(bmax2(w[4] & 0x7FFF7FFFu, w[5] & 0x7FFF7FFFu),
+                                      bmax2(w[6] & 0x7FFF7FFFu, w[7] & 0x7FFF7FFFu)));
       const uint32_t bm = max(m2 & 0xFFFFu, m2 >> 16);   // block max |x|, bf16 bits (exact)
       const float vmax = __uint_as_float(bm << 16);
       const uint32_t s8 = f32_to_e4m3(mul_ftz(g, mul_ftz(vmax, r6)));
@@ -184,12 +189,11 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(
       uint32_t byte[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float lo, hi;
-        mul2_ftz(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u), os, lo, hi);
-        byte[j] = f32x2_to_e2m1x2(lo, hi);
+        byte[j] = f32x2_to_e2m1x2(mul_ftz(__uint_as_float(w[j] << 16), os),
+                                  mul_ftz(__uint_as_float(w[j] & 0xFFFF0000u), os));
       }
-      const uint32_t c0 = byte[0] | (byte[1] << 8) | (byte[2] << 16) | (byte[3] << 24);
-      const uint32_t c1 = byte[4] | (byte[5] << 8) | (byte[6] << 16) | (byte[7] << 24);
+      const uint32_t c0 = pack4(byte[0], byte[1], byte[2], byte[3]);
+      const uint32_t c1 = pack4(byte[4], byte[5], byte[6], byte[7]);
       // gather the group's 4 scale bytes into its first lane (b % 4 == lane % 4)
       const int lead = lane & ~3;
       const uint32_t s1 = __shfl_sync(0xFFFFFFFFu, s8, lead + 1);
@@ -199,8 +203,11 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(
         *reinterpret_cast<uint2*>(codes + b * 8) = make_uint2(c0, c1);
       }
       if ((lane & 3) == 0 && b < n_all) {
-        const int64_t row = b / bpr;
-        const int64_t kc = (b - row * bpr) >> 2;
+        // block indices stay below 2^31 (checked by the host), so 32-bit division
+        const uint32_t b32 = static_cast<uint32_t>(b);
+        const uint32_t row32 = b32 / static_cast<uint32_t>(bpr);
+        const int64_t row = row32;
+        const int64_t kc = (b32 - row32 * static_cast<uint32_t>(bpr)) >> 2;
         const uint32_t word = (b < n_real) ? (s8 | (s1 << 8) | (s2 << 16) | (s3 << 24)) : 0u;
         const int64_t off = (row >> 7) * (gpr * 512) + kc * 512 + (row & 31) * 16 +
                             ((row & 127) >> 5) * 4;

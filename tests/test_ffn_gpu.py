@@ -58,6 +58,20 @@ def test_ffn_small_matches_reference_golden(ffn_layer):
     assert rel <= FFN_TOL, rel
 
 
+def test_ffn_bit_identical_to_reference(ffn_layer):
+    """Same kernel order and roundings as FlashInfer's mm_fp4 + torch bias/GELU:
+    the fused FFN reproduces the reference's bf16 output bit for bit."""
+    ffn, _ = ffn_layer
+    fix = golden("ffn_64")
+    y = ffn(bits_to_dev(W.student_t(64, W.D_MODEL, seed=1)))
+    got = dev_to_bits(y)
+    assert np.array_equal(got, fix["y"]), f"{int((got != fix['y']).sum())} of {got.size} differ"
+    fix = golden("ffn_7680_rows")
+    y = ffn(bits_to_dev(W.student_t(W.M_ONE_LAYER, W.D_MODEL, seed=1)))
+    got = dev_to_bits(y[torch.from_numpy(fix["rows"]).cuda()])
+    assert np.array_equal(got, fix["y_rows"]), f"{int((got != fix['y_rows']).sum())} differ"
+
+
 def test_ffn_fused_equals_unfused_modules(ffn_layer):
     """The fused call computes exactly what QuantLinear -> GELU -> QuantLinear computes."""
     ffn, _ = ffn_layer
