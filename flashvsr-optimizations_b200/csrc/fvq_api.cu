@@ -111,6 +111,18 @@ int gemm_impl(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
 
 }  // namespace
 
+namespace fvq {
+int report_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+}  // namespace fvq
+
 extern "C" {
 
 int fvq_version(void) { return 100; }

@@ -28,6 +28,9 @@ inline size_t sf_bytes(int64_t rows, int64_t k) {
 
 int sm_count();
 
+// Record a message for fvq_last_error() and return `code` (fvq_api.cu).
+int report_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+
 // Kernels (fvq_quant.cu)
 cudaError_t launch_amax(const uint16_t* x, int64_t numel, float* amax_out, float* g_out,
                         uint32_t* ws, float* zero_word, cudaStream_t st);

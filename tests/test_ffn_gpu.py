@@ -102,8 +102,8 @@ def test_ffn_one_layer_7680_matches_reference_rows(ffn_layer):
 def test_ffn_matches_oracle(ffn_layer, m, seed):
     """Oracle with this GPU's measured reciprocals: agreement to accumulation rounding."""
     ffn, (w1, b1, w2, b2) = ffn_layer
-    l1 = O.OracleQuantLinear(w1, b1)
-    l2 = O.OracleQuantLinear(w2, b2)
+    l1 = O.OracleQuantLinear(w1, b1, gpu_rcp_table)
+    l2 = O.OracleQuantLinear(w2, b2, gpu_rcp_table)
     xb = W.student_t(m, W.D_MODEL, seed=seed)
     y_ref = O.ffn_forward(xb, l1, l2, rcp_provider=gpu_rcp_table)
     y = ffn(bits_to_dev(xb))
