@@ -327,7 +327,7 @@ def main():
     gemm_flop = tokens * FLOP_PER_TOKEN
     achieved = gemm_flop / (kt["gemm_ms"] * 1e-3) / 1e12
     traffic = None
-    tp = ROOT / "profiles" / "gemm_traffic.json"
+    tp = ROOT / "profiles" / "nvfp4_gemm_ffn_layer_7680tok_traffic.json"
     if tp.exists():
         try:
             traffic = json.loads(tp.read_text()).get("dram_bytes_per_gemm_pair")
