@@ -56,6 +56,8 @@ SIGNATURES = {
     "fvq_nvfp4_mm": (_c.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "fvq_nvfp4_linear_workspace_bytes": (_sz, [_i64, _i64]),
     "fvq_nvfp4_linear": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _vp, _vp, _sz, _vp]),
+    "fvq_nvfp4_linear_noalloc": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _vp, _vp]),
+    "fvq_noalloc_scratch_bytes": (_sz, []),
     "fvq_nvfp4_ffn_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "fvq_nvfp4_ffn": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _c.POINTER(FvqLinear), _vp,
                                  _vp, _sz, _vp]),

@@ -129,6 +129,24 @@ size_t fvq_nvfp4_linear_workspace_bytes(int64_t rows, int64_t in_features);
 int fvq_nvfp4_linear(const uint16_t* x, int64_t rows, const fvq_linear* lin, uint16_t* y,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * QuantLinear.forward for callers that cannot allocate device memory (code
+ * running inside another runtime's memory arena, plugins handed only their
+ * input and output buffers, callers that must not touch the allocator while
+ * work is in flight).  No counterpart in the reference; no workspace
+ * argument: the scratch that fvq_nvfp4_linear takes as a workspace comes from
+ * a fixed 16 MiB array built into the library (fvq_noalloc_scratch_bytes),
+ * which every GPU that loads the library holds until the process exits.
+ * Calls whose fvq_nvfp4_linear_workspace_bytes(rows, in_features) exceeds it
+ * return FVQ_EWORKSPACE.  The first call on a device looks the array's
+ * address up (cudaGetSymbolAddress); make it before any stream capture.  All
+ * calls share the array, so calls that overlap on the GPU race.  Nothing is
+ * allocated by this call.
+ */
+int fvq_nvfp4_linear_noalloc(const uint16_t* x, int64_t rows, const fvq_linear* lin, uint16_t* y,
+                             void* stream);
+size_t fvq_noalloc_scratch_bytes(void);
+
 /* Bytes of workspace fvq_nvfp4_ffn needs for `rows` tokens. */
 size_t fvq_nvfp4_ffn_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff);
 
