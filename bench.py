@@ -296,25 +296,27 @@ def main():
     e2e = e2e_timing(torch, dist, fvq, NVFP4FFN, sets, tokens, dev, stream, world,
                      min(args.steps, 500), args.warmup)
 
-    # ---- output gather (NCCL all_gather over NVLink) of one layer's output
+    # ---- output gather (NCCL all-gather over NVLink) of one layer's output
     gather = None
     if world > 1:
-        out = torch.empty(world * tokens, D_MODEL, dtype=torch.bfloat16, device=dev)
+        from flashvsr_optimizations_b200.sharding import gather_rows
+        total = tokens * world
         for _ in range(3):
-            dist.all_gather_into_tensor(out, ys[0])
+            gather_rows(ys[0], total)
         barrier_sync()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
         for _ in range(20):
-            dist.all_gather_into_tensor(out, ys[0])
+            gather_rows(ys[0], total)
         e.record(stream)
         barrier_sync()
         gms = s.elapsed_time(e) / 20
         t = torch.tensor([gms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         gms = float(t.item())
-        gather = {"ms": gms, "bytes": world * tokens * D_MODEL * 2,
-                  "busbw_GBps": (world - 1) * tokens * D_MODEL * 2 / (gms * 1e-3) / 1e9}
+        gather = {"ms": gms, "bytes": total * D_MODEL * 2,
+                  "busbw_GBps": (world - 1) * tokens * D_MODEL * 2 / (gms * 1e-3) / 1e9,
+                  "api": "sharding.gather_rows (NCCL all_gather_into_tensor)"}
 
     peaks = measured_peaks()
     fp4_cublas = fp4_library_peak(torch, dev) if rank == 0 else None

@@ -17,7 +17,7 @@
 //     shared memory and applies bias / GELU row by row with coalesced
 //     128-byte stores, or (GEMM2) adds the bias and stores from registers,
 //     while the next tile's MMAs run.
-// No TMA multicast: every CTA loads its own tiles.
+// Every CTA loads its own tiles (no loads shared across a CTA cluster).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
