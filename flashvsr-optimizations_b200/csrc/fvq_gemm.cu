@@ -13,10 +13,11 @@
 //     tcgen05.cp and issues tcgen05.mma.kind::mxf4nvf4 (K = 64 per MMA);
 //   * warps 2-17: epilogue; each thread owns one accumulator row and 64
 //     columns, pulls them into registers, forms bf16(alpha*acc), frees the
-//     accumulator for the next tile, then (GEMM1) stages the bf16 tile in
-//     shared memory and applies bias / GELU row by row with coalesced
-//     128-byte stores, or (GEMM2) adds the bias and stores from registers,
-//     while the next tile's MMAs run.
+//     accumulator for the next tile, then adds the bias and (GEMM1) applies
+//     GELU through a shared-memory table, tracks max |h| and writes the
+//     warp's 32 x 64 block through a swizzled staging buffer with one TMA
+//     tensor store, or (GEMM2) stores from registers, while the next tile's
+//     MMAs run.
 // Every CTA loads its own tiles (no loads shared across a CTA cluster).
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -55,11 +56,15 @@ constexpr int kStagingBytes = BM * BN * 2;       // bf16 tile staged for coalesc
 // GELU of a bf16 input is a function of 16 bits.  Inputs with exponent field
 // in [115, 130) (|x| in [2^-12, 8)) are tabulated per CTA in shared memory
 // (computed with the exact fp32 formula at kernel start); all other inputs
-// take the exact formula directly.  Entry: sign * 1920 + (bits & 0x7FFF) - 14720.
-constexpr uint32_t kGeluTabLo = 115u << 7;       // 14720
-constexpr uint32_t kGeluTabSpan = 15u << 7;      // 1920
-constexpr int kGeluTabEntries = 2 * kGeluTabSpan;
+// take the exact formula directly.  Entry index: (sign << 11) | ((bits &
+// 0x7FFF) - 0x3980), so the sign is one shifted bit of the input (indices
+// 0x780..0x7FF of each half are unused).
+constexpr uint32_t kGeluTabLo = 115u << 7;       // 0x3980 = 2^-12
+constexpr uint32_t kGeluTabSpan = 15u << 7;      // 0x780: magnitudes below 8.0
+constexpr int kGeluTabEntries = 4096;
 constexpr int kGeluTabBytes = kGeluTabEntries * 2;
+constexpr int kStageRowBytes = 128;              // one epilogue row: 64 bf16 columns
+constexpr int kWarpStagingBytes = 32 * kStageRowBytes;
 
 // Shared-memory plan.  kResident: the W scales of the CTA's single N block
 // are loaded into TMEM once (K <= 1920), so stages carry only A, W and A scales.
@@ -135,31 +140,57 @@ __device__ __noinline__ uint32_t gelu_bf16_exact(uint32_t x_bits) {
 
 __device__ __forceinline__ void gelu_table_init(uint16_t* tab, int tid, int nthreads) {
   for (int i = tid; i < kGeluTabEntries; i += nthreads) {
-    const uint32_t sign = i >= static_cast<int>(kGeluTabSpan) ? 0x8000u : 0u;
-    const uint32_t off = static_cast<uint32_t>(i) - (sign ? kGeluTabSpan : 0u);
-    tab[i] = static_cast<uint16_t>(gelu_bf16_exact(sign | (kGeluTabLo + off)));
+    const uint32_t off = static_cast<uint32_t>(i) & 0x7FFu;
+    const uint32_t sign = (static_cast<uint32_t>(i) & 0x800u) << 4;
+    tab[i] = off < kGeluTabSpan ? static_cast<uint16_t>(gelu_bf16_exact(sign | (kGeluTabLo + off)))
+                                : static_cast<uint16_t>(0);
   }
 }
 
 // bf16(gelu(x)) for a bf16 input, bit-identical to the exact formula.
 __device__ __forceinline__ uint32_t gelu_bf16(uint32_t x_bits, const uint16_t* tab) {
   const uint32_t off = (x_bits & 0x7FFFu) - kGeluTabLo;
-  if (off < kGeluTabSpan) return tab[off + ((x_bits & 0x8000u) ? kGeluTabSpan : 0u)];
+  if (off < kGeluTabSpan) return tab[off | ((x_bits & 0x8000u) >> 4)];
   return gelu_bf16_exact(x_bits);
 }
 
-// Both halves of a bf16x2 word; a half outside the table range takes the
-// exact formula.
-__device__ __forceinline__ uint32_t gelu_bf16x2(uint32_t hv, const uint16_t* tab) {
-  const uint32_t lo = hv & 0xFFFFu, hi = hv >> 16;
-  const uint32_t off_lo = (lo & 0x7FFFu) - kGeluTabLo;
-  const uint32_t off_hi = (hi & 0x7FFFu) - kGeluTabLo;
-  if (off_lo < kGeluTabSpan && off_hi < kGeluTabSpan) {
-    const uint32_t r_lo = tab[off_lo + (lo >> 15) * kGeluTabSpan];
-    const uint32_t r_hi = tab[off_hi + (hi >> 15) * kGeluTabSpan];
-    return r_lo | (r_hi << 16);
-  }
-  return gelu_bf16(lo, tab) | (gelu_bf16(hi, tab) << 16);
+__device__ __noinline__ uint32_t gelu_bf16x2_slow(uint32_t hv, const uint16_t* tab) {
+  return gelu_bf16(hv & 0xFFFFu, tab) | (gelu_bf16(hv >> 16, tab) << 16);
+}
+
+__device__ __forceinline__ uint32_t min_u16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("min.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+  uint32_t r;
+  asm("ld.shared.u16 %0, [%1];" : "=r"(r) : "r"(addr));
+  return r;
+}
+
+// GELU of both halves of a bf16x2 word.  Both magnitude offsets are formed in
+// one 32-bit subtraction and clamped to the last entry in one min.u16x2, so
+// the two lookups stay inside the table whatever the input; when either half
+// was clamped (outside [2^-12, 8), or a borrow from the low half) the pair is
+// recomputed on the slow path.  tab_base is the table's shared-memory address.
+__device__ __forceinline__ uint32_t gelu_bf16x2(uint32_t hv, uint32_t tab_base,
+                                                const uint16_t* tab) {
+  const uint32_t d = (hv & 0x7FFF7FFFu) - ((kGeluTabLo << 16) | kGeluTabLo);
+  const uint32_t c = min_u16x2(d, ((kGeluTabSpan - 1) << 16) | (kGeluTabSpan - 1));
+  // byte offsets of both entries: 2 * ((sign << 11) | offset) per half
+  const uint32_t off2 = (c << 1) | ((hv >> 3) & 0x10001000u);
+  const uint32_t r_lo = lds_u16(tab_base + (off2 & 0xFFFFu));
+  const uint32_t r_hi = lds_u16(tab_base + (off2 >> 16));
+  if (c != d) return gelu_bf16x2_slow(hv, tab);
+  return __byte_perm(r_lo, r_hi, 0x5410);
 }
 
 // bf16x2 add, one rounding of the exact sum.  For two bf16 operands this equals
@@ -206,7 +237,8 @@ struct TileSeq {
 template <int kEpi, bool kResident>
 __global__ void __launch_bounds__(kNumThreads, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                      const __grid_constant__ CUtensorMap tmap_b, const uint8_t* __restrict__ a_sf,
+                      const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_out, const uint8_t* __restrict__ a_sf,
                       const uint8_t* __restrict__ w_sf, const float* __restrict__ g_a,
                       const float* __restrict__ g_w, const float* __restrict__ alpha_in,
                       const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m, int n,
@@ -406,9 +438,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       gelu_table_init(gelu_tab, threadIdx.x - 64, kEpiThreads);
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
     }
+    const uint32_t tab_base = smem_u32(gelu_tab);
+    uint8_t* warp_staging = staging + (warp - 2) * kWarpStagingBytes;
     // alpha = 1 / (g_a * g_w): torch's reciprocal of the product, IEEE rounded
     const float alpha = alpha_in != nullptr ? *alpha_in : __frcp_rn(__fmul_rn(*g_a, *g_w));
-    uint32_t amax2 = 0;  // max |h| as a bf16 bit pattern
+    uint32_t amax2 = 0;  // max |h| of the low and high columns, bf16 magnitude bits
     for (int i = 0; i < seq.count; ++i) {
       if (!mbar_wait_bounded(&bars->acc_full, static_cast<uint32_t>(i) & 1u, wait_limit)) {
         flag_error(bars, kErrWaitEpilogue);
@@ -434,49 +468,38 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       const int col0 = nb * BN + col_base;
       if constexpr (P::kStaged) {
-        // stage row `trow` (64 bf16 = 8 chunks of 16 B), chunk index XOR-swizzled by row
+        // GEMM1: bias, GELU and the amax on this thread's row, then the warp's
+        // 32 x 64 block goes out in one tensor store from 128B-swizzled staging
+        // (chunk c of row r at r*128 + ((c ^ (r & 7)) * 16), the tensor map's
+        // swizzle), which clips rows past m.
+        if (lane == 0) bulk_wait_group_read0();  // previous store has read the staging
+        __syncwarp();
+        const uint4* bias4 = reinterpret_cast<const uint4*>(bias + col0);
+        uint32_t tile_max = 0;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const int phys = quarter * 8 + (q ^ (trow & 7));
-          *reinterpret_cast<uint4*>(staging + trow * (BN * 2) + phys * 16) =
-              make_uint4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
-        }
-        __syncwarp();
-        // phase 2: lane handles columns col0 + 2*lane, +1 of each of the warp's 32 rows
-        const uint32_t bias2 =
-            bias != nullptr ? __ldg(reinterpret_cast<const uint32_t*>(bias + col0) + lane) : 0u;
-        // chunk offsets of this lane's word in each row class (row & 7)
-        const int lchunk = lane >> 2;
-        uint32_t xoff[8];
+          uint4 bv = make_uint4(0, 0, 0, 0);
+          if (bias != nullptr) bv = __ldg(bias4 + q);
+          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+          uint32_t o[4];
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          xoff[c] = static_cast<uint32_t>((quarter * 8 + (lchunk ^ c)) * 16 + (lane & 3) * 4);
-        const uint8_t* srow = staging + quad * 32 * (BN * 2);
-        uint16_t* orow = out + static_cast<int64_t>(mb * BM + quad * 32) * n + col0 + 2 * lane;
-        const int rows_here = min(32, m - (mb * BM + quad * 32));
-        auto row_word = [&](int rr, uint32_t xo) -> uint32_t {
-          uint32_t hv = *reinterpret_cast<const uint32_t*>(srow + rr * (BN * 2) + xo);
-          if (bias != nullptr) hv = add_bf16x2(hv, bias2);
-          if (kEpi == 1) hv = gelu_bf16x2(hv, gelu_tab);
-          return hv;
-        };
-        if (rows_here >= 32) {
-#pragma unroll 8
-          for (int rr = 0; rr < 32; ++rr) {
-            const uint32_t hv = row_word(rr, xoff[rr & 7]);
-            if (kEpi == 1) amax2 = max(amax2, max(hv & 0x7FFFu, (hv >> 16) & 0x7FFFu));
-            *reinterpret_cast<uint32_t*>(orow + static_cast<int64_t>(rr) * n) = hv;
+          for (int j = 0; j < 4; ++j) {
+            uint32_t hv = y[4 * q + j];
+            if (bias != nullptr) hv = add_bf16x2(hv, bw[j]);
+            hv = gelu_bf16x2(hv, tab_base, gelu_tab);
+            tile_max = max_u16x2(tile_max, hv & 0x7FFF7FFFu);
+            o[j] = hv;
           }
-        } else {
-          for (int rr = 0; rr < rows_here; ++rr) {
-            const uint32_t xo =
-                static_cast<uint32_t>((quarter * 8 + (lchunk ^ (rr & 7))) * 16 + (lane & 3) * 4);
-            const uint32_t hv = row_word(rr, xo);
-            if (kEpi == 1) amax2 = max(amax2, max(hv & 0x7FFFu, (hv >> 16) & 0x7FFFu));
-            *reinterpret_cast<uint32_t*>(orow + static_cast<int64_t>(rr) * n) = hv;
-          }
+          *reinterpret_cast<uint4*>(warp_staging + lane * kStageRowBytes + ((q ^ (lane & 7)) * 16)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
         }
+        if (mb * BM + trow < m) amax2 = max_u16x2(amax2, tile_max);
+        fence_proxy_async_smem();
         __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_out, warp_staging, col0, mb * BM + quad * 32);
+          bulk_commit_group();
+        }
       } else {
         const int row = mb * BM + trow;
         uint16_t* dst = out + static_cast<int64_t>(row) * n + col0;
@@ -490,10 +513,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           for (int j = 0; j < 4; ++j) {
             uint32_t w = y[c / 2 + j];
             if (bias != nullptr) w = add_bf16x2(w, bw[j]);
-            if (kEpi == 1) {
-              w = gelu_bf16_exact(w & 0xFFFFu) | (gelu_bf16_exact(w >> 16) << 16);
-              if (row < m) amax2 = max(amax2, max(w & 0x7FFFu, (w >> 16) & 0x7FFFu));
-            }
             o[j] = w;
           }
           if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -501,7 +520,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
     if (kEpi == 1) {
-      const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, amax2 << 16);
+      // the tensor stores must be complete before the CTA exits
+      if (lane == 0) bulk_wait_group0();
+      const uint32_t mag = max(amax2 & 0xFFFFu, amax2 >> 16);
+      const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, mag << 16);
       if (lane == 0 && bits != 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), bits);
     }
   }
@@ -512,15 +534,25 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-// GELU of bf16 values through the epilogue's table-plus-exact path (test support).
+// GELU of bf16 values through the epilogue's path (test support): values
+// 2i and 2i+1 form one bf16x2 word, as in the epilogue; an odd last value
+// goes through the single-value path.
 __global__ void __launch_bounds__(256) gelu_probe_kernel(const uint16_t* in, uint16_t* out,
                                                          int64_t count) {
-  __shared__ uint16_t tab[kGeluTabEntries];
+  __shared__ __align__(16) uint16_t tab[kGeluTabEntries];
   gelu_table_init(tab, threadIdx.x, blockDim.x);
   __syncthreads();
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    out[i] = static_cast<uint16_t>(gelu_bf16(in[i], tab));
+  const uint32_t tab_base = smem_u32(tab);
+  const int64_t pairs = count / 2;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < pairs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t w = static_cast<uint32_t>(in[2 * i]) | (static_cast<uint32_t>(in[2 * i + 1]) << 16);
+    const uint32_t g = gelu_bf16x2(w, tab_base, tab);
+    out[2 * i] = static_cast<uint16_t>(g & 0xFFFFu);
+    out[2 * i + 1] = static_cast<uint16_t>(g >> 16);
+  }
+  if ((count & 1) && blockIdx.x == 0 && threadIdx.x == 0)
+    out[count - 1] = static_cast<uint16_t>(gelu_bf16(in[count - 1], tab));
 }
 
 // ---------------------------------------------------------------- host side
@@ -559,8 +591,23 @@ bool make_code_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t 
   return r == CUDA_SUCCESS;
 }
 
+// 2-D map over a bf16 output [rows, n], box = 32 rows x 64 columns (128 B), 128B swizzle.
+bool make_out_map(CUtensorMap* map, const uint16_t* base, int64_t rows, int64_t n) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(n * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kStageRowBytes / 2), 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int kEpi, bool kResident>
-cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const uint8_t* a_sf,
+cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
+                          const uint8_t* a_sf,
                           const uint8_t* w_sf, const float* g_a, const float* g_w,
                           const float* alpha, const uint16_t* bias, uint16_t* out, int m, int n,
                           int k, float* amax_out, uint64_t wait_limit, cudaStream_t st) {
@@ -578,7 +625,7 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const ui
   int grid = sm_count();
   if (grid > tiles) grid = tiles;
   nvfp4_gemm_kernel<kEpi, kResident><<<grid, kNumThreads, kSmemBytes, st>>>(
-      ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit);
+      ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit);
   return cudaGetLastError();
 }
 
@@ -595,17 +642,23 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
     if (why) *why = "cuTensorMapEncodeTiled failed for the code matrices";
     return cudaErrorInvalidValue;
   }
+  alignas(64) CUtensorMap mo;
+  std::memset(&mo, 0, sizeof(mo));
+  if (epilogue == 1 && !make_out_map(&mo, out, m, n)) {
+    if (why) *why = "cuTensorMapEncodeTiled failed for the output";
+    return cudaErrorInvalidValue;
+  }
   const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
   if (epilogue == 1) {
     // W scales stay in TMEM when they fit and every N block gets a CTA
     const bool resident = (k / 64) <= kMaxResidentKSteps && (n / BN) <= sm_count();
     if (resident)
-      return launch_gemm_t<1, true>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
+      return launch_gemm_t<1, true>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
                                     amax_out, wait_limit, st);
-    return launch_gemm_t<1, false>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
+    return launch_gemm_t<1, false>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
                                    amax_out, wait_limit, st);
   }
-  return launch_gemm_t<0, false>(ma, mb, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
+  return launch_gemm_t<0, false>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
                                  amax_out, wait_limit, st);
 }
 

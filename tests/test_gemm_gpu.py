@@ -143,11 +143,19 @@ def test_mm_fp4_device_alpha_equals_gscales():
     assert torch.equal(y1, y2)
 
 
-def test_epilogue_gelu_matches_torch_on_every_bf16_input():
+@pytest.mark.parametrize("order", ["sorted", "shuffled", "shuffled_odd"])
+def test_epilogue_gelu_matches_torch_on_every_bf16_input(order):
     """The GELU epilogue (shared-memory table plus exact formula) equals torch's
-    GELU(approximate='tanh') on all 65536 bf16 inputs, NaNs compared as NaN."""
+    GELU(approximate='tanh') on all 65536 bf16 inputs, NaNs compared as NaN.
+    The probe pairs values 2i, 2i+1 into one bf16x2 word as the epilogue does;
+    the shuffled orders pair table-range values with out-of-range ones."""
     from flashvsr_optimizations_b200 import _lib
-    bits = torch.arange(0, 1 << 16, dtype=torch.int32).to(torch.int16).cuda()
+    bits = torch.arange(0, 1 << 16, dtype=torch.int32)
+    if order != "sorted":
+        bits = bits[torch.randperm(bits.numel(), generator=torch.Generator().manual_seed(7))]
+    if order == "shuffled_odd":
+        bits = bits[:-1]
+    bits = bits.to(torch.int16).cuda()
     x = bits.view(torch.bfloat16)
     out = torch.empty_like(bits)
     _lib.call("fvq_gelu_bf16_probe", bits.data_ptr(), out.data_ptr(), bits.numel(),
