@@ -48,6 +48,8 @@ FLOP_PER_TOKEN = 2 * D_MODEL * D_FF * 2
 ROTATE = 8
 METRIC = "nvfp4_ffn_tokens_per_s"
 WORKLOAD = "ffn_layer_d1536_ff8960_gelu_tanh_bias_7680tok_per_gpu"
+# fvq_nvfp4_ffn launches per layer: amax+quantize(x), GEMM1 (+bias, GELU, amax), quantize(h), GEMM2
+LAUNCHES_PER_LAYER = 4
 
 
 def parse():
@@ -344,7 +346,7 @@ def main():
                    "layers": 1, "parallelism": f"token-row shards x{world}, replicated weights",
                    "l2": f"inputs rotate over {ROTATE} distinct activation/weight sets (312 MB > 126 MB L2)"},
         "tflops": tflops, "tflops_frac_of_fp4_peak": tflops / peak,
-        "gpu_launches": 5 * args.steps,
+        "gpu_launches": LAUNCHES_PER_LAYER * args.steps,
         "roofline": {"bound": "tensor", "kernel": "nvfp4_gemm_kernel (GEMM1 + GEMM2 of the layer)",
                      "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": traffic,
@@ -370,7 +372,7 @@ def main():
 
 
 def kernel_timing(torch, lib, _lib, sets, tokens, dev, stream, steps) -> dict:
-    """Per-kernel CUDA-event timing of the layer's five launches (GEMMs and H-quantize)."""
+    """Per-kernel CUDA-event timing of the layer's six launches, as fvq_nvfp4_ffn issues them."""
     import ctypes as C
     d, f = D_MODEL, D_FF
     st = stream.cuda_stream
@@ -382,6 +384,7 @@ def kernel_timing(torch, lib, _lib, sets, tokens, dev, stream, steps) -> dict:
     y = torch.empty(tokens, d, dtype=torch.bfloat16, device=dev)
     scal = torch.zeros(64, dtype=torch.float32, device=dev)
     amax_ws = torch.zeros(lib.fvq_amax_workspace_bytes(), dtype=torch.uint8, device=dev)
+    w2_rep = torch.empty(lib.fvq_w_scales_replicated_bytes(d, f), dtype=torch.uint8, device=dev)
     gx, gh, amax_h = scal[0:1], scal[1:2], scal[2:3]
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
 
@@ -391,12 +394,13 @@ def kernel_timing(torch, lib, _lib, sets, tokens, dev, stream, steps) -> dict:
 
     def one(i, e):
         x, ((q1, s1, g1, b1), (q2, s2, g2, b2)) = sets[i % ROTATE]
-        if e: e[0].record(stream)
-        chk(lib.fvq_amax(x.data_ptr(), x.numel(), None, gx.data_ptr(), amax_ws.data_ptr(),
-                         amax_ws.numel(), st))
-        chk(lib.fvq_nvfp4_quantize(x.data_ptr(), tokens, d, gx.data_ptr(), codes_x.data_ptr(),
-                                   sf_x.data_ptr(), st))
         amax_h.zero_()
+        if e: e[0].record(stream)
+        # amax + global scale + quantize in one launch (fvq_nvfp4_ffn's first kernel also
+        # writes the 3.4 MB of replicated W2 scales)
+        chk(lib.fvq_nvfp4_quantize_dynamic(x.data_ptr(), tokens, d, None, gx.data_ptr(),
+                                           codes_x.data_ptr(), sf_x.data_ptr(), amax_ws.data_ptr(),
+                                           amax_ws.numel(), st))
         if e: e[1].record(stream)
         chk(lib.fvq_nvfp4_gemm(codes_x.data_ptr(), sf_x.data_ptr(), gx.data_ptr(), q1.data_ptr(),
                                s1.data_ptr(), g1.data_ptr(), b1.data_ptr(), h.data_ptr(), tokens, f, d,
@@ -405,10 +409,14 @@ def kernel_timing(torch, lib, _lib, sets, tokens, dev, stream, steps) -> dict:
         chk(lib.fvq_nvfp4_quantize_dynamic(h.data_ptr(), tokens, f, amax_h.data_ptr(), gh.data_ptr(),
                                            codes_h.data_ptr(), sf_h.data_ptr(), None, 0, st))
         if e: e[3].record(stream)
-        chk(lib.fvq_nvfp4_gemm(codes_h.data_ptr(), sf_h.data_ptr(), gh.data_ptr(), q2.data_ptr(),
-                               s2.data_ptr(), g2.data_ptr(), b2.data_ptr(), y.data_ptr(), tokens, d, f,
-                               0, None, st))
+        # the standalone replication kernel, timed for reference (fvq_nvfp4_ffn folds it
+        # into its first kernel), then GEMM2 on the replicated W2 scales
+        chk(lib.fvq_replicate_w_scales(s2.data_ptr(), d, f, w2_rep.data_ptr(), st))
         if e: e[4].record(stream)
+        chk(lib.fvq_nvfp4_gemm_wrep(codes_h.data_ptr(), sf_h.data_ptr(), gh.data_ptr(), q2.data_ptr(),
+                                    w2_rep.data_ptr(), g2.data_ptr(), b2.data_ptr(), y.data_ptr(),
+                                    tokens, d, f, st))
+        if e: e[5].record(stream)
 
     for i in range(5):
         one(i, None)
@@ -419,10 +427,12 @@ def kernel_timing(torch, lib, _lib, sets, tokens, dev, stream, steps) -> dict:
     qx = [e[0].elapsed_time(e[1]) for e in ev]
     g1t = [e[1].elapsed_time(e[2]) for e in ev]
     qh = [e[2].elapsed_time(e[3]) for e in ev]
-    g2t = [e[3].elapsed_time(e[4]) for e in ev]
+    rep = [e[3].elapsed_time(e[4]) for e in ev]
+    g2t = [e[4].elapsed_time(e[5]) for e in ev]
     mean = lambda v: sum(v) / len(v)  # noqa: E731
     qh_bytes = tokens * f * 2 + tokens * f // 2 + (tokens + 127) // 128 * 128 * f // 16
-    return {"quant_x_ms": mean(qx), "gemm1_ms": mean(g1t), "quant_h_ms": mean(qh), "gemm2_ms": mean(g2t),
+    return {"quant_x_ms": mean(qx), "gemm1_ms": mean(g1t), "quant_h_ms": mean(qh),
+            "w2_scale_replicate_standalone_ms": mean(rep), "gemm2_ms": mean(g2t),
             "gemm_ms": mean(g1t) + mean(g2t), "quant_h_gbs": qh_bytes / (mean(qh) * 1e-3) / 1e9,
             "gemm1_tflops": tokens * 2 * d * f / (mean(g1t) * 1e-3) / 1e12,
             "gemm2_tflops": tokens * 2 * d * f / (mean(g2t) * 1e-3) / 1e12, "steps": steps}

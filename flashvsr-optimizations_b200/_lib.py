@@ -54,6 +54,10 @@ SIGNATURES = {
     "fvq_nvfp4_gemm": (_c.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
                                   _c.c_int, _vp, _vp]),
     "fvq_nvfp4_mm": (_c.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "fvq_w_scales_replicated_bytes": (_sz, [_i64, _i64]),
+    "fvq_replicate_w_scales": (_c.c_int, [_vp, _i64, _i64, _vp, _vp]),
+    "fvq_nvfp4_gemm_wrep": (_c.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                       _vp]),
     "fvq_nvfp4_linear_workspace_bytes": (_sz, [_i64, _i64]),
     "fvq_nvfp4_linear": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _vp, _vp, _sz, _vp]),
     "fvq_nvfp4_linear_noalloc": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _vp, _vp]),

@@ -98,10 +98,10 @@ int check_gemm_shape(int64_t m, int64_t n, int64_t k) {
 int gemm_impl(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
               const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w, const float* alpha,
               const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k, int epilogue,
-              float* amax_out, cudaStream_t st) {
+              float* amax_out, cudaStream_t st, const uint8_t* w_sf_rep = nullptr) {
   const char* why = nullptr;
   cudaError_t e = fvq::launch_gemm(a_codes, a_sf, g_a, w_codes, w_sf, g_w, alpha, bias, out, m, n, k,
-                                   epilogue, amax_out, g_wait_limit, st, &why);
+                                   epilogue, amax_out, g_wait_limit, st, &why, w_sf_rep);
   if (e != cudaSuccess) {
     if (why) return fail(FVQ_ECUDA, "fvq_nvfp4_gemm: %s", why);
     return cuda_fail(e, "fvq_nvfp4_gemm launch");
@@ -178,10 +178,12 @@ int fvq_nvfp4_quantize_dynamic(const uint16_t* x, int64_t rows, int64_t k, const
                   fvq_amax_workspace_bytes());
     if (!aligned16(workspace))
       return fail(FVQ_EALIGN, "fvq_nvfp4_quantize_dynamic: workspace must be 16-byte aligned");
+    // amax, global scale and quantization in one launch
     uint32_t* ws = static_cast<uint32_t*>(workspace);
-    cudaError_t e = fvq::launch_amax(x, rows * k, nullptr, nullptr, ws, nullptr, st);
-    if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_quantize_dynamic amax launch");
-    amax = reinterpret_cast<const float*>(ws + 2);
+    cudaError_t e = fvq::launch_amax_quantize(x, rows, k, g_out, codes, sf, ws, nullptr, nullptr, 0,
+                                              0, nullptr, g_wait_limit, fvq::error_word_ptr(), st);
+    if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_quantize_dynamic launch");
+    return FVQ_OK;
   }
   cudaError_t e = fvq::launch_quantize(x, rows, k, nullptr, amax, g_out, codes, sf, nullptr, st);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_quantize_dynamic launch");
@@ -205,6 +207,42 @@ int fvq_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a
   if (int rc = check_device()) return rc;
   return gemm_impl(a_codes, a_sf, g_a, w_codes, w_sf, g_w, nullptr, bias, out, m, n, k, epilogue,
                    amax_out, static_cast<cudaStream_t>(stream));
+}
+
+size_t fvq_w_scales_replicated_bytes(int64_t n, int64_t k) {
+  if (n <= 0 || k <= 0) return 0;
+  return static_cast<size_t>(4 * n * (k / 16));
+}
+
+int fvq_replicate_w_scales(const uint8_t* w_sf, int64_t n, int64_t k, uint8_t* w_sf_rep,
+                           void* stream) {
+  if (n <= 0 || n % 256 != 0 || k <= 0 || k % 256 != 0)
+    return fail(FVQ_EINVAL, "fvq_replicate_w_scales: n and k must be positive multiples of 256 "
+                "(got %lld, %lld)", (long long)n, (long long)k);
+  if (!w_sf || !w_sf_rep) return fail(FVQ_EINVAL, "fvq_replicate_w_scales: NULL pointer");
+  if (!aligned16(w_sf) || !aligned16(w_sf_rep))
+    return fail(FVQ_EALIGN, "fvq_replicate_w_scales: pointers must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  cudaError_t e = fvq::launch_replicate_w_scales(w_sf, n, k, w_sf_rep,
+                                                 static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_replicate_w_scales launch");
+  return FVQ_OK;
+}
+
+int fvq_nvfp4_gemm_wrep(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
+                        const uint8_t* w_codes, const uint8_t* w_sf_rep, const float* g_w,
+                        const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
+                        void* stream) {
+  if (int rc = check_gemm_shape(m, n, k)) return rc;
+  if (!a_codes || !a_sf || !g_a || !w_codes || !w_sf_rep || !g_w || !out)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_gemm_wrep: NULL pointer");
+  if (!aligned16(a_codes) || !aligned16(a_sf) || !aligned16(w_codes) || !aligned16(w_sf_rep) ||
+      !aligned16(out) || !aligned16(bias))
+    return fail(FVQ_EALIGN,
+                "fvq_nvfp4_gemm_wrep: operands, scales, bias and out must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  return gemm_impl(a_codes, a_sf, g_a, w_codes, nullptr, g_w, nullptr, bias, out, m, n, k,
+                   FVQ_EPI_BF16, nullptr, static_cast<cudaStream_t>(stream), w_sf_rep);
 }
 
 int fvq_nvfp4_mm(const uint8_t* a_codes, const uint8_t* a_sf, const uint8_t* w_codes,
@@ -263,9 +301,9 @@ int fvq_nvfp4_linear(const uint16_t* x, int64_t rows, const fvq_linear* lin, uin
   float* scalars = reinterpret_cast<float*>(c.take(kScalarBytes));
   uint8_t* codes = c.take(static_cast<size_t>(rows * k / 2));
   uint8_t* sf = c.take(fvq::sf_bytes(rows, k));
-  cudaError_t e = fvq::launch_amax(x, rows * k, nullptr, &scalars[0], amax_ws, nullptr, st);
-  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_linear amax launch");
-  e = fvq::launch_quantize(x, rows, k, &scalars[0], nullptr, nullptr, codes, sf, nullptr, st);
+  cudaError_t e = fvq::launch_amax_quantize(x, rows, k, &scalars[0], codes, sf, amax_ws, nullptr,
+                                            nullptr, 0, 0, nullptr, g_wait_limit,
+                                            fvq::error_word_ptr(), st);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_linear quantize launch");
   return gemm_impl(codes, sf, &scalars[0], lin->qweight, lin->scale, lin->global_sf, nullptr,
                    lin->bias, y,
@@ -282,6 +320,7 @@ size_t fvq_nvfp4_ffn_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff
   c.take(static_cast<size_t>(rows * d_ff * 2));
   c.take(static_cast<size_t>(rows * d_ff / 2));
   c.take(fvq::sf_bytes(rows, d_ff));
+  c.take(static_cast<size_t>(4 * d_model * (d_ff / 16)));  // W2 scales, replicated
   return c.off;
 }
 
@@ -312,26 +351,28 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
   uint16_t* h = reinterpret_cast<uint16_t*>(c.take(static_cast<size_t>(rows * f * 2)));
   uint8_t* codes_h = c.take(static_cast<size_t>(rows * f / 2));
   uint8_t* sf_h = c.take(fvq::sf_bytes(rows, f));
+  uint8_t* sf_w2_rep = c.take(static_cast<size_t>(4 * d * (f / 16)));
   float* g_x = &scalars[0];
   float* g_h = &scalars[1];
   float* amax_h = &scalars[2];
-  // 1. amax(x) -> g_x; also zeroes amax_h before GEMM1 accumulates into it
-  cudaError_t e = fvq::launch_amax(x, rows * d, nullptr, g_x, amax_ws, amax_h, st);
-  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn amax launch");
-  // 2. x -> NVFP4
-  e = fvq::launch_quantize(x, rows, d, g_x, nullptr, nullptr, codes_x, sf_x, nullptr, st);
+  // 1. amax(x) -> g_x -> x in NVFP4, one launch; it also zeroes amax_h before GEMM1
+  //    accumulates into it and writes the W2 scales in the layout of GEMM2's
+  //    128x256b scale copies
+  cudaError_t e = fvq::launch_amax_quantize(x, rows, d, g_x, codes_x, sf_x, amax_ws, amax_h,
+                                            lin2->scale, d, f, sf_w2_rep, g_wait_limit,
+                                            fvq::error_word_ptr(), st);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(x) launch");
-  // 3. h = bf16(gelu(bf16(bf16(alpha1 * acc) + b1))), amax_h = max |h|
+  // 2. h = bf16(gelu(bf16(bf16(alpha1 * acc) + b1))), amax_h = max |h|
   if (int rc = gemm_impl(codes_x, sf_x, g_x, lin1->qweight, lin1->scale, lin1->global_sf, nullptr,
                          lin1->bias, h, rows, f, d, FVQ_EPI_GELU_AMAX, amax_h, st))
     return rc;
-  // 4. h -> NVFP4 with g_h = 2688 / max(amax_h, 1e-12)
-  e = fvq::launch_quantize(h, rows, f, nullptr, amax_h, g_h, codes_h, sf_h, nullptr, st);
+  // 3. h -> NVFP4 with g_h = 2688 / max(amax_h, 1e-12)
+  e = fvq::launch_quantize(h, rows, f, nullptr, amax_h, g_h, codes_h, sf_h, nullptr, st,
+                           /*scratch_input=*/true);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(h) launch");
-  // 5. y = bf16(bf16(alpha2 * acc) + b2)
+  // 4. y = bf16(bf16(alpha2 * acc) + b2)
   return gemm_impl(codes_h, sf_h, g_h, lin2->qweight, lin2->scale, lin2->global_sf, nullptr,
-                   lin2->bias, y,
-                   rows, d, f, FVQ_EPI_BF16, nullptr, st);
+                   lin2->bias, y, rows, d, f, FVQ_EPI_BF16, nullptr, st, sf_w2_rep);
 }
 
 int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream) {

@@ -43,6 +43,7 @@ constexpr int kABytes = BM * BKB;                // 16 KB
 constexpr int kBBytes = BN * BKB;                // 32 KB
 constexpr int kSfaBytes = BM * (BK / 16);        // 2 KB
 constexpr int kSfbBytes = BN * (BK / 16);        // 4 KB
+constexpr int kSfbRepBytes = 4 * kSfbBytes;      // 16 KB: W scales replicated for 128x256b copies
 constexpr int kEpiWarps = 16;                    // 4 per TMEM lane quadrant, 64 columns each
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kNumThreads = 64 + kEpiThreads;
@@ -68,10 +69,14 @@ constexpr int kWarpStagingBytes = 32 * kStageRowBytes;
 
 // Shared-memory plan.  kResident: the W scales of the CTA's single N block
 // are loaded into TMEM once (K <= 1920), so stages carry only A, W and A scales.
-template <int kEpi, bool kResident>
+// kRepSfb: stages carry the W scales already replicated four times (16 KB per
+// K tile), moved to TMEM with four 128x256b copies instead of eight
+// 32x128b.warpx4 copies.
+template <int kEpi, bool kResident, bool kRepSfb = false>
 struct Plan {
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + (kResident ? 0 : kSfbBytes);
-  static constexpr int kStages = kEpi == 0 ? 4 : (kResident ? 3 : 2);
+  static constexpr int kStageBytes =
+      kABytes + kBBytes + kSfaBytes + (kResident ? 0 : (kRepSfb ? kSfbRepBytes : kSfbBytes));
+  static constexpr int kStages = kEpi == 0 ? (kRepSfb ? 3 : 4) : (kResident ? 3 : 2);
   static constexpr bool kStaged = kEpi == 1;
   static constexpr int kStagingOff = kStages * kStageBytes;
   static constexpr int kTableOff = kStagingOff + (kStaged ? kStagingBytes : 0);
@@ -81,6 +86,7 @@ struct Plan {
 static_assert(Plan<1, true>::kSmemBytes <= 232448, "GEMM1 resident plan exceeds shared memory");
 static_assert(Plan<1, false>::kSmemBytes <= 232448, "GEMM1 streaming plan exceeds shared memory");
 static_assert(Plan<0, false>::kSmemBytes <= 232448, "GEMM2 plan exceeds shared memory");
+static_assert(Plan<0, false, true>::kSmemBytes <= 232448, "GEMM2 replicated plan exceeds shared memory");
 
 // Instruction descriptor, kind::mxf4nvf4: A/B E2M1 (1), UE4M3 scales (0),
 // K-major A and B, N = 256 (>>3 at bit 17), M = 128 (>>4 at bit 24).
@@ -234,7 +240,7 @@ struct TileSeq {
   }
 };
 
-template <int kEpi, bool kResident>
+template <int kEpi, bool kResident, bool kRepSfb>
 __global__ void __launch_bounds__(kNumThreads, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -243,7 +249,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                       const float* __restrict__ g_w, const float* __restrict__ alpha_in,
                       const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m, int n,
                       int k, float* amax_out, uint64_t wait_limit) {
-  using P = Plan<kEpi, kResident>;
+  using P = Plan<kEpi, kResident, kRepSfb>;
   constexpr int kStages = P::kStages;
   constexpr int kStageBytes = P::kStageBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -322,7 +328,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           tma_load_2d(sa, &tmap_a, &bars->full[stage], kt * BKB, mb * BM);
           tma_load_2d(sb, &tmap_b, &bars->full[stage], kt * BKB, nb * BN);
           bulk_load(ssfa, a_sf + mb * sf_tile_stride + kt * 2048, kSfaBytes, &bars->full[stage]);
-          if (!kResident) {
+          if (kRepSfb) {
+            // replicated layout: K tile kt of N block nb is 16 KB contiguous
+            bulk_load(ssfa + kSfaBytes,
+                      w_sf + (static_cast<int64_t>(nb) * (k / 64) + kt * 4) * (2 * 2048),
+                      kSfbRepBytes, &bars->full[stage]);
+          } else if (!kResident) {
             uint8_t* ssfb = ssfa + kSfaBytes;
             bulk_load(ssfb, w_sf + (2 * nb) * sf_tile_stride + kt * 2048, 2048, &bars->full[stage]);
             bulk_load(ssfb + 2048, w_sf + (2 * nb + 1) * sf_tile_stride + kt * 2048, 2048,
@@ -392,7 +403,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           for (int j = 0; j < 4; ++j) {
             tmem_cp_32x128b_x4(tmem + kSfaCol + 4 * j,
                                make_smem_desc(smem_u32(ssfa + 512 * j), 16, 128, 0));
-            if (!kResident) {
+            if (kRepSfb) {
+              // row i of the 4 KB source: line i % 32 of the rows 0-127 atom
+              // (first 2 KB) and of the rows 128-255 atom (LBO = 2 KB later)
+              tmem_cp_128x256b(tmem + kSfbCol + 8 * j,
+                               make_smem_desc(smem_u32(ssfa + kSfaBytes + 4096 * j), 2048, 128, 0));
+            } else if (!kResident) {
               uint8_t* ssfb = ssfa + kSfaBytes;
               tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j,
                                  make_smem_desc(smem_u32(ssfb + 512 * j), 16, 128, 0));
@@ -605,18 +621,18 @@ bool make_out_map(CUtensorMap* map, const uint16_t* base, int64_t rows, int64_t 
   return r == CUDA_SUCCESS;
 }
 
-template <int kEpi, bool kResident>
+template <int kEpi, bool kResident, bool kRepSfb = false>
 cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
                           const uint8_t* a_sf,
                           const uint8_t* w_sf, const float* g_a, const float* g_w,
                           const float* alpha, const uint16_t* bias, uint16_t* out, int m, int n,
                           int k, float* amax_out, uint64_t wait_limit, cudaStream_t st) {
   static bool attr_set[64] = {false};
-  constexpr int kSmemBytes = Plan<kEpi, kResident>::kSmemBytes;
+  constexpr int kSmemBytes = Plan<kEpi, kResident, kRepSfb>::kSmemBytes;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_kernel<kEpi, kResident>,
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_kernel<kEpi, kResident, kRepSfb>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
@@ -624,7 +640,7 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CU
   const int tiles = ((m + BM - 1) / BM) * (n / BN);
   int grid = sm_count();
   if (grid > tiles) grid = tiles;
-  nvfp4_gemm_kernel<kEpi, kResident><<<grid, kNumThreads, kSmemBytes, st>>>(
+  nvfp4_gemm_kernel<kEpi, kResident, kRepSfb><<<grid, kNumThreads, kSmemBytes, st>>>(
       ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit);
   return cudaGetLastError();
 }
@@ -635,7 +651,7 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
                         const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
                         int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
-                        const char** why) {
+                        const char** why, const uint8_t* w_sf_rep) {
   alignas(64) CUtensorMap ma;
   alignas(64) CUtensorMap mb;
   if (!make_code_map(&ma, a_codes, m, k, BM) || !make_code_map(&mb, w_codes, n, k, BN)) {
@@ -658,6 +674,9 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
     return launch_gemm_t<1, false>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
                                    amax_out, wait_limit, st);
   }
+  if (w_sf_rep != nullptr)
+    return launch_gemm_t<0, false, true>(ma, mb, mo, a_sf, w_sf_rep, g_a, g_w, alpha, bias, out, mi,
+                                         ni, ki, amax_out, wait_limit, st);
   return launch_gemm_t<0, false>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
                                  amax_out, wait_limit, st);
 }
@@ -668,6 +687,21 @@ cudaError_t launch_gelu_probe(const uint16_t* in, uint16_t* out, int64_t count, 
   if (blocks > 1024) blocks = 1024;
   gelu_probe_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(in, out, count);
   return cudaGetLastError();
+}
+
+uint32_t* error_word_ptr() {
+  static uint32_t* cached[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess)
+      cached[dev] = static_cast<uint32_t*>(p);
+  }
+  return cached[dev];
 }
 
 cudaError_t set_error_word(uint32_t v, cudaStream_t st) {

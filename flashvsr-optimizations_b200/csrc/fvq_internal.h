@@ -13,6 +13,7 @@ constexpr uint32_t kErrWaitMma = 1u << 1;       // MMA warp gave up on a full st
 constexpr uint32_t kErrWaitEpilogue = 1u << 2;  // epilogue gave up on the accumulator
 constexpr uint32_t kErrWaitTeardown = 1u << 3;  // teardown gave up on in-flight work
 constexpr uint32_t kErrSmemAlign = 1u << 4;     // dynamic shared memory not 1024-byte aligned
+constexpr uint32_t kErrWaitGrid = 1u << 5;      // fused quantizer gave up at its grid barrier
 
 // Bound on any single pipeline wait inside a kernel (wall time, ns).
 constexpr uint64_t kDefaultWaitLimit = 2000000000ull;
@@ -34,19 +35,34 @@ int report_error(int code, const char* fmt, ...) __attribute__((format(printf, 2
 // Kernels (fvq_quant.cu)
 cudaError_t launch_amax(const uint16_t* x, int64_t numel, float* amax_out, float* g_out,
                         uint32_t* ws, float* zero_word, cudaStream_t st);
+// scratch_input: x is a scratch buffer nothing reads afterwards; it is walked from its
+// end and its 128-byte lines are dropped from L2 after reading (no write-back).
 cudaError_t launch_quantize(const uint16_t* x, int64_t rows, int64_t k, const float* g,
                             const float* amax, float* g_out, uint8_t* codes, uint8_t* sf,
-                            float* zero_word, cudaStream_t st);
+                            float* zero_word, cudaStream_t st, bool scratch_input = false);
 cudaError_t launch_rcp_probe(const float* in, float* out, int64_t n, cudaStream_t st);
+// amax + global scale + quantize of x in one cooperative launch; with rep_dst != NULL it
+// also writes the replicated W scales of an [rep_n, rep_k] weight.  ws: the amax workspace
+// (counter ws[0] and generation ws[1] left re-armed), ws[2] receives amax.
+cudaError_t launch_amax_quantize(const uint16_t* x, int64_t rows, int64_t k, float* g_out,
+                                 uint8_t* codes, uint8_t* sf, uint32_t* ws, float* zero_word,
+                                 const uint8_t* rep_src, int64_t rep_n, int64_t rep_k,
+                                 uint8_t* rep_dst, uint64_t wait_limit, uint32_t* err_word,
+                                 cudaStream_t st);
+// W scales (128x4 layout, n % 256 == 0, k % 256 == 0) -> the replicated layout the
+// GEMM's 128x256b scale copies read; 4 * n * k / 16 bytes.
+cudaError_t launch_replicate_w_scales(const uint8_t* sf, int64_t n, int64_t k, uint8_t* rep,
+                                      cudaStream_t st);
 
 // GEMM (fvq_gemm.cu)
 cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
                         const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
                         int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
-                        const char** why);
+                        const char** why, const uint8_t* w_sf_rep = nullptr);
 cudaError_t launch_gelu_probe(const uint16_t* in, uint16_t* out, int64_t count, cudaStream_t st);
 cudaError_t set_error_word(uint32_t v, cudaStream_t st);
+uint32_t* error_word_ptr();   // device address of the error word (current device)
 cudaError_t read_error_word(uint32_t* v, cudaStream_t st);
 
 }  // namespace fvq

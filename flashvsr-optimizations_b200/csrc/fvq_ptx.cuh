@@ -162,6 +162,12 @@ __device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdes
 }
 
 // Arrive on `bar` once all tcgen05 operations issued so far by this thread complete.
+// 128 TMEM lanes x 256 bits: lane i gets row i of the shared-memory source
+// (two 16-byte core-matrix columns, LBO apart), columns [col, col+8).
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(

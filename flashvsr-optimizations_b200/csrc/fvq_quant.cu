@@ -137,34 +137,67 @@ __device__ __forceinline__ void ld_stream_v8(const void* p, uint32_t (&r)[8]) {
 
 constexpr int kQuantUnroll = 2;
 
-__global__ void __launch_bounds__(kThreads) quantize_kernel(
-    const uint16_t* __restrict__ x, int64_t rows, int64_t k, const float* __restrict__ g_ptr,
-    const float* __restrict__ amax_ptr, float* g_out, uint8_t* __restrict__ codes,
-    uint8_t* __restrict__ sf, float* zero_word) {
-  const float g = amax_ptr != nullptr ? encode_scale(*amax_ptr) : *g_ptr;
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    if (g_out != nullptr) *g_out = g;
-    if (zero_word != nullptr) *zero_word = 0.0f;
-  }
+// floor(n / d) for every n < 2^31 as umulhi(n, magic) >> shift, with
+// l = ceil(log2 d), magic = ceil(2^(31 + l) / d) < 2^32 and shift = l - 1:
+// the product overestimates n / d by less than n / 2^(31 + l) < 1 / d, which
+// never reaches the next integer.
+struct Div31 {
+  uint32_t magic, shift;
+};
+
+Div31 make_div31(uint32_t d) {  // d >= 2
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const uint64_t num = 1ull << (31 + l);
+  return Div31{static_cast<uint32_t>((num + d - 1) / d), l - 1};
+}
+
+// bf16x2 word times the block's scale (both halves, one mul.rn.ftz.f32x2),
+// converted to two E2M1 codes.
+__device__ __forceinline__ uint32_t scaled_e2m1x2(uint32_t w, uint64_t os2) {
+  uint64_t xv, pv;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(xv) : "r"(w << 16), "r"(w & 0xFFFF0000u));
+  asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(pv) : "l"(xv), "l"(os2));
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(pv));
+  return f32x2_to_e2m1x2(lo, hi);
+}
+
+__device__ __forceinline__ void discard_l2_line(const void* p) {
+  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+
+// Quantize x with encode scale g.  The work is cut into chunks of 32 blocks
+// (1 KB of x, one per warp step); this warp takes chunks warp_first,
+// warp_first + warp_stride, ...  kReverse walks the chunks from the end of x
+// (the part a producer kernel wrote last, most likely still in L2).
+// kDiscard drops each fully read 128-byte line of x from L2 without a
+// write-back: only for a scratch input that nothing reads afterwards.
+template <bool kReverse, bool kDiscard>
+__device__ __forceinline__ void quantize_blocks(const uint16_t* __restrict__ x, uint32_t rows,
+                                                uint32_t bpr, float g, uint8_t* __restrict__ codes,
+                                                uint8_t* __restrict__ sf, uint32_t warp_first,
+                                                uint32_t warp_stride, Div31 div) {
   const float r6 = rcp_approx_ftz(6.0f);
   const float rg = rcp_approx_ftz(g);
 
-  const int lane = threadIdx.x & 31;
-  const int64_t bpr = k / 16;                      // scale blocks per row
-  const int64_t gpr = k / 64;                      // 64-column groups per row
-  const int64_t n_real = rows * bpr;
-  const int64_t n_all = pad_up_dev(rows) * bpr;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t gpr = bpr / 4;                    // 64-column groups per row
+  const uint32_t n_real = rows * bpr;              // < 2^31 (checked by the host)
+  const uint32_t n_all = ((rows + 127) / 128 * 128) * bpr;
+  const uint32_t n_chunks = (n_all + 31) / 32;
   const uint32_t* xw = reinterpret_cast<const uint32_t*>(x);
 
-  for (int64_t base = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; base - lane < n_all;
-       base += stride * kQuantUnroll) {
+  for (uint32_t c = warp_first; c < n_chunks; c += warp_stride * kQuantUnroll) {
     uint32_t v[kQuantUnroll][8];
+    uint32_t chunk[kQuantUnroll];
 #pragma unroll
     for (int u = 0; u < kQuantUnroll; ++u) {
-      const int64_t b = base + u * stride;
-      if (b < n_real) {
-        ld_stream_v8(xw + b * 8, v[u]);
+      const uint32_t cu = c + u * warp_stride;
+      chunk[u] = kReverse ? n_chunks - 1 - cu : cu;
+      const uint32_t b = chunk[u] * 32 + lane;
+      if (cu < n_chunks && b < n_real) {
+        ld_stream_v8(xw + static_cast<size_t>(b) * 8, v[u]);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[u][j] = 0;
@@ -172,9 +205,8 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(
     }
 #pragma unroll
     for (int u = 0; u < kQuantUnroll; ++u) {
-      const int64_t b = base + u * stride;
-      // warp-uniform exit: the warp's blocks are consecutive
-      if (b - lane >= n_all) break;
+      if (c + u * warp_stride >= n_chunks) break;  // warp-uniform
+      const uint32_t b = chunk[u] * 32 + lane;
       const uint32_t* w = v[u];
       const uint32_t m2 = bmax2(bmax2(bmax2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
                                       bmax2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)),
@@ -186,35 +218,186 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(
       const float sfv = e4m3_to_f32(s8);
       // vmax != 0 under flush-to-zero: a subnormal maximum counts as zero
       const float os = (bm >= 0x0080u) ? rcp_approx_ftz(mul_ftz(sfv, rg)) : 0.0f;
+      uint64_t os2;
+      asm("mov.b64 %0, {%1, %1};" : "=l"(os2) : "f"(os));
       uint32_t byte[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        byte[j] = f32x2_to_e2m1x2(mul_ftz(__uint_as_float(w[j] << 16), os),
-                                  mul_ftz(__uint_as_float(w[j] & 0xFFFF0000u), os));
-      }
+      for (int j = 0; j < 8; ++j) byte[j] = scaled_e2m1x2(w[j], os2);
       const uint32_t c0 = pack4(byte[0], byte[1], byte[2], byte[3]);
       const uint32_t c1 = pack4(byte[4], byte[5], byte[6], byte[7]);
       // gather the group's 4 scale bytes into its first lane (b % 4 == lane % 4)
-      const int lead = lane & ~3;
+      const uint32_t lead = lane & ~3u;
       const uint32_t s1 = __shfl_sync(0xFFFFFFFFu, s8, lead + 1);
       const uint32_t s2 = __shfl_sync(0xFFFFFFFFu, s8, lead + 2);
       const uint32_t s3 = __shfl_sync(0xFFFFFFFFu, s8, lead + 3);
       if (b < n_real) {
-        *reinterpret_cast<uint2*>(codes + b * 8) = make_uint2(c0, c1);
+        *reinterpret_cast<uint2*>(codes + static_cast<size_t>(b) * 8) = make_uint2(c0, c1);
       }
       if ((lane & 3) == 0 && b < n_all) {
-        // block indices stay below 2^31 (checked by the host), so 32-bit division
-        const uint32_t b32 = static_cast<uint32_t>(b);
-        const uint32_t row32 = b32 / static_cast<uint32_t>(bpr);
-        const int64_t row = row32;
-        const int64_t kc = (b32 - row32 * static_cast<uint32_t>(bpr)) >> 2;
+        const uint32_t row = __umulhi(b, div.magic) >> div.shift;
+        const uint32_t kc = (b - row * bpr) >> 2;
         const uint32_t word = (b < n_real) ? (s8 | (s1 << 8) | (s2 << 16) | (s3 << 24)) : 0u;
-        const int64_t off = (row >> 7) * (gpr * 512) + kc * 512 + (row & 31) * 16 +
-                            ((row & 127) >> 5) * 4;
+        const size_t off = static_cast<size_t>(row >> 7) * (gpr * 512) + kc * 512 +
+                           (row & 31) * 16 + ((row & 127) >> 5) * 4;
         *reinterpret_cast<uint32_t*>(sf + off) = word;
+      }
+      if (kDiscard) {
+        __syncwarp();  // every lane has consumed its part of the chunk
+        const uint32_t line_first_block = chunk[u] * 32 + lane * 4;
+        if (lane < 8 && line_first_block + 4 <= n_real)
+          discard_l2_line(xw + static_cast<size_t>(line_first_block) * 8);
       }
     }
   }
+}
+
+template <bool kReverse, bool kDiscard>
+__global__ void __launch_bounds__(kThreads) quantize_kernel(
+    const uint16_t* __restrict__ x, uint32_t rows, uint32_t bpr, const float* __restrict__ g_ptr,
+    const float* __restrict__ amax_ptr, float* g_out, uint8_t* __restrict__ codes,
+    uint8_t* __restrict__ sf, float* zero_word, Div31 div) {
+  const float g = amax_ptr != nullptr ? encode_scale(*amax_ptr) : *g_ptr;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (g_out != nullptr) *g_out = g;
+    if (zero_word != nullptr) *zero_word = 0.0f;
+  }
+  constexpr uint32_t kWarps = kThreads / 32;
+  quantize_blocks<kReverse, kDiscard>(x, rows, bpr, g, codes, sf,
+                                      blockIdx.x * kWarps + (threadIdx.x >> 5), gridDim.x * kWarps,
+                                      div);
+}
+
+// ---------------------------------------------------------------- W scale replication
+// The GEMM's W scales for one 256-row N block and one 64-deep K step are two
+// 512-byte atoms of the 128x4 layout (rows 0-127 and 128-255).  The tensor
+// cores want each atom in all four 32-lane TMEM sub-partitions; a
+// 128-lane x 256-bit tcgen05.cp does that in one instruction when the source
+// row i already holds line i % 32 of both atoms.  This kernel writes that
+// source: for N block nb, K step j, half h and replica r the 512-byte atom
+// (2*nb + h, j) goes to byte ((((nb * k64 + j) * 2 + h) * 4 + r) * 512), so
+// one K tile (four K steps) is 16 KB contiguous.
+__global__ void __launch_bounds__(kThreads) replicate_w_scales_kernel(const uint4* __restrict__ sf,
+                                                                       int64_t k64, int64_t total16,
+                                                                       uint4* __restrict__ rep) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t o = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; o < total16;
+       o += stride) {
+    const int64_t x16 = o & 31;          // 16-byte word within the 512-byte atom
+    const int64_t h = (o >> 7) & 1;      // o >> 5 = replica index bits, >> 7 = half
+    const int64_t jb = o >> 8;           // nb * k64 + j
+    const int64_t nb = jb / k64, j = jb - nb * k64;
+    rep[o] = __ldg(sf + ((2 * nb + h) * k64 + j) * 32 + x16);
+  }
+}
+
+// ---------------------------------------------------------------- fused amax + quantize
+// One cooperative launch for the dynamic quantization of an activation:
+//   pass 1: max |x| over this CTA's grid-stride share, published to ws[16 + cta]
+//           (plus, optionally, a share of the W-scale replication above);
+//   grid barrier: arrival counter ws[0] and generation word ws[1]; the last CTA
+//           to arrive resets the counter and advances the generation, the others
+//           wait for the generation to change (bounded by wait_limit ns: on expiry
+//           the CTA flags kErrWaitGrid and skips pass 2);
+//   pass 2: every CTA reduces the published maxima to the same amax, forms
+//           g = 2688 / max(amax, 1e-12) and quantizes its share of x, which pass 1
+//           has just brought into L2.
+// The cooperative launch makes all CTAs co-resident, so the barrier cannot wait
+// on a CTA that has not started.
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads) amax_quantize_kernel(
+    const uint16_t* __restrict__ x, int64_t rows, int64_t k, float* g_out,
+    uint8_t* __restrict__ codes, uint8_t* __restrict__ sf, uint32_t* ws, float* zero_word,
+    const uint4* __restrict__ rep_src, int64_t rep_k64, int64_t rep_total16,
+    uint4* __restrict__ rep_dst, uint64_t wait_limit, uint32_t* err_word, Div31 div) {
+  __shared__ uint32_t warp_max[kThreads / 32];
+  __shared__ int go;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kThreads;
+  uint32_t gen = 0;
+  if (threadIdx.x == 0) gen = ld_acquire_gpu(&ws[1]);
+
+  // pass 1: amax share
+  const int64_t numel = rows * k;                  // k % 64 == 0: no ragged tail
+  const int64_t nvec = numel / 8;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  uint32_t m = 0;
+  int64_t i = tid;
+  for (; i + (kUnroll - 1) * nthreads < nvec; i += kUnroll * nthreads) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = ld_stream(xv + i + u * nthreads);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) m = max(m, absmax8(v[u]));
+  }
+  for (; i < nvec; i += nthreads) m = max(m, absmax8(ld_stream(xv + i)));
+  // W-scale replication share
+  for (int64_t o = tid; o < rep_total16; o += nthreads) {
+    const int64_t x16 = o & 31, h = (o >> 7) & 1, jb = o >> 8;
+    const int64_t nb = jb / rep_k64, j = jb - nb * rep_k64;
+    rep_dst[o] = __ldg(rep_src + ((2 * nb + h) * rep_k64 + j) * 32 + x16);
+  }
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t bm = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) bm = max(bm, warp_max[w]);
+    ws[16 + blockIdx.x] = bm;
+    __threadfence();
+    const uint32_t prev = atomicAdd(&ws[0], 1u);
+    bool ok = true;
+    if (prev == gridDim.x - 1) {
+      ws[0] = 0;                       // re-armed for the next launch
+      __threadfence();
+      st_release_gpu(&ws[1], gen + 1);
+    } else {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_gpu(&ws[1]) == gen) {
+        if (global_timer_ns() - t0 > wait_limit) {
+          atomicOr(err_word, kErrWaitGrid);
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    go = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (!go) return;
+
+  // pass 2: the same amax in every CTA, then quantize
+  uint32_t bm = 0;
+  for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += kThreads)
+    bm = max(bm, __ldcg(&ws[16 + b]));
+  bm = __reduce_max_sync(0xFFFFFFFFu, bm);
+  __syncthreads();                     // warp_max reuse
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = bm;
+  __syncthreads();
+  uint32_t r = 0;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) r = max(r, warp_max[w]);
+  const float amax = __uint_as_float(r << 16);
+  const float g = encode_scale(amax);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    ws[2] = __float_as_uint(amax);
+    if (g_out != nullptr) *g_out = g;
+    if (zero_word != nullptr) *zero_word = 0.0f;
+  }
+  constexpr uint32_t kWarps = kThreads / 32;
+  quantize_blocks<false, false>(x, static_cast<uint32_t>(rows), static_cast<uint32_t>(k / 16), g,
+                                codes, sf, blockIdx.x * kWarps + (threadIdx.x >> 5),
+                                gridDim.x * kWarps, div);
 }
 
 __global__ void rcp_probe_kernel(const float* in, float* out, int64_t n) {
@@ -252,15 +435,70 @@ cudaError_t launch_amax(const uint16_t* x, int64_t numel, float* amax_out, float
 
 cudaError_t launch_quantize(const uint16_t* x, int64_t rows, int64_t k, const float* g,
                             const float* amax, float* g_out, uint8_t* codes, uint8_t* sf,
-                            float* zero_word, cudaStream_t st) {
+                            float* zero_word, cudaStream_t st, bool scratch_input) {
   const int64_t n_all = pad_up(rows, 128) * (k / 16);
-  int64_t blocks = (n_all + kThreads * kQuantUnroll - 1) / (kThreads * kQuantUnroll);
+  const int64_t chunks = (n_all + 31) / 32;
+  int64_t blocks = (chunks + (kThreads / 32) * kQuantUnroll - 1) / ((kThreads / 32) * kQuantUnroll);
   blocks = blocks < 1 ? 1 : blocks;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
-  quantize_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(x, rows, k, g, amax, g_out,
-                                                                      codes, sf, zero_word);
+  const Div31 div = make_div31(static_cast<uint32_t>(k / 16));
+  const uint32_t r = static_cast<uint32_t>(rows), bpr = static_cast<uint32_t>(k / 16);
+  // the discard works on whole 128-byte lines
+  if (scratch_input && (reinterpret_cast<uintptr_t>(x) & 127) == 0) {
+    quantize_kernel<true, true><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+        x, r, bpr, g, amax, g_out, codes, sf, zero_word, div);
+  } else {
+    quantize_kernel<false, false><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+        x, r, bpr, g, amax, g_out, codes, sf, zero_word, div);
+  }
   return cudaGetLastError();
+}
+
+cudaError_t launch_replicate_w_scales(const uint8_t* sf, int64_t n, int64_t k, uint8_t* rep,
+                                     cudaStream_t st) {
+  const int64_t total16 = n * (k / 16) * 4 / 16;   // 4 replicas of n * k/16 scale bytes
+  if (total16 <= 0) return cudaSuccess;
+  int64_t blocks = (total16 + kThreads - 1) / kThreads;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  replicate_w_scales_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
+      reinterpret_cast<const uint4*>(sf), k / 64, total16, reinterpret_cast<uint4*>(rep));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_amax_quantize(const uint16_t* x, int64_t rows, int64_t k, float* g_out,
+                                 uint8_t* codes, uint8_t* sf, uint32_t* ws, float* zero_word,
+                                 const uint8_t* rep_src, int64_t rep_n, int64_t rep_k,
+                                 uint8_t* rep_dst, uint64_t wait_limit, uint32_t* err_word,
+                                 cudaStream_t st) {
+  static int resident[64] = {0};   // CTAs of this kernel per SM, per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (resident[dev] == 0) {
+    int nb = 0;
+    cudaError_t e =
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, amax_quantize_kernel, kThreads, 0);
+    if (e != cudaSuccess) return e;
+    resident[dev] = nb > 0 ? nb : 1;
+  }
+  const int64_t n_all = pad_up(rows, 128) * (k / 16);
+  int64_t blocks = (n_all + kThreads * kQuantUnroll - 1) / (kThreads * kQuantUnroll);
+  blocks = blocks < 1 ? 1 : blocks;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * resident[dev];
+  if (blocks > cap) blocks = cap;
+  if (blocks > kAmaxMaxBlocks) blocks = kAmaxMaxBlocks;
+  const uint4* rsrc = reinterpret_cast<const uint4*>(rep_src);
+  uint4* rdst = reinterpret_cast<uint4*>(rep_dst);
+  int64_t rep_k64 = rep_k / 64 > 0 ? rep_k / 64 : 1;
+  int64_t rep_total16 = rep_dst != nullptr ? rep_n * (rep_k / 16) * 4 / 16 : 0;
+  Div31 div = make_div31(static_cast<uint32_t>(k / 16));
+  void* args[] = {&x, &rows, &k, &g_out, &codes, &sf, &ws, &zero_word, &rsrc, &rep_k64,
+                  &rep_total16, &rdst, &wait_limit, &err_word, &div};
+  return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(amax_quantize_kernel),
+                                     dim3(static_cast<unsigned>(blocks)), dim3(kThreads), args, 0,
+                                     st);
 }
 
 cudaError_t launch_rcp_probe(const float* in, float* out, int64_t n, cudaStream_t st) {

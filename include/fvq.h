@@ -103,6 +103,31 @@ int fvq_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a
                    int epilogue, float* amax_out, void* stream);
 
 /*
+ * Weight preparation with no reference counterpart.  The W scales of an
+ * [n, k] weight (128x4 layout) rewritten as the GEMM's 128-lane tensor-memory
+ * scale copies read them: each 512-byte atom four times, the two 128-row
+ * halves of a 256-row N block interleaved per 64-deep K step, so that one K
+ * tile's W scales take four copies instead of eight.  n % 256 == 0,
+ * k % 256 == 0; the output holds fvq_w_scales_replicated_bytes(n, k) =
+ * 4 * n * k / 16 bytes.  fvq_nvfp4_ffn does this for its second linear on
+ * every call; callers with fixed weights can do it once.
+ */
+size_t fvq_w_scales_replicated_bytes(int64_t n, int64_t k);
+int fvq_replicate_w_scales(const uint8_t* w_sf, int64_t n, int64_t k, uint8_t* w_sf_rep,
+                           void* stream);
+
+/*
+ * fvq_nvfp4_gemm with the FVQ_EPI_BF16 epilogue and the W scales in the
+ * replicated layout of fvq_replicate_w_scales; bit-identical results.  No
+ * reference counterpart (the reference's mm_fp4 takes the 128x4 layout, which
+ * fvq_nvfp4_gemm and fvq_nvfp4_mm accept).
+ */
+int fvq_nvfp4_gemm_wrep(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
+                        const uint8_t* w_codes, const uint8_t* w_sf_rep, const float* g_w,
+                        const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
+                        void* stream);
+
+/*
  * The same GEMM with a precomputed device alpha (fp32 scalar) instead of the
  * two global scales: the exact argument list of flashinfer.mm_fp4 as the
  * reference calls it (ffn_quantization.py:65-67), plus the optional bias of

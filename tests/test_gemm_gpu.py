@@ -166,3 +166,54 @@ def test_epilogue_gelu_matches_torch_on_every_bf16_input(order):
     assert torch.equal(torch.isnan(got), nan)
     mismatch = (got.view(torch.int16) != ref.view(torch.int16)) & ~nan
     assert int(mismatch.sum()) == 0, bits[mismatch][:10].tolist()
+
+
+def _replicate_ref(sf, n, k):
+    """The replicated W-scale layout, restated with numpy: atom (2*nb + h, j) of
+    the 128x4 layout at ((((nb * k64 + j) * 2 + h) * 4 + r) * 512) for r = 0..3."""
+    k64 = k // 64
+    atoms = sf.reshape(n // 256, 2, k64, 512).transpose(0, 2, 1, 3)        # [nb, j, h, 512]
+    return np.ascontiguousarray(np.broadcast_to(atoms[:, :, :, None, :],
+                                                (n // 256, k64, 2, 4, 512))).reshape(-1)
+
+
+@pytest.mark.parametrize("n,k", [(256, 256), (512, 768), (1536, 8960)])
+def test_replicated_w_scales_layout(n, k):
+    from flashvsr_optimizations_b200 import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(n + k)
+    sf = rng.integers(0, 256, size=n * k // 16, dtype=np.uint8)
+    assert lib.fvq_w_scales_replicated_bytes(n, k) == 4 * sf.size
+    dsf = torch.from_numpy(sf).cuda()
+    rep = torch.empty(4 * sf.size, dtype=torch.uint8, device="cuda")
+    _lib.call("fvq_replicate_w_scales", dsf.data_ptr(), n, k, rep.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    assert np.array_equal(rep.cpu().numpy(), _replicate_ref(sf, n, k))
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 256, 256), (200, 512, 512), (300, 256, 1536),
+                                   (513, 768, 768), (7680, 1536, 8960)])
+def test_gemm_with_replicated_w_scales_is_bit_identical(m, n, k):
+    """fvq_nvfp4_gemm_wrep (four 128x256b W-scale copies per K tile) gives the
+    same bits as fvq_nvfp4_gemm (eight 32x128b.warpx4 copies), bias included."""
+    from flashvsr_optimizations_b200 import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(m + 3 * n + k)
+    a, a_sf = _random_operand(m, k, rng)
+    w, w_sf = _random_operand(n, k, rng)
+    ta, tas, tw, tws = (torch.from_numpy(v).cuda() for v in (a, a_sf, w, w_sf))
+    ga = torch.tensor([1.25], device="cuda")
+    gw = torch.tensor([0.5], device="cuda")
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(k)) * 0.05).to(torch.bfloat16).cuda()
+    st = torch.cuda.current_stream().cuda_stream
+    ref = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    got = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+    rep = torch.empty(lib.fvq_w_scales_replicated_bytes(n, k), dtype=torch.uint8, device="cuda")
+    _lib.call("fvq_nvfp4_gemm", ta.data_ptr(), tas.data_ptr(), ga.data_ptr(), tw.data_ptr(),
+              tws.data_ptr(), gw.data_ptr(), bias.data_ptr(), ref.data_ptr(), m, n, k,
+              _lib.EPI_BF16, None, st)
+    _lib.call("fvq_replicate_w_scales", tws.data_ptr(), n, k, rep.data_ptr(), st)
+    _lib.call("fvq_nvfp4_gemm_wrep", ta.data_ptr(), tas.data_ptr(), ga.data_ptr(), tw.data_ptr(),
+              rep.data_ptr(), gw.data_ptr(), bias.data_ptr(), got.data_ptr(), m, n, k, st)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))

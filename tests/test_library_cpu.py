@@ -29,10 +29,14 @@ def test_version_and_workspace_sizes():
     assert lib.fvq_version() == 100
     assert lib.fvq_amax_workspace_bytes() >= 64 + 4 * 148 * 8
     ws = lib.fvq_nvfp4_ffn_workspace_bytes(7680, 1536, 8960)
-    # codes + scales of x, bf16 intermediate, codes + scales of the intermediate
-    need = 7680 * 768 + 7680 * 96 + 7680 * 8960 * 2 + 7680 * 4480 + 7680 * 560
+    # codes + scales of x, bf16 intermediate, codes + scales of the intermediate,
+    # W2 scales replicated four times
+    need = (7680 * 768 + 7680 * 96 + 7680 * 8960 * 2 + 7680 * 4480 + 7680 * 560
+            + 4 * 1536 * 8960 // 16)
     assert need <= ws <= need + 64 * 1024
     assert lib.fvq_nvfp4_ffn_workspace_bytes(0, 1536, 8960) == 0
+    assert lib.fvq_w_scales_replicated_bytes(1536, 8960) == 4 * 1536 * 8960 // 16
+    assert lib.fvq_w_scales_replicated_bytes(0, 8960) == 0
 
 
 def _rc(name, *args):
@@ -60,6 +64,15 @@ def test_gemm_rejects_bad_shapes_and_epilogue():
     assert gemm(0, 256, 256) == _lib.FVQ_EINVAL
     assert gemm(128, 256, 256, epi=7) == _lib.FVQ_EINVAL
     assert gemm(128, 256, 256, epi=1, amax=None) == _lib.FVQ_EINVAL
+    wrep = lambda m, n, k, ptr=b: _rc(  # noqa: E731
+        "fvq_nvfp4_gemm_wrep", b, b, b, b, ptr, b, None, b, m, n, k, None)
+    assert wrep(128, 200, 256) == _lib.FVQ_EINVAL
+    assert wrep(128, 256, 100) == _lib.FVQ_EINVAL
+    assert wrep(128, 256, 256, ptr=None) == _lib.FVQ_EINVAL
+    assert wrep(128, 256, 256, ptr=b + 8) == _lib.FVQ_EALIGN
+    assert _rc("fvq_replicate_w_scales", b, 300, 256, b, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_replicate_w_scales", b, 256, 320, b, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_replicate_w_scales", b, 256, 256, b + 4, None) == _lib.FVQ_EALIGN
 
 
 def test_linear_and_ffn_check_descriptors():

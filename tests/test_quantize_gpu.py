@@ -154,3 +154,29 @@ def test_rcp_probe_powers_of_two_exact():
     r = ops.rcp_approx_probe(v)
     assert torch.equal(r, 1.0 / v)
 
+
+
+@pytest.mark.parametrize("m,k", [(1, 64), (77, 1536), (300, 1536), (7680, 1536), (4096, 8960)])
+def test_fused_dynamic_quantize_equals_two_pass(m, k):
+    """fvq_nvfp4_quantize_dynamic (amax, grid barrier and quantize in one cooperative
+    launch) gives the bits of the two-pass path (amax kernel, then quantize with g),
+    call after call on one workspace (the barrier re-arms itself)."""
+    from flashvsr_optimizations_b200 import _lib
+    lib = fvq.load_library()
+    st = torch.cuda.current_stream().cuda_stream
+    ws = torch.zeros(lib.fvq_amax_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    for seed in range(3):
+        xb = W.student_t(m, k, seed=seed + m)
+        x = bits_to_dev(xb)
+        g_ref = ops.global_scale(x)
+        q_ref, s_ref = ops.nvfp4_quantize(x, g_ref)
+        q = torch.empty_like(q_ref)
+        s = torch.full_like(s_ref, 0xAB)
+        g = torch.empty(1, dtype=torch.float32, device="cuda")
+        _lib.call("fvq_nvfp4_quantize_dynamic", x.data_ptr(), m, k, None, g.data_ptr(),
+                  q.data_ptr(), s.data_ptr(), ws.data_ptr(), ws.numel(), st)
+        torch.cuda.synchronize()
+        assert g.item() == g_ref.item()
+        assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
+        assert not ws[:4].any()
+    assert ops.read_device_error() == 0
