@@ -287,8 +287,8 @@ def main():
     value = total_tokens / (ms * 1e-3)
     tflops = value * FLOP_PER_TOKEN / 1e12
 
-    # ---- per-kernel timing (same kernels through the per-op C-ABI entry points)
-    kt = kernel_timing(torch, lib, _lib, sets, tokens, dev, stream, min(args.steps, 400))
+    # ---- per-kernel timing (the library's events around fvq_nvfp4_ffn's launches)
+    kt = kernel_timing(lib, structs, ys, ws, ws_bytes, tokens, sptr, min(args.steps, 400))
     if world > 1:
         t = torch.tensor([kt["gemm_ms"], kt["quant_h_ms"]], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -371,71 +371,34 @@ def main():
         dist.destroy_process_group()
 
 
-def kernel_timing(torch, lib, _lib, sets, tokens, dev, stream, steps) -> dict:
-    """Per-kernel CUDA-event timing of the layer's six launches, as fvq_nvfp4_ffn issues them."""
-    import ctypes as C
-    d, f = D_MODEL, D_FF
-    st = stream.cuda_stream
-    codes_x = torch.empty(tokens, d // 2, dtype=torch.uint8, device=dev)
-    sf_x = torch.empty((tokens + 127) // 128 * 128, d // 16, dtype=torch.uint8, device=dev)
-    h = torch.empty(tokens, f, dtype=torch.bfloat16, device=dev)
-    codes_h = torch.empty(tokens, f // 2, dtype=torch.uint8, device=dev)
-    sf_h = torch.empty((tokens + 127) // 128 * 128, f // 16, dtype=torch.uint8, device=dev)
-    y = torch.empty(tokens, d, dtype=torch.bfloat16, device=dev)
-    scal = torch.zeros(64, dtype=torch.float32, device=dev)
-    amax_ws = torch.zeros(lib.fvq_amax_workspace_bytes(), dtype=torch.uint8, device=dev)
-    w2_rep = torch.empty(lib.fvq_w_scales_replicated_bytes(d, f), dtype=torch.uint8, device=dev)
-    gx, gh, amax_h = scal[0:1], scal[1:2], scal[2:3]
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
+def kernel_timing(lib, structs, ys, ws, ws_bytes, tokens, sptr, steps) -> dict:
+    """Device time of each of fvq_nvfp4_ffn's four launches, from the library's own
+    CUDA events (fvq_nvfp4_ffn_profile runs the same launch sequence and synchronises
+    after each layer, so every launch here starts on an idle GPU)."""
+    ms = (ctypes.c_float * 4)()
+    acc = [[] for _ in range(4)]
 
-    def chk(rc):
+    def one(i):
+        x, l1, l2 = structs[i % ROTATE]
+        rc = lib.fvq_nvfp4_ffn_profile(x.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2),
+                                       ys[i % ROTATE].data_ptr(), ws.data_ptr(), ws_bytes, sptr, ms)
         if rc != 0:
             raise RuntimeError(lib.fvq_last_error().decode())
 
-    def one(i, e):
-        x, ((q1, s1, g1, b1), (q2, s2, g2, b2)) = sets[i % ROTATE]
-        amax_h.zero_()
-        if e: e[0].record(stream)
-        # amax + global scale + quantize in one launch (fvq_nvfp4_ffn's first kernel also
-        # writes the 3.4 MB of replicated W2 scales)
-        chk(lib.fvq_nvfp4_quantize_dynamic(x.data_ptr(), tokens, d, None, gx.data_ptr(),
-                                           codes_x.data_ptr(), sf_x.data_ptr(), amax_ws.data_ptr(),
-                                           amax_ws.numel(), st))
-        if e: e[1].record(stream)
-        chk(lib.fvq_nvfp4_gemm(codes_x.data_ptr(), sf_x.data_ptr(), gx.data_ptr(), q1.data_ptr(),
-                               s1.data_ptr(), g1.data_ptr(), b1.data_ptr(), h.data_ptr(), tokens, f, d,
-                               1, amax_h.data_ptr(), st))
-        if e: e[2].record(stream)
-        chk(lib.fvq_nvfp4_quantize_dynamic(h.data_ptr(), tokens, f, amax_h.data_ptr(), gh.data_ptr(),
-                                           codes_h.data_ptr(), sf_h.data_ptr(), None, 0, st))
-        if e: e[3].record(stream)
-        # the standalone replication kernel, timed for reference (fvq_nvfp4_ffn folds it
-        # into its first kernel), then GEMM2 on the replicated W2 scales
-        chk(lib.fvq_replicate_w_scales(s2.data_ptr(), d, f, w2_rep.data_ptr(), st))
-        if e: e[4].record(stream)
-        chk(lib.fvq_nvfp4_gemm_wrep(codes_h.data_ptr(), sf_h.data_ptr(), gh.data_ptr(), q2.data_ptr(),
-                                    w2_rep.data_ptr(), g2.data_ptr(), b2.data_ptr(), y.data_ptr(),
-                                    tokens, d, f, st))
-        if e: e[5].record(stream)
-
     for i in range(5):
-        one(i, None)
-    torch.cuda.synchronize(dev)
+        one(i)
     for i in range(steps):
-        one(i, ev[i])
-    torch.cuda.synchronize(dev)
-    qx = [e[0].elapsed_time(e[1]) for e in ev]
-    g1t = [e[1].elapsed_time(e[2]) for e in ev]
-    qh = [e[2].elapsed_time(e[3]) for e in ev]
-    rep = [e[3].elapsed_time(e[4]) for e in ev]
-    g2t = [e[4].elapsed_time(e[5]) for e in ev]
-    mean = lambda v: sum(v) / len(v)  # noqa: E731
+        one(i)
+        for j in range(4):
+            acc[j].append(ms[j])
+    qx, g1t, qh, g2t = (sum(v) / len(v) for v in acc)
+    d, f = D_MODEL, D_FF
     qh_bytes = tokens * f * 2 + tokens * f // 2 + (tokens + 127) // 128 * 128 * f // 16
-    return {"quant_x_ms": mean(qx), "gemm1_ms": mean(g1t), "quant_h_ms": mean(qh),
-            "w2_scale_replicate_standalone_ms": mean(rep), "gemm2_ms": mean(g2t),
-            "gemm_ms": mean(g1t) + mean(g2t), "quant_h_gbs": qh_bytes / (mean(qh) * 1e-3) / 1e9,
-            "gemm1_tflops": tokens * 2 * d * f / (mean(g1t) * 1e-3) / 1e12,
-            "gemm2_tflops": tokens * 2 * d * f / (mean(g2t) * 1e-3) / 1e12, "steps": steps}
+    return {"quant_x_ms": qx, "gemm1_ms": g1t, "quant_h_ms": qh, "gemm2_ms": g2t,
+            "gemm_ms": g1t + g2t, "quant_h_gbs": qh_bytes / (qh * 1e-3) / 1e9,
+            "gemm1_tflops": tokens * 2 * d * f / (g1t * 1e-3) / 1e12,
+            "gemm2_tflops": tokens * 2 * d * f / (g2t * 1e-3) / 1e12, "steps": steps,
+            "note": "quant_x includes the W2 scale replication; launches timed one layer at a time"}
 
 
 def e2e_timing(torch, dist, fvq, NVFP4FFN, sets, tokens, dev, stream, world, steps, warmup) -> dict:

@@ -65,6 +65,9 @@ SIGNATURES = {
     "fvq_nvfp4_ffn_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "fvq_nvfp4_ffn": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _c.POINTER(FvqLinear), _vp,
                                  _vp, _sz, _vp]),
+    "fvq_nvfp4_ffn_profile": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear),
+                                         _c.POINTER(FvqLinear), _vp, _vp, _sz, _vp,
+                                         _c.POINTER(_c.c_float)]),
     "fvq_rcp_approx_probe": (_c.c_int, [_vp, _vp, _i64, _vp]),
     "fvq_gelu_bf16_probe": (_c.c_int, [_vp, _vp, _i64, _vp]),
     "fvq_set_wait_limit": (_c.c_int, [_c.c_uint64]),

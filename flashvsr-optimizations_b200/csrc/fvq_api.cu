@@ -324,8 +324,13 @@ size_t fvq_nvfp4_ffn_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff
   return c.off;
 }
 
-int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
-                  uint16_t* y, void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+
+// The FFN launch sequence.  ev: NULL, or 5 events recorded before the first
+// launch and after each of the four (for fvq_nvfp4_ffn_profile).
+int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
+             uint16_t* y, void* workspace, size_t workspace_bytes, cudaStream_t st,
+             cudaEvent_t* ev) {
   if (int rc = check_linear(lin1, "fvq_nvfp4_ffn (linear 1)")) return rc;
   if (int rc = check_linear(lin2, "fvq_nvfp4_ffn (linear 2)")) return rc;
   if (lin1->out_features != lin2->in_features || lin2->out_features != lin1->in_features)
@@ -342,7 +347,6 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
   if (!aligned32(x) || !aligned16(y) || !aligned16(workspace))
     return fail(FVQ_EALIGN, "fvq_nvfp4_ffn: x must be 32-byte aligned, y and workspace 16-byte");
   if (int rc = check_device()) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carve c(workspace);
   uint32_t* amax_ws = reinterpret_cast<uint32_t*>(c.take(fvq::kAmaxWorkspaceBytes));
   float* scalars = reinterpret_cast<float*>(c.take(kScalarBytes));
@@ -355,6 +359,10 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
   float* g_x = &scalars[0];
   float* g_h = &scalars[1];
   float* amax_h = &scalars[2];
+  auto mark = [&](int i) {
+    if (ev != nullptr) cudaEventRecord(ev[i], st);
+  };
+  mark(0);
   // 1. amax(x) -> g_x -> x in NVFP4, one launch; it also zeroes amax_h before GEMM1
   //    accumulates into it and writes the W2 scales in the layout of GEMM2's
   //    128x256b scale copies
@@ -362,17 +370,59 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
                                             lin2->scale, d, f, sf_w2_rep, g_wait_limit,
                                             fvq::error_word_ptr(), st);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(x) launch");
+  mark(1);
   // 2. h = bf16(gelu(bf16(bf16(alpha1 * acc) + b1))), amax_h = max |h|
   if (int rc = gemm_impl(codes_x, sf_x, g_x, lin1->qweight, lin1->scale, lin1->global_sf, nullptr,
                          lin1->bias, h, rows, f, d, FVQ_EPI_GELU_AMAX, amax_h, st))
     return rc;
-  // 3. h -> NVFP4 with g_h = 2688 / max(amax_h, 1e-12)
+  mark(2);
+  // 3. h -> NVFP4 with g_h = 2688 / max(amax_h, 1e-12); h is scratch, so its lines
+  //    are dropped from L2 once read
   e = fvq::launch_quantize(h, rows, f, nullptr, amax_h, g_h, codes_h, sf_h, nullptr, st,
                            /*scratch_input=*/true);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(h) launch");
+  mark(3);
   // 4. y = bf16(bf16(alpha2 * acc) + b2)
-  return gemm_impl(codes_h, sf_h, g_h, lin2->qweight, lin2->scale, lin2->global_sf, nullptr,
-                   lin2->bias, y, rows, d, f, FVQ_EPI_BF16, nullptr, st, sf_w2_rep);
+  if (int rc = gemm_impl(codes_h, sf_h, g_h, lin2->qweight, lin2->scale, lin2->global_sf, nullptr,
+                         lin2->bias, y, rows, d, f, FVQ_EPI_BF16, nullptr, st, sf_w2_rep))
+    return rc;
+  mark(4);
+  return FVQ_OK;
+}
+
+}  // namespace
+
+int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
+                  uint16_t* y, void* workspace, size_t workspace_bytes, void* stream) {
+  return ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes,
+                  static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                          const fvq_linear* lin2, uint16_t* y, void* workspace,
+                          size_t workspace_bytes, void* stream, float* kernel_ms) {
+  if (kernel_ms == nullptr) return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_profile: kernel_ms is NULL");
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaEvent_t ev[5];
+  int made = 0;
+  for (; made < 5; ++made) {
+    if (cudaEventCreate(&ev[made]) != cudaSuccess) break;
+  }
+  int rc = FVQ_OK;
+  if (made < 5) {
+    rc = fail(FVQ_ECUDA, "fvq_nvfp4_ffn_profile: cudaEventCreate failed");
+  } else {
+    rc = ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes, st, ev);
+    if (rc == FVQ_OK) {
+      cudaError_t e = cudaEventSynchronize(ev[4]);
+      for (int i = 0; e == cudaSuccess && i < 4; ++i)
+        e = cudaEventElapsedTime(&kernel_ms[i], ev[i], ev[i + 1]);
+      if (e != cudaSuccess) rc = cuda_fail(e, "fvq_nvfp4_ffn_profile timing");
+    }
+  }
+  for (int i = 0; i < made; ++i) cudaEventDestroy(ev[i]);
+  return rc;
 }
 
 int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream) {

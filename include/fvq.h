@@ -187,6 +187,17 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
                   uint16_t* y, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Instrumentation with no reference counterpart: fvq_nvfp4_ffn with CUDA
+ * events around its four launches (amax+quantize of x, GEMM1 with bias, GELU
+ * and amax, quantize of the intermediate, GEMM2 with bias).  Synchronises on
+ * the last event and writes the four device times in milliseconds to
+ * kernel_ms[0..3].
+ */
+int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                          const fvq_linear* lin2, uint16_t* y, void* workspace,
+                          size_t workspace_bytes, void* stream, float* kernel_ms);
+
+/*
  * Test support: out[i] = rcp.approx.ftz.f32(in[i]) on the device, the
  * reciprocal the quantizer uses (so a CPU checker can use measured values).
  */

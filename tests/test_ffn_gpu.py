@@ -172,3 +172,27 @@ def test_shape_errors_raise():
     with pytest.raises(fvq.FvqError) as e:
         ops.nvfp4_quantize(x, g)
     assert e.value.code == -1
+
+
+def test_ffn_profile_entry_point_same_output_and_times(ffn_layer):
+    """fvq_nvfp4_ffn_profile runs fvq_nvfp4_ffn's launches with events around them:
+    the same output bits, and four positive device times."""
+    import ctypes
+    from flashvsr_optimizations_b200 import _lib
+    ffn, _ = ffn_layer
+    q1, q2 = ffn[0], ffn[2]
+    x = bits_to_dev(W.student_t(W.M_ONE_LAYER, W.D_MODEL, seed=5))
+    ref = ffn(x)
+    lib = _lib.load()
+    m, d, f = W.M_ONE_LAYER, W.D_MODEL, W.D_FF
+    ws = torch.zeros(lib.fvq_nvfp4_ffn_workspace_bytes(m, d, f), dtype=torch.uint8, device="cuda")
+    l1 = _lib.FvqLinear(q1.qweight.data_ptr(), q1.scale.data_ptr(), q1.global_sf.data_ptr(),
+                        q1.bias.data_ptr(), d, f)
+    l2 = _lib.FvqLinear(q2.qweight.data_ptr(), q2.scale.data_ptr(), q2.global_sf.data_ptr(),
+                        q2.bias.data_ptr(), f, d)
+    y = torch.empty_like(ref)
+    ms = (ctypes.c_float * 4)()
+    _lib.call("fvq_nvfp4_ffn_profile", x.data_ptr(), m, ctypes.byref(l1), ctypes.byref(l2),
+              y.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream, ms)
+    assert torch.equal(y, ref)
+    assert all(t > 0 for t in ms), list(ms)
