@@ -199,6 +199,17 @@ __device__ __forceinline__ uint32_t gelu_bf16x2(uint32_t hv, uint32_t tab_base,
   return __byte_perm(r_lo, r_hi, 0x5410);
 }
 
+// alpha * (lo, hi) with one mul.rn.f32x2 (two IEEE products), rounded to a bf16x2 pair.
+__device__ __forceinline__ uint32_t scale_pack_bf16x2(uint32_t lo_bits, uint32_t hi_bits,
+                                                      uint64_t alpha2) {
+  uint64_t v, p;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo_bits), "r"(hi_bits));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(v), "l"(alpha2));
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(p));
+  return pack_bf16x2(lo, hi);
+}
+
 // bf16x2 add, one rounding of the exact sum.  For two bf16 operands this equals
 // torch's fp32 add followed by a bf16 rounding: the fp32 sum is exact unless
 // the exponents differ by more than 16, and then it lies far from a bf16 tie.
@@ -458,6 +469,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     uint8_t* warp_staging = staging + (warp - 2) * kWarpStagingBytes;
     // alpha = 1 / (g_a * g_w): torch's reciprocal of the product, IEEE rounded
     const float alpha = alpha_in != nullptr ? *alpha_in : __frcp_rn(__fmul_rn(*g_a, *g_w));
+    uint64_t alpha2;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(alpha2) : "f"(alpha));
     uint32_t amax2 = 0;  // max |h| of the low and high columns, bf16 magnitude bits
     for (int i = 0; i < seq.count; ++i) {
       if (!mbar_wait_bounded(&bars->acc_full, static_cast<uint32_t>(i) & 1u, wait_limit)) {
@@ -478,10 +491,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // mm_fp4's output: bf16(alpha * acc), packed in pairs
       uint32_t y[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        y[j] = pack_bf16x2(__fmul_rn(__uint_as_float(r[2 * j]), alpha),
-                           __fmul_rn(__uint_as_float(r[2 * j + 1]), alpha));
-      }
+      for (int j = 0; j < 32; ++j) y[j] = scale_pack_bf16x2(r[2 * j], r[2 * j + 1], alpha2);
       const int col0 = nb * BN + col_base;
       if constexpr (P::kStaged) {
         // GEMM1: bias, GELU and the amax on this thread's row, then the warp's
