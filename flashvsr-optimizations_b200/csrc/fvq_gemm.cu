@@ -92,6 +92,9 @@ static_assert(Plan<0, false, true>::kSmemBytes <= 232448, "GEMM2 replicated plan
 // K-major A and B, N = 256 (>>3 at bit 17), M = 128 (>>4 at bit 24).
 constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
                             (static_cast<uint32_t>(BM >> 4) << 24);
+// N = 128: one half of a W tile (tail tiles split in two, see TileSeq)
+constexpr uint32_t kIdescHalf = (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN / 2 >> 3) << 17) |
+                                (static_cast<uint32_t>(BM >> 4) << 24);
 
 template <int kStages>
 struct Barriers {
@@ -221,11 +224,18 @@ __device__ __forceinline__ uint32_t add_bf16x2(uint32_t a, uint32_t b) {
 
 // Tiles of one CTA.  Streaming: tile t = blockIdx + i*grid, M-block fastest.
 // Resident: the CTA keeps one N block (blockIdx % NB) and strides over M blocks.
-template <bool kResident>
+// kSplitTail (streaming only): when the tiles past the last full round of the
+// grid number at most half the grid, each of them is split into two N = 128
+// halves, one per CTA, so that the last round takes about half as long;
+// `half` is -1 for a whole tile, else 0 or 1.
+template <bool kResident, bool kSplitTail>
 struct TileSeq {
-  int count, nb_fixed, mb0, mb_step, num_m_blocks;
+  int count, nb_fixed, mb0, mb_step, num_m_blocks, full_rounds;
+  bool split;
   __device__ TileSeq(int num_m, int num_n) : num_m_blocks(num_m) {
     const int c = blockIdx.x, g = gridDim.x;
+    split = false;
+    full_rounds = 0;
     if (kResident) {
       nb_fixed = c % num_n;
       mb0 = c / num_n;
@@ -237,14 +247,25 @@ struct TileSeq {
       mb0 = 0;
       mb_step = 0;
       count = c < tiles ? (tiles - 1 - c) / g + 1 : 0;
+      const int rounds = tiles / g, rest = tiles - rounds * g;
+      if (kSplitTail && rounds > 0 && rest > 0 && 2 * rest <= g) {
+        split = true;
+        full_rounds = rounds;
+        count = rounds + (c < 2 * rest ? 1 : 0);
+      }
     }
   }
-  __device__ void at(int i, int& mb, int& nb) const {
+  __device__ void at(int i, int& mb, int& nb, int& half) const {
+    half = -1;
     if (kResident) {
       mb = mb0 + i * mb_step;
       nb = nb_fixed;
     } else {
-      const int t = blockIdx.x + i * gridDim.x;
+      int t = blockIdx.x + i * gridDim.x;
+      if (split && i == full_rounds) {
+        t = full_rounds * gridDim.x + (blockIdx.x >> 1);
+        half = blockIdx.x & 1;
+      }
       mb = t % num_m_blocks;
       nb = t / num_m_blocks;
     }
@@ -280,7 +301,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int num_k_tiles = k / BK;
   const int64_t sf_tile_stride = static_cast<int64_t>(k / 64) * 512;  // bytes per 128-row block
   const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
-  const TileSeq<kResident> seq(num_m_blocks, num_n_blocks);
+  const TileSeq<kResident, kEpi == 0> seq(num_m_blocks, num_n_blocks);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -325,8 +346,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int i = 0; i < seq.count && !aborted(bars); ++i) {
-        int mb, nb;
-        seq.at(i, mb, nb);
+        int mb, nb, half;
+        seq.at(i, mb, nb, half);  // a half tile loads the whole W tile
         for (int kt = 0; kt < num_k_tiles; ++kt) {
           if (!mbar_wait_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
             flag_error(bars, kErrWaitProducer);
@@ -393,6 +414,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
       }
       for (int i = 0; ok && i < seq.count && !aborted(bars); ++i) {
+        int mb_unused, nb_unused, half;
+        seq.at(i, mb_unused, nb_unused, half);
+        // a half tile: N = 128 MMAs on W rows [128 * half, +128) of the stage and
+        // the matching 4 of the 8 W-scale columns per K step
+        const uint32_t idesc = half < 0 ? kIdesc : kIdescHalf;
+        const uint32_t b_off = half > 0 ? static_cast<uint32_t>(kBBytes / 2) : 0u;
+        const uint32_t sfb_off = half > 0 ? 4u : 0u;
         if (!mbar_wait_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
                                wait_limit)) {
           flag_error(bars, kErrWaitMma);
@@ -428,12 +456,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
           }
           const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
-          const uint64_t bdesc = make_smem_desc(smem_u32(sb), 16, 1024, 2);
+          const uint64_t bdesc = make_smem_desc(smem_u32(sb) + b_off, 16, 1024, 2);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t sfb = tmem + kSfbCol + 8 * (kResident ? kt * 4 + j : j);
+            const uint32_t sfb = tmem + kSfbCol + 8 * (kResident ? kt * 4 + j : j) + sfb_off;
             mma_nvf4(acc, adesc + static_cast<uint64_t>(2 * j), bdesc + static_cast<uint64_t>(2 * j),
-                     kIdesc, tmem + kSfaCol + 4 * j, sfb, (kt > 0 || j > 0) ? 1u : 0u);
+                     idesc, tmem + kSfaCol + 4 * j, sfb, (kt > 0 || j > 0) ? 1u : 0u);
           }
           issued_any = true;
           tc_commit(&bars->empty[stage]);
@@ -478,8 +506,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         break;
       }
       tc_fence_after();
-      int mb, nb;
-      seq.at(i, mb, nb);
+      int mb, nb, half;
+      seq.at(i, mb, nb, half);
+      if (half >= 0 && quarter >= 2) {
+        // a half tile has 128 accumulator columns: this warp's 64 are not part of it
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->acc_empty);
+        continue;
+      }
       uint32_t r[64];
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + col_base;
       tmem_ld_32x32b_x32(taddr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
@@ -492,7 +526,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t y[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) y[j] = scale_pack_bf16x2(r[2 * j], r[2 * j + 1], alpha2);
-      const int col0 = nb * BN + col_base;
+      const int col0 = nb * BN + (half > 0 ? BN / 2 : 0) + col_base;
       if constexpr (P::kStaged) {
         // GEMM1: bias, GELU and the amax on this thread's row, then the warp's
         // 32 x 64 block goes out in one tensor store from 128B-swizzled staging
