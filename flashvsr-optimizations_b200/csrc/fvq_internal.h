@@ -20,7 +20,16 @@ constexpr uint64_t kDefaultWaitLimit = 2000000000ull;
 
 // amax workspace: [0] arrival counter, [2] amax bits, partials from byte 64.
 constexpr int kAmaxMaxBlocks = 2048;
-constexpr size_t kAmaxWorkspaceBytes = 64 + kAmaxMaxBlocks * 4;
+// amax workspace words: arrival counter, barrier generation, amax bits, the
+// grid barrier's per-group counters, then one partial maximum per CTA
+constexpr int kWsCounter = 0;
+constexpr int kWsGeneration = 1;
+constexpr int kWsAmax = 2;
+constexpr int kWsGroups = 32;          // 64 group counters
+constexpr int kBarrierGroup = 64;      // CTAs per group counter
+constexpr int kWsPartial = 128;
+constexpr size_t kAmaxWorkspaceBytes = (kWsPartial + kAmaxMaxBlocks) * 4;
+static_assert(kAmaxMaxBlocks / kBarrierGroup <= kWsPartial - kWsGroups, "group counters");
 
 inline int64_t pad_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 inline size_t sf_bytes(int64_t rows, int64_t k) {

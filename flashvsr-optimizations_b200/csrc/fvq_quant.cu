@@ -44,6 +44,25 @@ __device__ __forceinline__ uint32_t absmax8(uint4 v) {
   return max(m & 0xFFFFu, m >> 16);
 }
 
+// max |x| over the 16-byte words first, first + stride, ... below nvec: batches
+// of kUnroll independent loads (the last batch predicated), so every thread
+// keeps kUnroll loads in flight even when it has fewer than kUnroll words.
+__device__ __forceinline__ uint32_t absmax_words(const uint4* __restrict__ xv, int64_t nvec,
+                                                 int64_t first, int64_t stride) {
+  uint32_t m = 0;
+  for (int64_t i = first; i < nvec; i += kUnroll * stride) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t j = i + u * stride;
+      v[u] = j < nvec ? ld_stream(xv + j) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) m = max(m, absmax8(v[u]));
+  }
+  return m;
+}
+
 // four bytes (low 8 bits of each argument) -> one word, b0 lowest
 __device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
   uint32_t lo, hi, r;
@@ -74,17 +93,7 @@ __global__ void __launch_bounds__(kThreads) amax_kernel(const uint16_t* __restri
   const int64_t nvec = numel / 8;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kThreads;
-  const uint4* xv = reinterpret_cast<const uint4*>(x);
-  uint32_t m = 0;
-  int64_t i = tid;
-  for (; i + (kUnroll - 1) * nthreads < nvec; i += kUnroll * nthreads) {
-    uint4 v[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) v[u] = ld_stream(xv + i + u * nthreads);
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) m = max(m, absmax8(v[u]));
-  }
-  for (; i < nvec; i += nthreads) m = max(m, absmax8(ld_stream(xv + i)));
+  uint32_t m = absmax_words(reinterpret_cast<const uint4*>(x), nvec, tid, nthreads);
   // ragged tail (numel % 8)
   for (int64_t t = nvec * 8 + tid; t < numel; t += nthreads) m = max(m, x[t] & 0x7FFFu);
 
@@ -95,9 +104,9 @@ __global__ void __launch_bounds__(kThreads) amax_kernel(const uint16_t* __restri
     uint32_t bm = 0;
 #pragma unroll
     for (int w = 0; w < kThreads / 32; ++w) bm = max(bm, warp_max[w]);
-    ws[16 + blockIdx.x] = bm;
+    ws[kWsPartial + blockIdx.x] = bm;
     __threadfence();
-    uint32_t prev = atomicAdd(&ws[0], 1u);
+    uint32_t prev = atomicAdd(&ws[kWsCounter], 1u);
     is_last = (prev == gridDim.x - 1);
   }
   __syncthreads();
@@ -106,7 +115,7 @@ __global__ void __launch_bounds__(kThreads) amax_kernel(const uint16_t* __restri
   __threadfence();
   uint32_t bm = 0;
   for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += kThreads)
-    bm = max(bm, __ldcg(&ws[16 + b]));
+    bm = max(bm, __ldcg(&ws[kWsPartial + b]));
   bm = __reduce_max_sync(0xFFFFFFFFu, bm);
   if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = bm;
   __syncthreads();
@@ -115,10 +124,10 @@ __global__ void __launch_bounds__(kThreads) amax_kernel(const uint16_t* __restri
 #pragma unroll
     for (int w = 0; w < kThreads / 32; ++w) r = max(r, warp_max[w]);
     const float amax = __uint_as_float(r << 16);
-    ws[2] = __float_as_uint(amax);
+    ws[kWsAmax] = __float_as_uint(amax);
     if (amax_out) *amax_out = amax;
     if (g_out) *g_out = encode_scale(amax);
-    ws[0] = 0;
+    ws[kWsCounter] = 0;
   }
 }
 
@@ -188,6 +197,24 @@ __device__ __forceinline__ void quantize_blocks(const uint16_t* __restrict__ x, 
   const uint32_t n_chunks = (n_all + 31) / 32;
   const uint32_t* xw = reinterpret_cast<const uint32_t*>(x);
 
+  // software pipeline: the next batch's loads are issued before this batch is
+  // processed, so each thread keeps 2 * kQuantUnroll blocks of loads in flight
+  uint32_t vn[kQuantUnroll][8];
+  auto load_batch = [&](uint32_t c0, uint32_t (&dst)[kQuantUnroll][8]) {
+#pragma unroll
+    for (int u = 0; u < kQuantUnroll; ++u) {
+      const uint32_t cu = c0 + u * warp_stride;
+      const uint32_t ch = kReverse ? n_chunks - 1 - cu : cu;
+      const uint32_t b = ch * 32 + lane;
+      if (cu < n_chunks && b < n_real) {
+        ld_stream_v8(xw + static_cast<size_t>(b) * 8, dst[u]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dst[u][j] = 0;
+      }
+    }
+  };
+  load_batch(warp_first, vn);
   for (uint32_t c = warp_first; c < n_chunks; c += warp_stride * kQuantUnroll) {
     uint32_t v[kQuantUnroll][8];
     uint32_t chunk[kQuantUnroll];
@@ -195,14 +222,10 @@ __device__ __forceinline__ void quantize_blocks(const uint16_t* __restrict__ x, 
     for (int u = 0; u < kQuantUnroll; ++u) {
       const uint32_t cu = c + u * warp_stride;
       chunk[u] = kReverse ? n_chunks - 1 - cu : cu;
-      const uint32_t b = chunk[u] * 32 + lane;
-      if (cu < n_chunks && b < n_real) {
-        ld_stream_v8(xw + static_cast<size_t>(b) * 8, v[u]);
-      } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[u][j] = 0;
-      }
+      for (int j = 0; j < 8; ++j) v[u][j] = vn[u][j];
     }
+    load_batch(c + warp_stride * kQuantUnroll, vn);
 #pragma unroll
     for (int u = 0; u < kQuantUnroll; ++u) {
       if (c + u * warp_stride >= n_chunks) break;  // warp-uniform
@@ -292,12 +315,11 @@ __global__ void __launch_bounds__(kThreads) replicate_w_scales_kernel(const uint
 
 // ---------------------------------------------------------------- fused amax + quantize
 // One cooperative launch for the dynamic quantization of an activation:
-//   pass 1: max |x| over this CTA's grid-stride share, published to ws[16 + cta]
+//   pass 1: max |x| over this CTA's grid-stride share, published to ws[kWsPartial + cta]
 //           (plus, optionally, a share of the W-scale replication above);
-//   grid barrier: arrival counter ws[0] and generation word ws[1]; the last CTA
-//           to arrive resets the counter and advances the generation, the others
-//           wait for the generation to change (bounded by wait_limit ns: on expiry
-//           the CTA flags kErrWaitGrid and skips pass 2);
+//   grid barrier (grid_barrier): the last CTA to arrive advances the generation
+//           word ws[kWsGeneration], the others wait for it to change (bounded by
+//           wait_limit ns: on expiry the CTA flags kErrWaitGrid and skips pass 2);
 //   pass 2: every CTA reduces the published maxima to the same amax, forms
 //           g = 2688 / max(amax, 1e-12) and quantizes its share of x, which pass 1
 //           has just brought into L2.
@@ -313,6 +335,40 @@ __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Grid barrier for thread 0 of each CTA, in two levels so that no counter sees
+// more than 64 arrivals: the last CTA of each group of 64 arrives at the top
+// counter, the last of those advances the generation word.  Counters are
+// reset by their last arrival, so the next launch finds them at zero.
+// Returns false (and flags kErrWaitGrid) if the generation did not change
+// within wait_limit ns.
+__device__ bool grid_barrier(uint32_t* ws, uint32_t gen, uint64_t wait_limit, uint32_t* err_word) {
+  const uint32_t ngroups = (gridDim.x + kBarrierGroup - 1) / kBarrierGroup;
+  const uint32_t group = blockIdx.x / kBarrierGroup;
+  const uint32_t in_group = min(static_cast<uint32_t>(kBarrierGroup), gridDim.x - group * kBarrierGroup);
+  __threadfence();
+  if (atomicAdd(&ws[kWsGroups + group], 1u) == in_group - 1) {
+    ws[kWsGroups + group] = 0;
+    __threadfence();
+    if (atomicAdd(&ws[kWsCounter], 1u) == ngroups - 1) {
+      ws[kWsCounter] = 0;
+      __threadfence();
+      st_release_gpu(&ws[kWsGeneration], gen + 1);
+      return true;
+    }
+  }
+  const uint64_t t0 = global_timer_ns();
+  uint32_t sleep_ns = 32;
+  while (ld_acquire_gpu(&ws[kWsGeneration]) == gen) {
+    if (global_timer_ns() - t0 > wait_limit) {
+      atomicOr(err_word, kErrWaitGrid);
+      return false;
+    }
+    __nanosleep(sleep_ns);
+    if (sleep_ns < 256) sleep_ns *= 2;
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads) amax_quantize_kernel(
     const uint16_t* __restrict__ x, int64_t rows, int64_t k, float* g_out,
     uint8_t* __restrict__ codes, uint8_t* __restrict__ sf, uint32_t* ws, float* zero_word,
@@ -323,22 +379,12 @@ __global__ void __launch_bounds__(kThreads) amax_quantize_kernel(
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kThreads;
   uint32_t gen = 0;
-  if (threadIdx.x == 0) gen = ld_acquire_gpu(&ws[1]);
+  if (threadIdx.x == 0) gen = ld_acquire_gpu(&ws[kWsGeneration]);
 
   // pass 1: amax share
   const int64_t numel = rows * k;                  // k % 64 == 0: no ragged tail
   const int64_t nvec = numel / 8;
-  const uint4* xv = reinterpret_cast<const uint4*>(x);
-  uint32_t m = 0;
-  int64_t i = tid;
-  for (; i + (kUnroll - 1) * nthreads < nvec; i += kUnroll * nthreads) {
-    uint4 v[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) v[u] = ld_stream(xv + i + u * nthreads);
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) m = max(m, absmax8(v[u]));
-  }
-  for (; i < nvec; i += nthreads) m = max(m, absmax8(ld_stream(xv + i)));
+  uint32_t m = absmax_words(reinterpret_cast<const uint4*>(x), nvec, tid, nthreads);
   // W-scale replication share
   for (int64_t o = tid; o < rep_total16; o += nthreads) {
     const int64_t x16 = o & 31, h = (o >> 7) & 1, jb = o >> 8;
@@ -352,26 +398,8 @@ __global__ void __launch_bounds__(kThreads) amax_quantize_kernel(
     uint32_t bm = 0;
 #pragma unroll
     for (int w = 0; w < kThreads / 32; ++w) bm = max(bm, warp_max[w]);
-    ws[16 + blockIdx.x] = bm;
-    __threadfence();
-    const uint32_t prev = atomicAdd(&ws[0], 1u);
-    bool ok = true;
-    if (prev == gridDim.x - 1) {
-      ws[0] = 0;                       // re-armed for the next launch
-      __threadfence();
-      st_release_gpu(&ws[1], gen + 1);
-    } else {
-      const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_gpu(&ws[1]) == gen) {
-        if (global_timer_ns() - t0 > wait_limit) {
-          atomicOr(err_word, kErrWaitGrid);
-          ok = false;
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    go = ok ? 1 : 0;
+    ws[kWsPartial + blockIdx.x] = bm;
+    go = grid_barrier(ws, gen, wait_limit, err_word) ? 1 : 0;
   }
   __syncthreads();
   if (!go) return;
@@ -379,7 +407,7 @@ __global__ void __launch_bounds__(kThreads) amax_quantize_kernel(
   // pass 2: the same amax in every CTA, then quantize
   uint32_t bm = 0;
   for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += kThreads)
-    bm = max(bm, __ldcg(&ws[16 + b]));
+    bm = max(bm, __ldcg(&ws[kWsPartial + b]));
   bm = __reduce_max_sync(0xFFFFFFFFu, bm);
   __syncthreads();                     // warp_max reuse
   if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = bm;
@@ -390,7 +418,7 @@ __global__ void __launch_bounds__(kThreads) amax_quantize_kernel(
   const float amax = __uint_as_float(r << 16);
   const float g = encode_scale(amax);
   if (blockIdx.x == 0 && threadIdx.x == 0) {
-    ws[2] = __float_as_uint(amax);
+    ws[kWsAmax] = __float_as_uint(amax);
     if (g_out != nullptr) *g_out = g;
     if (zero_word != nullptr) *zero_word = 0.0f;
   }
