@@ -17,7 +17,11 @@ Prints one JSON line (rank 0).  `value` is whole-job tokens/s with inputs
 resident in HBM; `e2e` is the same metric through the public module API with
 host buffers (pinned H2D of the input and D2H of the output inside the timed
 region); `roofline` describes the GEMM kernel; `cpu_baseline` times the
-reference arithmetic (the CPU oracle) on this host.
+reference arithmetic (the CPU oracle) on this host.  Two separate measurements
+follow the timed steps (skip them with --no-extras): `stack_30_layers`, the
+30-layer stack of distinct layers over 15360 tokens with rows sharded across the
+ranks and the outputs all-gathered, and `quantize_sweep` (rank 0), the
+activation quantizer on K in {1536, 8960} x M in {1024, 4096, 16384, 65536}.
 
 `--impl reference` times the reference's NVFP4 FFN arithmetic on the host CPU
 (the oracle restatement; the reference itself needs FlashInfer on a GPU) with
@@ -60,6 +64,8 @@ def parse():
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the quantize sweep and the 30-layer stack (separate measurements)")
     ap.add_argument("--cpu-seconds", type=float, default=20.0,
                     help="wall-time budget of the CPU baseline sample")
     return ap.parse_args()
@@ -185,6 +191,127 @@ def make_sets(torch, ops, dev, tokens, rank):
             layers.append((q, s, g, b))
         sets.append((x, layers))
     return sets
+
+
+def quantize_sweep(torch, lib, dev, stream, hbm_peak) -> list:
+    """The standalone activation-quantize sweep: K in {1536, 8960} x M in {1024, 4096, 16384,
+    65536}, N(0,1) with 0.1% of elements x50 (seed 2).  Per shape: the quantizer with a
+    given scale (one read of x: 2MK + MK/2 + pad128(M)K/16 bytes) and the dynamic path
+    (amax + scale + quantize in one launch; x is read twice when it does not fit in L2)."""
+    st = stream.cuda_stream
+    ws = torch.zeros(lib.fvq_amax_workspace_bytes(), dtype=torch.uint8, device=dev)
+    out = []
+    for k in (1536, 8960):
+        for m in (1024, 4096, 16384, 65536):
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(2)
+            x = torch.randn(m, k, device=dev, generator=gen)
+            idx = torch.randint(0, m * k, (max(1, m * k // 1000),), device=dev, generator=gen)
+            x.view(-1)[idx] *= 50.0
+            x = x.to(torch.bfloat16)
+            del idx
+            codes = torch.empty(m, k // 2, dtype=torch.uint8, device=dev)
+            sf = torch.empty((m + 127) // 128 * 128, k // 16, dtype=torch.uint8, device=dev)
+            g = torch.empty(1, dtype=torch.float32, device=dev)
+
+            def dyn():
+                lib.fvq_nvfp4_quantize_dynamic(x.data_ptr(), m, k, None, g.data_ptr(), codes.data_ptr(),
+                                               sf.data_ptr(), ws.data_ptr(), ws.numel(), st)
+
+            def fixed():
+                lib.fvq_nvfp4_quantize(x.data_ptr(), m, k, g.data_ptr(), codes.data_ptr(),
+                                       sf.data_ptr(), st)
+            one_read = 2 * m * k + m * k // 2 + (m + 127) // 128 * 128 * k // 16
+            row = {"m": m, "k": k}
+            for name, f, nbytes in (("quantize", fixed, one_read), ("dynamic", dyn, one_read + 2 * m * k)):
+                reps = max(5, min(200, int(2e9 // (2 * m * k))))
+                for _ in range(3):
+                    f()
+                torch.cuda.synchronize(dev)
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                for _ in range(reps):
+                    f()
+                e.record(stream)
+                e.synchronize()
+                us = s.elapsed_time(e) / reps * 1e3
+                gbs = nbytes / (us * 1e-6) / 1e9
+                row[name] = {"us": round(us, 2), "GBps": round(gbs, 1),
+                             "frac_of_hbm": round(gbs / hbm_peak, 3) if hbm_peak else None}
+            out.append(row)
+            del x, codes, sf
+    torch.cuda.empty_cache()
+    return out
+
+
+def stack_timing(torch, dist, ops, lib, dev, stream, world, rank, steps=10) -> dict:
+    """The 30-layer FFN stack: M = 15360 N(0,1) tokens (seed 3), 30 layers with distinct
+    N(0,0.02) weights (and N(0,0.01) biases), token rows sharded over the ranks, outputs
+    all-gathered.  Time = max over ranks of (30 layers + gather)."""
+    from flashvsr_optimizations_b200.sharding import gather_rows, row_range
+    total, layers = 15360, 30
+    r0, r1 = row_range(total, world, rank)
+    rows = r1 - r0
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    x_all = torch.randn(total, D_MODEL, device=dev, generator=gen).to(torch.bfloat16)
+    x = x_all[r0:r1].contiguous()
+    del x_all
+    structs, keep = [], []
+    for layer in range(layers):
+        gl = torch.Generator(device=dev)
+        gl.manual_seed(100 + layer)
+        pair = []
+        for (n, k) in ((D_FF, D_MODEL), (D_MODEL, D_FF)):
+            w = (torch.randn(n, k, device=dev, generator=gl) * 0.02).to(torch.bfloat16)
+            b = (torch.randn(n, device=dev, generator=gl) * 0.01).to(torch.bfloat16)
+            gsc = ops.global_scale(w)
+            q, sc = ops.nvfp4_quantize(w, gsc)
+            keep.append((q, sc, gsc, b))
+            pair.append(_lib_linear(q, sc, gsc, b, k, n))
+        structs.append(pair)
+    ws_bytes = lib.fvq_nvfp4_ffn_workspace_bytes(rows, D_MODEL, D_FF)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    bufs = [torch.empty(rows, D_MODEL, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    st = stream.cuda_stream
+
+    def run_stack():
+        cur = x
+        for i, (l1, l2) in enumerate(structs):
+            out = bufs[i % 2]
+            rc = lib.fvq_nvfp4_ffn(cur.data_ptr(), rows, ctypes.byref(l1), ctypes.byref(l2),
+                                   out.data_ptr(), ws.data_ptr(), ws_bytes, st)
+            if rc != 0:
+                raise RuntimeError(lib.fvq_last_error().decode())
+            cur = out
+        return gather_rows(cur, total) if world > 1 else cur
+
+    for _ in range(2):
+        run_stack()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        y = run_stack()
+    e.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = s.elapsed_time(e) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    tflops = total * layers * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12
+    finite = bool(torch.isfinite(y.float()).all().item())
+    return {"tokens": total, "layers": layers, "ms_per_stack": ms,
+            "tokens_per_s": total / (ms * 1e-3), "tflops": tflops, "finite_output": finite,
+            "rows_per_rank": rows, "includes": "30 fvq_nvfp4_ffn calls per rank + all-gather of the outputs"}
+
+
+def _lib_linear(q, s, g, b, in_f, out_f):
+    from flashvsr_optimizations_b200 import _lib
+    return _lib.FvqLinear(q.data_ptr(), s.data_ptr(), g.data_ptr(), b.data_ptr(), in_f, out_f)
 
 
 def fp4_library_peak(torch, dev) -> float | None:
@@ -337,6 +464,13 @@ def main():
             traffic = json.loads(tp.read_text()).get("dram_bytes_per_gemm_pair")
         except ValueError:
             traffic = None
+    extras = {}
+    if not args.no_extras:
+        stack = stack_timing(torch, dist, ops, lib, dev, stream, world, rank)
+        stack["tflops_frac_of_fp4_peak"] = stack["tflops"] / peak
+        extras["stack_30_layers"] = stack
+        if rank == 0:
+            extras["quantize_sweep"] = quantize_sweep(torch, lib, dev, stream, hbm)
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -360,6 +494,7 @@ def main():
     }
     if gather:
         result["gather"] = gather
+    result.update(extras)
     if fp4_cublas:
         result["fp4_cublas_8192_tflops"] = fp4_cublas
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
