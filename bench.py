@@ -449,11 +449,15 @@ def main():
 
     peaks = measured_peaks()
     fp4_cublas = fp4_library_peak(torch, dev) if rank == 0 else None
-    bf16_burst = peaks.get("bf16_tflops")
-    if bf16_burst:
-        peak, peak_src = 4.0 * bf16_burst, "4 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json); dense FP4 runs at 4x bf16 on B200"
+    # the GEMMs are timed inside long runs of layers, where the 1000 W cap holds the SM
+    # clock well below its maximum: the sustained bf16 figure is the matching denominator
+    bf16_sustained = peaks.get("bf16_tflops_sustained")
+    if bf16_sustained:
+        peak = 4.0 * bf16_sustained
+        peak_src = ("4 x measured cuBLAS bf16 sustained (MEASURED_PEAKS.json, power-capped); "
+                    "dense FP4 runs at 4x bf16 on B200")
     else:
-        peak, peak_src = 4.0 * 1590.0, "4 x fallback bf16 1.59 PFLOP/s"
+        peak, peak_src = 4.0 * 1400.0, "4 x fallback sustained bf16 1.4 PFLOP/s"
     hbm = peaks.get("hbm_gbs") or 6650.0
     gemm_flop = tokens * FLOP_PER_TOKEN
     achieved = gemm_flop / (kt["gemm_ms"] * 1e-3) / 1e12

@@ -442,6 +442,11 @@ int fvq_gelu_bf16_probe(const uint16_t* in, uint16_t* out, int64_t count, void* 
   return FVQ_OK;
 }
 
+int fvq_set_gemm_pairing(int enabled) {
+  fvq::set_gemm_pairing(enabled != 0);
+  return FVQ_OK;
+}
+
 int fvq_set_wait_limit(uint64_t nanoseconds) {
   g_wait_limit = nanoseconds == 0 ? fvq::kDefaultWaitLimit : nanoseconds;
   return FVQ_OK;

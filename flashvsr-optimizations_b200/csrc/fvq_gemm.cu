@@ -594,6 +594,254 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+// ---------------------------------------------------------------- SM-pair GEMM
+// nvfp4_gemm_pair_kernel: the FVQ_EPI_BF16 GEMM with replicated W scales on
+// clusters of two CTAs (the two SMs of a pair) and tcgen05.mma.cta_group::2: a
+// 256 x 256 output tile per pair.  Each CTA loads its 128 rows of A, 128 of the
+// tile's 256 W rows, its A scales and the replicated W scales of all 256 rows;
+// the even CTA issues the scale copies and MMAs for both (one copy instruction
+// fills both SMs' TMEM, so per SM a K tile costs half the copy instructions).  The odd CTA's warp 1 relays "my stage
+// landed" to the even CTA; the even CTA commits "stage free" and "accumulator
+// full" to both CTAs' barriers; both epilogues report a drained accumulator
+// to the even CTA.  All loads of both CTAs (codes, and the scales through 3-D
+// tensor maps over their 512-byte atoms) count their bytes on the even CTA's
+// stage barrier, which only the even CTA arms, so the MMA issuer needs no
+// message from the odd CTA.  Rows per pair tile: 256, so the host uses it for
+// m % 256 == 0.
+constexpr int kPairStages = 4;
+constexpr int kPairBBytes = kBBytes / 2;  // 128 W rows per CTA
+constexpr int kPairStageBytes = kABytes + kPairBBytes + kSfaBytes + kSfbRepBytes;  // 50 KB
+constexpr int kPairBarrierOff = kPairStages * kPairStageBytes;
+constexpr int kPairSmemBytes = kPairBarrierOff + kBarrierBytes;
+static_assert(kPairSmemBytes <= 232448, "pair plan exceeds shared memory");
+constexpr uint32_t kIdescPair = (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                (static_cast<uint32_t>(2 * BM >> 4) << 24);
+
+struct PairBarriers {
+  uint64_t full[kPairStages];       // even CTA: both CTAs' stage landed
+  uint64_t empty[kPairStages];      // the pair's MMAs on the stage completed
+  uint64_t acc_full;                // the pair's accumulator is complete
+  uint64_t acc_empty;               // even CTA: both epilogues drained their TMEM
+  uint64_t teardown;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(PairBarriers) <= kBarrierBytes, "pair barrier area");
+
+__global__ void __launch_bounds__(kNumThreads, 1)
+    nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                           const __grid_constant__ CUtensorMap tmap_b_half,
+                           const __grid_constant__ CUtensorMap tmap_sfa,
+                           const __grid_constant__ CUtensorMap tmap_sfb,
+                           const float* __restrict__ g_a, const float* __restrict__ g_w,
+                           const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m,
+                           int n, int k, uint64_t wait_limit) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicOr(&g_device_error, kErrSmemAlign);
+    return;  // both CTAs see the same layout, so both return here
+  }
+  auto* bars = reinterpret_cast<PairBarriers*>(smem + kPairBarrierOff);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool even = rank == 0;
+  const int pairs = gridDim.x / 2, pair = blockIdx.x / 2;
+  const int num_m_pairs = m / (2 * BM);
+  const int num_n_blocks = n / BN;
+  const int tiles = num_m_pairs * num_n_blocks;
+  const int count = pair < tiles ? (tiles - 1 - pair) / pairs + 1 : 0;  // same in both CTAs
+  const int num_k_tiles = k / BK;
+  const int64_t sf_tile_stride = static_cast<int64_t>(k / 64) * 512;
+  const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 2 * kEpiWarps);
+    mbar_init(&bars->teardown, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b_half);
+    prefetch_tmap(&tmap_sfa);
+    prefetch_tmap(&tmap_sfb);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&bars->tmem_base, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const auto even_addr = [&](const void* p) { return mapa_shared(smem_u32(p), 0); };
+  const auto odd_addr = [&](const void* p) { return mapa_shared(smem_u32(p), 1); };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0 && count > 0) {
+      uint32_t armed[kPairStages];
+#pragma unroll
+      for (int s = 0; s < kPairStages; ++s) armed[s] = 0;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int i = 0; i < count && !aborted(bars); ++i) {
+        const int t = pair + i * pairs;
+        const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
+        const int a_block = 2 * mbp + static_cast<int>(rank);  // this CTA's 128 rows
+        for (int kt = 0; kt < num_k_tiles; ++kt) {
+          if (!mbar_wait_cluster_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
+            flag_error(bars, kErrWaitProducer);
+            break;
+          }
+          uint8_t* sa = smem + stage * kPairStageBytes;
+          uint8_t* sb = sa + kABytes;
+          uint8_t* ssfa = sb + kPairBBytes;
+          uint8_t* ssfb = ssfa + kSfaBytes;
+          const uint32_t bar = even_addr(&bars->full[stage]);
+          if (even) mbar_arrive_expect_tx(&bars->full[stage], 2 * kPairStageBytes);
+          tma_load_2d_pair(sa, &tmap_a, bar, kt * BKB, a_block * BM);
+          tma_load_2d_pair(sb, &tmap_b_half, bar, kt * BKB,
+                           nb * BN + static_cast<int>(rank) * (BN / 2));
+          // A scales: atoms 4kt..4kt+3 of 128-row block a_block; W scales: the
+          // 32 replicated atoms of K steps 4kt..4kt+3 of N block nb
+          tma_load_3d_pair(ssfa, &tmap_sfa, bar, 0, kt * 4, a_block);
+          tma_load_3d_pair(ssfb, &tmap_sfb, bar, 0, 0, nb * (k / 64) + kt * 4);
+          armed[stage] += 1;
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // the even CTA's stage barriers count both CTAs' loads; the odd CTA's land
+      // before the even CTA's MMAs consume the stage, which the final cluster
+      // barrier waits for
+      for (int s = 0; even && s < kPairStages; ++s) {
+        if (armed[s] > 0 &&
+            !mbar_wait_cluster_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit))
+          flag_error(bars, kErrWaitTeardown);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && count > 0 && even) {
+      // ---------------------------------------------------------- MMA issuer (even CTA)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued_any = false;
+      bool ok = true;
+      for (int i = 0; ok && i < count && !aborted(bars); ++i) {
+        if (!mbar_wait_cluster_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
+                                       wait_limit)) {
+          flag_error(bars, kErrWaitMma);
+          break;
+        }
+        tc_fence_after();
+        for (int kt = 0; kt < num_k_tiles; ++kt) {
+          if (!mbar_wait_cluster_bounded(&bars->full[stage], phase, wait_limit)) {
+            flag_error(bars, kErrWaitMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* sa = smem + stage * kPairStageBytes;
+          uint8_t* sb = sa + kABytes;
+          uint8_t* ssfa = sb + kPairBBytes;
+          uint8_t* ssfb = ssfa + kSfaBytes;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            tmem_cp_32x128b_x4_pair(tmem + kSfaCol + 4 * j,
+                                    make_smem_desc(smem_u32(ssfa + 512 * j), 16, 128, 0));
+            tmem_cp_128x256b_pair(tmem + kSfbCol + 8 * j,
+                                  make_smem_desc(smem_u32(ssfb + 4096 * j), 2048, 128, 0));
+          }
+          const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
+          const uint64_t bdesc = make_smem_desc(smem_u32(sb), 16, 1024, 2);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            mma_nvf4_pair(tmem, adesc + static_cast<uint64_t>(2 * j),
+                          bdesc + static_cast<uint64_t>(2 * j), kIdescPair, tmem + kSfaCol + 4 * j,
+                          tmem + kSfbCol + 8 * j, (kt > 0 || j > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          tc_commit_pair(smem_u32(&bars->empty[stage]));
+          tc_commit_pair(odd_addr(&bars->empty[stage]));
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(smem_u32(&bars->acc_full));
+        tc_commit_pair(odd_addr(&bars->acc_full));
+      }
+      if (aborted(bars) && issued_any) {
+        tc_commit_pair(smem_u32(&bars->teardown));
+        if (!mbar_wait_bounded(&bars->teardown, 0, teardown_limit))
+          flag_error(bars, kErrWaitTeardown);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;
+    const int quarter = (warp - 2) >> 2;
+    const int col_base = quarter * 64;
+    const int trow = quad * 32 + lane;
+    const float alpha = __frcp_rn(__fmul_rn(*g_a, *g_w));
+    uint64_t alpha2;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(alpha2) : "f"(alpha));
+    const uint32_t acc_empty_addr = even_addr(&bars->acc_empty);
+    for (int i = 0; i < count; ++i) {
+      if (!mbar_wait_cluster_bounded(&bars->acc_full, static_cast<uint32_t>(i) & 1u, wait_limit)) {
+        flag_error(bars, kErrWaitEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const int t = pair + i * pairs;
+      const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
+      uint32_t r[64];
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + col_base;
+      tmem_ld_32x32b_x32(taddr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_addr);
+      uint32_t y[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) y[j] = scale_pack_bf16x2(r[2 * j], r[2 * j + 1], alpha2);
+      const int col0 = nb * BN + col_base;
+      const int row = mbp * 2 * BM + static_cast<int>(rank) * BM + trow;
+      uint16_t* dst = out + static_cast<int64_t>(row) * n + col0;
+#pragma unroll
+      for (int c = 0; c < 64; c += 8) {
+        uint4 bv = make_uint4(0, 0, 0, 0);
+        if (bias != nullptr) bv = __ldg(reinterpret_cast<const uint4*>(bias + col0 + c));
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t w = y[c / 2 + j];
+          if (bias != nullptr) w = add_bf16x2(w, bw[j]);
+          o[j] = w;
+        }
+        if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // neither CTA leaves while the pair's MMAs or arrivals may touch it
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
+}
+
 // GELU of bf16 values through the epilogue's path (test support): values
 // 2i and 2i+1 form one bf16x2 word, as in the epilogue; an odd last value
 // goes through the single-value path.
@@ -689,7 +937,72 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CU
   return cudaGetLastError();
 }
 
+// 3-D maps over 512-byte scale atoms (128 x u32): A scales [blocks][k/64 atoms][128],
+// box 4 atoms (one K tile); replicated W scales [n/256 * k/64][8 atoms][128], box
+// 4 x 8 atoms (one K tile of one N block).
+bool make_scale_maps(CUtensorMap* sfa, CUtensorMap* sfb, const uint8_t* a_sf, int64_t a_blocks,
+                     const uint8_t* w_sf_rep, int64_t n, int64_t k) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint64_t k64 = static_cast<cuuint64_t>(k / 64);
+  cuuint32_t estr[3] = {1, 1, 1};
+  cuuint64_t dims_a[3] = {128, k64, static_cast<cuuint64_t>(a_blocks)};
+  cuuint64_t strides_a[2] = {512, k64 * 512};
+  cuuint32_t box_a[3] = {128, 4, 1};
+  CUresult r = enc(sfa, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(a_sf), dims_a,
+                   strides_a, box_a, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  cuuint64_t dims_b[3] = {128, 8, static_cast<cuuint64_t>(n / BN) * k64};
+  cuuint64_t strides_b[2] = {512, 4096};
+  cuuint32_t box_b[3] = {128, 8, 4};
+  r = enc(sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(w_sf_rep), dims_b, strides_b,
+          box_b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
+                             const CUtensorMap& msfa, const CUtensorMap& msfb, const float* g_a,
+                             const float* g_w,
+                             const uint16_t* bias, uint16_t* out, int m, int n, int k,
+                             uint64_t wait_limit, cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_pair_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int tiles = (m / (2 * BM)) * (n / BN);
+  int pairs = sm_count() / 2;
+  if (pairs > tiles) pairs = tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(kNumThreads);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, nvfp4_gemm_pair_kernel, ma, mb_half, msfa, msfb, g_a, g_w, bias,
+                            out, m, n, k, wait_limit);
+}
+
 }  // namespace
+
+// GEMMs with replicated W scales and m % 256 == 0 run on SM pairs when enabled
+// (off by default: measured at the one-SM kernel's speed, both clock-limited by
+// the power cap under sustained tensor load).
+static bool g_pairing = false;
+void set_gemm_pairing(bool enabled) { g_pairing = enabled; }
+bool gemm_pairs(int64_t m, int epilogue) { return g_pairing && epilogue == 0 && m % (2 * BM) == 0; }
 
 cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
@@ -717,6 +1030,17 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                                     amax_out, wait_limit, st);
     return launch_gemm_t<1, false>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
                                    amax_out, wait_limit, st);
+  }
+  if (gemm_pairs(m, epilogue) && alpha == nullptr && w_sf_rep != nullptr) {
+    alignas(64) CUtensorMap mb_half;
+    alignas(64) CUtensorMap msfa;
+    alignas(64) CUtensorMap msfb;
+    if (!make_code_map(&mb_half, w_codes, n, k, BN / 2) ||
+        !make_scale_maps(&msfa, &msfb, a_sf, m / BM, w_sf_rep, n, k)) {
+      if (why) *why = "cuTensorMapEncodeTiled failed for the SM-pair GEMM";
+      return cudaErrorInvalidValue;
+    }
+    return launch_gemm_pair(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki, wait_limit, st);
   }
   if (w_sf_rep != nullptr)
     return launch_gemm_t<0, false, true>(ma, mb, mo, a_sf, w_sf_rep, g_a, g_w, alpha, bias, out, mi,

@@ -69,6 +69,10 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                         const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
                         int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
                         const char** why, const uint8_t* w_sf_rep = nullptr);
+// FVQ_EPI_BF16 GEMMs with replicated W scales, alpha from the global scales and
+// m % 256 == 0 run on SM pairs (nvfp4_gemm_pair_kernel) when enabled.
+void set_gemm_pairing(bool enabled);
+bool gemm_pairs(int64_t m, int epilogue);
 cudaError_t launch_gelu_probe(const uint16_t* in, uint16_t* out, int64_t count, cudaStream_t st);
 cudaError_t set_error_word(uint32_t v, cudaStream_t st);
 uint32_t* error_word_ptr();   // device address of the error word (current device)

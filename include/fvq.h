@@ -211,6 +211,15 @@ int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream);
 int fvq_gelu_bf16_probe(const uint16_t* in, uint16_t* out, int64_t count, void* stream);
 
 /*
+ * Library setting with no reference counterpart: GEMMs with replicated W scales
+ * (fvq_nvfp4_gemm_wrep, and the second GEMM of fvq_nvfp4_ffn) whose m is a
+ * multiple of 256 run on pairs of SMs (clusters of two CTAs sharing 256 x 256
+ * tiles, tcgen05 cta_group::2) when enabled; 0 (the default) selects the one-SM
+ * kernel.  Both give the same bits.  Applies to later launches from any thread.
+ */
+int fvq_set_gemm_pairing(int enabled);
+
+/*
  * Bounded device waits: a GEMM whose pipeline wait exceeds the limit sets a
  * device error word and returns early (after letting its own copies and MMAs
  * drain).  fvq_set_wait_limit changes the limit, in nanoseconds of wall time

@@ -193,11 +193,16 @@ def test_replicated_w_scales_layout(n, k):
     assert np.array_equal(rep.cpu().numpy(), _replicate_ref(sf, n, k))
 
 
+# m % 256 == 0 runs on SM pairs (clusters of two CTAs, tcgen05.mma.cta_group::2);
+# (2560, 2048, 512) has 80 pair tiles for 74 pairs, so some pairs take two tiles
 @pytest.mark.parametrize("m,n,k", [(1, 256, 256), (200, 512, 512), (300, 256, 1536),
-                                   (513, 768, 768), (7680, 1536, 8960)])
-def test_gemm_with_replicated_w_scales_is_bit_identical(m, n, k):
-    """fvq_nvfp4_gemm_wrep (four 128x256b W-scale copies per K tile) gives the
-    same bits as fvq_nvfp4_gemm (eight 32x128b.warpx4 copies), bias included."""
+                                   (513, 768, 768), (256, 256, 256), (512, 768, 512),
+                                   (768, 256, 1536), (2560, 2048, 512), (7680, 1536, 8960)])
+@pytest.mark.parametrize("pairing", [0, 1])
+def test_gemm_with_replicated_w_scales_is_bit_identical(m, n, k, pairing):
+    """fvq_nvfp4_gemm_wrep (four 128x256b W-scale copies per K tile; on SM pairs
+    when pairing is on and m % 256 == 0) gives the same bits as fvq_nvfp4_gemm
+    (one SM per tile, eight 32x128b.warpx4 copies), bias included."""
     from flashvsr_optimizations_b200 import _lib
     lib = _lib.load()
     rng = np.random.default_rng(m + 3 * n + k)
@@ -215,7 +220,11 @@ def test_gemm_with_replicated_w_scales_is_bit_identical(m, n, k):
               tws.data_ptr(), gw.data_ptr(), bias.data_ptr(), ref.data_ptr(), m, n, k,
               _lib.EPI_BF16, None, st)
     _lib.call("fvq_replicate_w_scales", tws.data_ptr(), n, k, rep.data_ptr(), st)
-    _lib.call("fvq_nvfp4_gemm_wrep", ta.data_ptr(), tas.data_ptr(), ga.data_ptr(), tw.data_ptr(),
-              rep.data_ptr(), gw.data_ptr(), bias.data_ptr(), got.data_ptr(), m, n, k, st)
+    try:
+        _lib.call("fvq_set_gemm_pairing", pairing)
+        _lib.call("fvq_nvfp4_gemm_wrep", ta.data_ptr(), tas.data_ptr(), ga.data_ptr(), tw.data_ptr(),
+                  rep.data_ptr(), gw.data_ptr(), bias.data_ptr(), got.data_ptr(), m, n, k, st)
+    finally:
+        _lib.call("fvq_set_gemm_pairing", 0)
     torch.cuda.synchronize()
     assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
