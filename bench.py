@@ -471,7 +471,7 @@ def main():
     extras = {}
     if not args.no_extras:
         stack = stack_timing(torch, dist, ops, lib, dev, stream, world, rank)
-        stack["tflops_frac_of_fp4_peak"] = stack["tflops"] / peak
+        stack["tflops_frac_of_fp4_peak"] = stack["tflops"] / (peak * world)  # whole job / N GPUs
         extras["stack_30_layers"] = stack
         if rank == 0:
             extras["quantize_sweep"] = quantize_sweep(torch, lib, dev, stream, hbm)
@@ -483,7 +483,7 @@ def main():
         "config": {"workload": WORKLOAD, "tokens_per_gpu": tokens, "d_model": D_MODEL, "d_ff": D_FF,
                    "layers": 1, "parallelism": f"token-row shards x{world}, replicated weights",
                    "l2": f"inputs rotate over {ROTATE} distinct activation/weight sets (312 MB > 126 MB L2)"},
-        "tflops": tflops, "tflops_frac_of_fp4_peak": tflops / peak,
+        "tflops": tflops, "tflops_frac_of_fp4_peak": tflops / (peak * world),
         "gpu_launches": LAUNCHES_PER_LAYER * args.steps,
         "roofline": {"bound": "tensor", "kernel": "nvfp4_gemm_kernel (GEMM1 + GEMM2 of the layer)",
                      "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "TFLOP/s",
