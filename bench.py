@@ -314,6 +314,40 @@ def _lib_linear(q, s, g, b, in_f, out_f):
     return _lib.FvqLinear(q.data_ptr(), s.data_ptr(), g.data_ptr(), b.data_ptr(), in_f, out_f)
 
 
+def fp4_library_sustained(torch, dev, seconds=2.0) -> dict | None:
+    """cuBLASLt NVFP4 (torch._scaled_mm) on the layer's two GEMM shapes, each run back to
+    back for `seconds` so that it sits under the same power cap as the layer: the library's
+    sustained TFLOP/s next to which the layer's GEMMs can be read."""
+    try:
+        out = {}
+        for name, (m, n, k) in (("gemm1_7680x8960x1536", (TOKENS, D_FF, D_MODEL)),
+                                ("gemm2_7680x1536x8960", (TOKENS, D_MODEL, D_FF))):
+            a = torch.randint(0, 256, (m, k // 2), dtype=torch.uint8, device=dev).view(torch.float4_e2m1fn_x2)
+            b = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev).view(torch.float4_e2m1fn_x2)
+            sa = torch.full((m * k // 16,), 0x38, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+            sb = torch.full((n * k // 16,), 0x38, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+            f = lambda: torch._scaled_mm(a, b.t(), sa, sb, out_dtype=torch.bfloat16)  # noqa: E731
+            for _ in range(10):
+                f()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            reps = 0
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            while time.perf_counter() - t0 < seconds:
+                for _ in range(50):
+                    f()
+                reps += 50
+                torch.cuda.synchronize()
+            e.record()
+            e.synchronize()
+            us = s.elapsed_time(e) / reps * 1e3
+            out[name] = {"us": round(us, 2), "tflops": round(2 * m * n * k / (us * 1e-6) / 1e12, 1)}
+        return out
+    except Exception:
+        return None
+
+
 def fp4_library_peak(torch, dev) -> float | None:
     """Dense NVFP4 throughput of cuBLASLt (torch._scaled_mm) at 8192^3, TFLOP/s, or None."""
     try:
@@ -501,6 +535,10 @@ def main():
     result.update(extras)
     if fp4_cublas:
         result["fp4_cublas_8192_tflops"] = fp4_cublas
+    if rank == 0 and not args.no_extras:
+        lib_sustained = fp4_library_sustained(torch, dev)
+        if lib_sustained:
+            result["fp4_cublas_sustained_layer_shapes"] = lib_sustained
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_ffn_tokens_per_s(5, 1, args.cpu_seconds)
     if rank == 0:
