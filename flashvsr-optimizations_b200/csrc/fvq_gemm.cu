@@ -156,10 +156,15 @@ __device__ __forceinline__ void gelu_table_init(uint16_t* tab, int tid, int nthr
   }
 }
 
-// bf16(gelu(x)) for a bf16 input, bit-identical to the exact formula.
+// bf16(gelu(x)) for a bf16 input, bit-identical to the exact formula.  For
+// 8 <= |x| (finite, and +inf) the fp32 tanh saturates to +-1, so the formula
+// gives x itself for positive x and -0 for negative x.
 __device__ __forceinline__ uint32_t gelu_bf16(uint32_t x_bits, const uint16_t* tab) {
-  const uint32_t off = (x_bits & 0x7FFFu) - kGeluTabLo;
+  const uint32_t mag = x_bits & 0x7FFFu;
+  const uint32_t off = mag - kGeluTabLo;
   if (off < kGeluTabSpan) return tab[off | ((x_bits & 0x8000u) >> 4)];
+  if (mag >= 0x4100u && mag < 0x7F80u) return (x_bits & 0x8000u) ? 0x8000u : x_bits;
+  if (x_bits == 0x7F80u) return x_bits;
   return gelu_bf16_exact(x_bits);
 }
 
