@@ -43,6 +43,18 @@ class FvqLinear(_c.Structure):
     ]
 
 
+class FvqLinearFp8(_c.Structure):
+    """Mirror of ``struct fvq_linear_fp8``."""
+
+    _fields_ = [
+        ("qweight", _vp),
+        ("scale", _vp),
+        ("bias", _vp),
+        ("in_features", _i64),
+        ("out_features", _i64),
+    ]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "fvq_version": (_c.c_int, []),
@@ -69,6 +81,19 @@ SIGNATURES = {
     "fvq_nvfp4_ffn_profile": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear),
                                          _c.POINTER(FvqLinear), _vp, _vp, _sz, _vp,
                                          _c.POINTER(_c.c_float)]),
+    "fvq_fp8_row_quantize": (_c.c_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "fvq_fp8_tensor_quantize_workspace_bytes": (_sz, []),
+    "fvq_fp8_tensor_quantize": (_c.c_int, [_vp, _i64, _vp, _vp, _vp, _sz, _vp]),
+    "fvq_fp8_scaled_mm": (_c.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "fvq_fp8_linear_workspace_bytes": (_sz, [_i64, _i64]),
+    "fvq_fp8_linear": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinearFp8), _vp, _vp, _sz, _vp]),
+    "fvq_fp8_ffn_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "fvq_fp8_ffn": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinearFp8), _c.POINTER(FvqLinearFp8),
+                               _vp, _vp, _sz, _vp]),
+    "fvq_fp8_ffn_profile": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinearFp8),
+                                       _c.POINTER(FvqLinearFp8), _vp, _vp, _sz, _vp,
+                                       _c.POINTER(_c.c_float)]),
+    "fvq_div_full_probe": (_c.c_int, [_vp, _vp, _vp, _i64, _vp]),
     "fvq_rcp_approx_probe": (_c.c_int, [_vp, _vp, _i64, _vp]),
     "fvq_gelu_bf16_probe": (_c.c_int, [_vp, _vp, _i64, _vp]),
     "fvq_set_wait_limit": (_c.c_int, [_c.c_uint64]),

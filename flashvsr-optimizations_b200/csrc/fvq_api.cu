@@ -425,6 +425,264 @@ int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin
   return rc;
 }
 
+// ---------------------------------------------------------------- FP8 (W8A8) mode
+
+int fvq_fp8_row_quantize(const uint16_t* x, int64_t rows, int64_t k, uint8_t* q, float* scale,
+                         void* stream) {
+  if (rows <= 0 || rows > (int64_t(1) << 31) - 1)
+    return fail(FVQ_EINVAL, "fvq_fp8_row_quantize: rows must be in [1, 2^31) (got %lld)",
+                (long long)rows);
+  if (k <= 0 || k % 8 != 0 || k > fvq::fp8_row_quant_max_k())
+    return fail(FVQ_EINVAL, "fvq_fp8_row_quantize: k must be a positive multiple of 8 up to %lld "
+                "(got %lld)", (long long)fvq::fp8_row_quant_max_k(), (long long)k);
+  if (!x || !q || !scale) return fail(FVQ_EINVAL, "fvq_fp8_row_quantize: NULL pointer");
+  if (!aligned16(x) || !aligned16(q) || (reinterpret_cast<uintptr_t>(scale) & 3u) != 0)
+    return fail(FVQ_EALIGN, "fvq_fp8_row_quantize: x and q must be 16-byte aligned, scale 4-byte");
+  if (int rc = check_device()) return rc;
+  cudaError_t e = fvq::launch_fp8_row_quant(x, rows, k, q, scale, nullptr, nullptr,
+                                            static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_fp8_row_quantize launch");
+  return FVQ_OK;
+}
+
+size_t fvq_fp8_tensor_quantize_workspace_bytes(void) {
+  return round_up(fvq::kAmaxWorkspaceBytes) + kScalarBytes;
+}
+
+int fvq_fp8_tensor_quantize(const uint16_t* x, int64_t numel, uint8_t* q, float* scale,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  if (numel <= 0)
+    return fail(FVQ_EINVAL, "fvq_fp8_tensor_quantize: numel must be > 0 (got %lld)",
+                (long long)numel);
+  if (!x || !q || !scale || !workspace) return fail(FVQ_EINVAL, "fvq_fp8_tensor_quantize: NULL pointer");
+  if (workspace_bytes < fvq_fp8_tensor_quantize_workspace_bytes())
+    return fail(FVQ_EWORKSPACE, "fvq_fp8_tensor_quantize: workspace needs %zu bytes, got %zu",
+                fvq_fp8_tensor_quantize_workspace_bytes(), workspace_bytes);
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u) != 0 || !aligned16(workspace))
+    return fail(FVQ_EALIGN,
+                "fvq_fp8_tensor_quantize: x and workspace must be 16-byte aligned, q 8-byte");
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c(workspace);
+  uint32_t* amax_ws = reinterpret_cast<uint32_t*>(c.take(fvq::kAmaxWorkspaceBytes));
+  float* amax = reinterpret_cast<float*>(c.take(kScalarBytes));
+  cudaError_t e = fvq::launch_amax(x, numel, amax, nullptr, amax_ws, nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_fp8_tensor_quantize amax launch");
+  e = fvq::launch_fp8_tensor_quant(x, numel, amax, q, scale, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_fp8_tensor_quantize launch");
+  return FVQ_OK;
+}
+
+namespace {
+
+int check_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w, const float* sw,
+                   const uint16_t* bias, const uint16_t* out, int64_t m, int64_t n, int64_t k,
+                   const char* who) {
+  if (m <= 0 || m > (int64_t(1) << 30))
+    return fail(FVQ_EINVAL, "%s: m must be in [1, 2^30] (got %lld)", who, (long long)m);
+  if (n <= 0 || n % 256 != 0)
+    return fail(FVQ_EINVAL, "%s: n must be a positive multiple of 256 (got %lld)", who,
+                (long long)n);
+  if (k <= 0 || k % 128 != 0 || k > fvq::fp8_row_quant_max_k())
+    return fail(FVQ_EINVAL, "%s: k must be a positive multiple of 128 up to %lld (got %lld)", who,
+                (long long)fvq::fp8_row_quant_max_k(), (long long)k);
+  if (n * k > (int64_t(1) << 31) || m * k > (int64_t(1) << 40))
+    return fail(FVQ_EINVAL, "%s: operand too large", who);
+  if (!a || !sa || !w || !sw || !out) return fail(FVQ_EINVAL, "%s: NULL pointer", who);
+  if (!aligned16(a) || !aligned16(w) || !aligned16(sw) || !aligned16(out) || !aligned16(bias) ||
+      (reinterpret_cast<uintptr_t>(sa) & 3u) != 0)
+    return fail(FVQ_EALIGN, "%s: operands, W scales, bias and out must be 16-byte aligned", who);
+  return FVQ_OK;
+}
+
+int fp8_gemm_impl(const uint8_t* a, const float* sa, const uint8_t* w, const float* sw,
+                  const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
+                  int epilogue, uint32_t* row_amax, cudaStream_t st) {
+  const char* why = nullptr;
+  cudaError_t e = fvq::launch_fp8_gemm(a, sa, w, sw, bias, out, m, n, k, epilogue, row_amax,
+                                       g_wait_limit, st, &why);
+  if (e != cudaSuccess) {
+    if (why) return fail(FVQ_ECUDA, "fp8 GEMM: %s", why);
+    return cuda_fail(e, "fp8 GEMM launch");
+  }
+  return FVQ_OK;
+}
+
+int check_fp8_linear(const fvq_linear_fp8* lin, const char* who) {
+  if (lin == nullptr) return fail(FVQ_EINVAL, "%s: linear descriptor is NULL", who);
+  if (!lin->qweight || !lin->scale)
+    return fail(FVQ_EINVAL, "%s: qweight and scale are required", who);
+  if (lin->in_features <= 0 || lin->in_features % 128 != 0 ||
+      lin->in_features > fvq::fp8_row_quant_max_k() || lin->out_features <= 0 ||
+      lin->out_features % 256 != 0)
+    return fail(FVQ_EINVAL,
+                "%s: in_features must be a positive multiple of 128 up to %lld and out_features "
+                "a positive multiple of 256 (got %lld, %lld)",
+                who, (long long)fvq::fp8_row_quant_max_k(), (long long)lin->in_features,
+                (long long)lin->out_features);
+  if (!aligned16(lin->qweight) || !aligned16(lin->scale) || !aligned16(lin->bias))
+    return fail(FVQ_EALIGN, "%s: weight buffers must be 16-byte aligned", who);
+  return FVQ_OK;
+}
+
+int check_fp8_rows(int64_t rows, const char* who) {
+  if (rows <= 0 || rows > (int64_t(1) << 30))
+    return fail(FVQ_EINVAL, "%s: rows must be in [1, 2^30] (got %lld)", who, (long long)rows);
+  return FVQ_OK;
+}
+
+}  // namespace
+
+int fvq_fp8_scaled_mm(const uint8_t* a, const float* scale_a, const uint8_t* w,
+                      const float* scale_w, const uint16_t* bias, uint16_t* out, int64_t m,
+                      int64_t n, int64_t k, void* stream) {
+  if (int rc = check_fp8_gemm(a, scale_a, w, scale_w, bias, out, m, n, k, "fvq_fp8_scaled_mm"))
+    return rc;
+  if (int rc = check_device()) return rc;
+  return fp8_gemm_impl(a, scale_a, w, scale_w, bias, out, m, n, k, FVQ_EPI_BF16, nullptr,
+                       static_cast<cudaStream_t>(stream));
+}
+
+size_t fvq_fp8_linear_workspace_bytes(int64_t rows, int64_t in_features) {
+  if (rows <= 0 || in_features <= 0) return 0;
+  Carve c(nullptr);
+  c.take(static_cast<size_t>(rows * in_features));
+  c.take(static_cast<size_t>(rows * 4));
+  return c.off;
+}
+
+int fvq_fp8_linear(const uint16_t* x, int64_t rows, const fvq_linear_fp8* lin, uint16_t* y,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_fp8_linear(lin, "fvq_fp8_linear")) return rc;
+  if (int rc = check_fp8_rows(rows, "fvq_fp8_linear")) return rc;
+  if (!x || !y || !workspace) return fail(FVQ_EINVAL, "fvq_fp8_linear: NULL pointer");
+  const size_t need = fvq_fp8_linear_workspace_bytes(rows, lin->in_features);
+  if (workspace_bytes < need)
+    return fail(FVQ_EWORKSPACE, "fvq_fp8_linear: workspace needs %zu bytes, got %zu", need,
+                workspace_bytes);
+  if (!aligned16(x) || !aligned16(y) || !aligned16(workspace))
+    return fail(FVQ_EALIGN, "fvq_fp8_linear: x, y and workspace must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t k = lin->in_features;
+  Carve c(workspace);
+  uint8_t* q = c.take(static_cast<size_t>(rows * k));
+  float* s = reinterpret_cast<float*>(c.take(static_cast<size_t>(rows * 4)));
+  cudaError_t e = fvq::launch_fp8_row_quant(x, rows, k, q, s, nullptr, nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_fp8_linear quantize launch");
+  return fp8_gemm_impl(q, s, lin->qweight, lin->scale, lin->bias, y, rows, lin->out_features, k,
+                       FVQ_EPI_BF16, nullptr, st);
+}
+
+size_t fvq_fp8_ffn_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff) {
+  if (rows <= 0 || d_model <= 0 || d_ff <= 0) return 0;
+  Carve c(nullptr);
+  c.take(static_cast<size_t>(rows * 4));          // per-row max |h|
+  c.take(static_cast<size_t>(rows * d_model));    // x in E4M3
+  c.take(static_cast<size_t>(rows * 4));          // x row scales
+  c.take(static_cast<size_t>(rows * d_ff * 2));   // h
+  c.take(static_cast<size_t>(rows * d_ff));       // h in E4M3
+  c.take(static_cast<size_t>(rows * 4));          // h row scales
+  return c.off;
+}
+
+namespace {
+
+int fp8_ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear_fp8* lin1,
+                 const fvq_linear_fp8* lin2, uint16_t* y, void* workspace, size_t workspace_bytes,
+                 cudaStream_t st, cudaEvent_t* ev) {
+  if (int rc = check_fp8_linear(lin1, "fvq_fp8_ffn (linear 1)")) return rc;
+  if (int rc = check_fp8_linear(lin2, "fvq_fp8_ffn (linear 2)")) return rc;
+  if (lin1->out_features != lin2->in_features || lin2->out_features != lin1->in_features)
+    return fail(FVQ_EINVAL, "fvq_fp8_ffn: linear shapes do not chain (%lld->%lld, %lld->%lld)",
+                (long long)lin1->in_features, (long long)lin1->out_features,
+                (long long)lin2->in_features, (long long)lin2->out_features);
+  if (int rc = check_fp8_rows(rows, "fvq_fp8_ffn")) return rc;
+  if (!x || !y || !workspace) return fail(FVQ_EINVAL, "fvq_fp8_ffn: NULL pointer");
+  const int64_t d = lin1->in_features, f = lin1->out_features;
+  const size_t need = fvq_fp8_ffn_workspace_bytes(rows, d, f);
+  if (workspace_bytes < need)
+    return fail(FVQ_EWORKSPACE, "fvq_fp8_ffn: workspace needs %zu bytes, got %zu", need,
+                workspace_bytes);
+  if (!aligned16(x) || !aligned16(y) || !aligned16(workspace))
+    return fail(FVQ_EALIGN, "fvq_fp8_ffn: x, y and workspace must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  Carve c(workspace);
+  uint32_t* row_amax = reinterpret_cast<uint32_t*>(c.take(static_cast<size_t>(rows * 4)));
+  uint8_t* q_x = c.take(static_cast<size_t>(rows * d));
+  float* s_x = reinterpret_cast<float*>(c.take(static_cast<size_t>(rows * 4)));
+  uint16_t* h = reinterpret_cast<uint16_t*>(c.take(static_cast<size_t>(rows * f * 2)));
+  uint8_t* q_h = c.take(static_cast<size_t>(rows * f));
+  float* s_h = reinterpret_cast<float*>(c.take(static_cast<size_t>(rows * 4)));
+  auto mark = [&](int i) {
+    if (ev != nullptr) cudaEventRecord(ev[i], st);
+  };
+  mark(0);
+  // 1. x -> E4M3 with per-row scales; also zeroes the per-row maxima GEMM1 accumulates
+  cudaError_t e = fvq::launch_fp8_row_quant(x, rows, d, q_x, s_x, nullptr, row_amax, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_fp8_ffn quantize(x) launch");
+  mark(1);
+  // 2. h = bf16(gelu(bf16(bf16(acc * s_x * s_w1) + b1))), row_amax = max |h| per row
+  if (int rc = fp8_gemm_impl(q_x, s_x, lin1->qweight, lin1->scale, lin1->bias, h, rows, f, d,
+                             FVQ_EPI_GELU_AMAX, row_amax, st))
+    return rc;
+  mark(2);
+  // 3. h -> E4M3 with per-row scales from row_amax (which it re-zeroes)
+  e = fvq::launch_fp8_row_quant(h, rows, f, q_h, s_h, row_amax, nullptr, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_fp8_ffn quantize(h) launch");
+  mark(3);
+  // 4. y = bf16(bf16(acc * s_h * s_w2) + b2)
+  if (int rc = fp8_gemm_impl(q_h, s_h, lin2->qweight, lin2->scale, lin2->bias, y, rows, d, f,
+                             FVQ_EPI_BF16, nullptr, st))
+    return rc;
+  mark(4);
+  return FVQ_OK;
+}
+
+}  // namespace
+
+int fvq_fp8_ffn(const uint16_t* x, int64_t rows, const fvq_linear_fp8* lin1,
+                const fvq_linear_fp8* lin2, uint16_t* y, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  return fp8_ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes,
+                      static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int fvq_fp8_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear_fp8* lin1,
+                        const fvq_linear_fp8* lin2, uint16_t* y, void* workspace,
+                        size_t workspace_bytes, void* stream, float* kernel_ms) {
+  if (kernel_ms == nullptr) return fail(FVQ_EINVAL, "fvq_fp8_ffn_profile: kernel_ms is NULL");
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaEvent_t ev[5];
+  int made = 0;
+  for (; made < 5; ++made) {
+    if (cudaEventCreate(&ev[made]) != cudaSuccess) break;
+  }
+  int rc = FVQ_OK;
+  if (made < 5) {
+    rc = fail(FVQ_ECUDA, "fvq_fp8_ffn_profile: cudaEventCreate failed");
+  } else {
+    rc = fp8_ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes, st, ev);
+    if (rc == FVQ_OK) {
+      cudaError_t e = cudaEventSynchronize(ev[4]);
+      for (int i = 0; e == cudaSuccess && i < 4; ++i)
+        e = cudaEventElapsedTime(&kernel_ms[i], ev[i], ev[i + 1]);
+      if (e != cudaSuccess) rc = cuda_fail(e, "fvq_fp8_ffn_profile timing");
+    }
+  }
+  for (int i = 0; i < made; ++i) cudaEventDestroy(ev[i]);
+  return rc;
+}
+
+int fvq_div_full_probe(const float* a, const float* b, float* out, int64_t n, void* stream) {
+  if (n < 0 || (n > 0 && (!a || !b || !out))) return fail(FVQ_EINVAL, "fvq_div_full_probe: bad args");
+  if (int rc = check_device()) return rc;
+  cudaError_t e = fvq::launch_div_full_probe(a, b, out, n, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_div_full_probe launch");
+  return FVQ_OK;
+}
+
 int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream) {
   if (n < 0 || (n > 0 && (!in || !out))) return fail(FVQ_EINVAL, "fvq_rcp_approx_probe: bad args");
   if (int rc = check_device()) return rc;

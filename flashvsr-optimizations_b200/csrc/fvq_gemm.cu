@@ -847,6 +847,296 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
 }
 
+// ---------------------------------------------------------------- FP8 GEMM
+// fp8_gemm_kernel: E4M3 x E4M3 with fp32 accumulation (tcgen05.mma.kind::f8f6f4,
+// K = 32 per MMA) and the row-wise scales of torch._scaled_mm (reference
+// ffn_quantization.py:58-60), followed by the bias add of :68-69:
+//   y[m, n] = bf16((acc[m, n] * sa[m]) * sw[n]),  then bf16(y + bias[n])
+// kEpi 1 (the FFN's first linear) also applies GELU-tanh and records each
+// row's max |h| (atomic max of its fp32 bits into row_amax[m]) for the per-row
+// quantizer of the second linear.  CTA layout as in the NVFP4 kernel (warp 0
+// TMA producer, warp 1 TMEM owner and MMA issuer, warps 2-17 epilogue); a
+// stage holds the two code tiles of one 128-deep K tile and nothing else: the
+// scales are per row and per column, applied in the epilogue.
+constexpr int kF8BK = 128;                            // K elements (= bytes) per stage
+constexpr uint32_t kF8TmemCols = 256;                 // the fp32 accumulator only
+template <int kEpi>
+struct F8Plan {
+  static constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
+  static constexpr int kStages = kEpi == 0 ? 4 : 3;
+  static constexpr int kStagingOff = kStages * kStageBytes;
+  static constexpr int kTableOff = kStagingOff + (kEpi == 1 ? kStagingBytes : 0);
+  static constexpr int kBarrierOff = kTableOff + (kEpi == 1 ? kGeluTabBytes : 0);
+  static constexpr int kSmemBytes = kBarrierOff + kBarrierBytes;
+};
+static_assert(F8Plan<0>::kSmemBytes <= 232448, "FP8 GEMM plan exceeds shared memory");
+static_assert(F8Plan<1>::kSmemBytes <= 232448, "FP8 GEMM1 plan exceeds shared memory");
+static_assert(kF8BK == BKB, "an FP8 K tile spans the same 128 bytes per row as an FP4 one");
+
+// Instruction descriptor, kind::f8f6f4: fp32 accumulator (1 at bit 4), A and B
+// E4M3 (format 0 at bits 7 and 10), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t kIdescF8 = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                              (static_cast<uint32_t>(BM >> 4) << 24);
+constexpr uint32_t kIdescF8Half = (1u << 4) | (static_cast<uint32_t>(BN / 2 >> 3) << 17) |
+                                  (static_cast<uint32_t>(BM >> 4) << 24);
+
+// (lo, hi) * (sa, sa) * (sw_lo, sw_hi), two IEEE products per value (mul.rn.f32x2),
+// rounded to a bf16x2 pair.
+__device__ __forceinline__ uint32_t rowcol_scale_pack_bf16x2(uint32_t lo_bits, uint32_t hi_bits,
+                                                             uint64_t sa2, float sw_lo,
+                                                             float sw_hi) {
+  uint64_t v, p, w, q;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo_bits), "r"(hi_bits));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(v), "l"(sa2));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(w) : "f"(sw_lo), "f"(sw_hi));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q) : "l"(p), "l"(w));
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(q));
+  return pack_bf16x2(lo, hi);
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_b,
+                    const __grid_constant__ CUtensorMap tmap_out, const float* __restrict__ sa_rows,
+                    const float* __restrict__ sw_cols, const uint16_t* __restrict__ bias,
+                    uint16_t* __restrict__ out, int m, int n, int k, uint32_t* row_amax,
+                    uint64_t wait_limit) {
+  using P = F8Plan<kEpi>;
+  constexpr int kStages = P::kStages;
+  constexpr int kStageBytes = P::kStageBytes;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicOr(&g_device_error, kErrSmemAlign);
+    return;
+  }
+  auto* bars = reinterpret_cast<Barriers<kStages>*>(smem + P::kBarrierOff);
+  uint8_t* staging = smem + P::kStagingOff;
+  uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + P::kTableOff);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m_blocks = (m + BM - 1) / BM;
+  const int num_n_blocks = n / BN;
+  const int num_k_tiles = k / kF8BK;
+  const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
+  const TileSeq<false, true> seq(num_m_blocks, num_n_blocks);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, kEpiWarps);
+    mbar_init(&bars->teardown, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, kF8TmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && seq.count > 0) {
+      uint32_t armed[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) armed[s] = 0;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int i = 0; i < seq.count && !aborted(bars); ++i) {
+        int mb, nb, half;
+        seq.at(i, mb, nb, half);  // a half tile loads the whole W tile
+        for (int kt = 0; kt < num_k_tiles; ++kt) {
+          if (!mbar_wait_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
+            flag_error(bars, kErrWaitProducer);
+            break;
+          }
+          uint8_t* sa = smem + stage * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          mbar_arrive_expect_tx(&bars->full[stage], kStageBytes);
+          tma_load_2d(sa, &tmap_a, &bars->full[stage], kt * kF8BK, mb * BM);
+          tma_load_2d(sb, &tmap_b, &bars->full[stage], kt * kF8BK, nb * BN);
+          armed[stage] += 1;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      for (int s = 0; s < kStages; ++s) {
+        if (armed[s] > 0 &&
+            !mbar_wait_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit)) {
+          flag_error(bars, kErrWaitTeardown);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && seq.count > 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued_any = false;
+      bool ok = true;
+      for (int i = 0; ok && i < seq.count && !aborted(bars); ++i) {
+        int mb_unused, nb_unused, half;
+        seq.at(i, mb_unused, nb_unused, half);
+        const uint32_t idesc = half < 0 ? kIdescF8 : kIdescF8Half;
+        const uint32_t b_off = half > 0 ? static_cast<uint32_t>(kBBytes / 2) : 0u;
+        if (!mbar_wait_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
+                               wait_limit)) {
+          flag_error(bars, kErrWaitMma);
+          break;
+        }
+        tc_fence_after();
+        for (int kt = 0; kt < num_k_tiles; ++kt) {
+          if (!mbar_wait_bounded(&bars->full[stage], phase, wait_limit)) {
+            flag_error(bars, kErrWaitMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* sa = smem + stage * kStageBytes;
+          uint8_t* sb = sa + kABytes;
+          const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
+          const uint64_t bdesc = make_smem_desc(smem_u32(sb) + b_off, 16, 1024, 2);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // 32-byte K steps inside the 128B swizzle atom
+            mma_f8(tmem, adesc + static_cast<uint64_t>(2 * j), bdesc + static_cast<uint64_t>(2 * j),
+                   idesc, (kt > 0 || j > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          tc_commit(&bars->empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&bars->acc_full);
+      }
+      if (aborted(bars) && issued_any) {
+        tc_commit(&bars->teardown);
+        if (!mbar_wait_bounded(&bars->teardown, 0, teardown_limit))
+          flag_error(bars, kErrWaitTeardown);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // Warp w: TMEM lanes 32*(w%4).. and columns [64*q, 64*q+64), q = (w-2)/4,
+    // as in the NVFP4 kernel.  The accumulator slice is pulled into registers
+    // and TMEM released before any scaling, so the next tile's MMAs overlap it.
+    const int quad = warp & 3;
+    const int quarter = (warp - 2) >> 2;
+    const int col_base = quarter * 64;
+    const int trow = quad * 32 + lane;
+    if constexpr (kEpi == 1) {
+      gelu_table_init(gelu_tab, threadIdx.x - 64, kEpiThreads);
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+    }
+    const uint32_t tab_base = smem_u32(gelu_tab);
+    uint8_t* warp_staging = staging + (warp - 2) * kWarpStagingBytes;
+    for (int i = 0; i < seq.count; ++i) {
+      int mb, nb, half;
+      seq.at(i, mb, nb, half);
+      const int row = mb * BM + trow;
+      const float sa = row < m ? __ldg(sa_rows + row) : 0.0f;
+      if (!mbar_wait_bounded(&bars->acc_full, static_cast<uint32_t>(i) & 1u, wait_limit)) {
+        flag_error(bars, kErrWaitEpilogue);
+        break;
+      }
+      tc_fence_after();
+      if (half >= 0 && quarter >= 2) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->acc_empty);
+        continue;
+      }
+      uint32_t r[64];
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + col_base;
+      tmem_ld_32x32b_x32(taddr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty);
+      uint64_t sa2;
+      asm("mov.b64 %0, {%1, %1};" : "=l"(sa2) : "f"(sa));
+      const int col0 = nb * BN + (half > 0 ? BN / 2 : 0) + col_base;
+      const float4* sw4 = reinterpret_cast<const float4*>(sw_cols + col0);
+      if constexpr (kEpi == 1) {
+        if (lane == 0) bulk_wait_group_read0();  // previous store has read the staging
+        __syncwarp();
+        const uint4* bias4 = reinterpret_cast<const uint4*>(bias + col0);
+        uint32_t tile_max = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 s0 = __ldg(sw4 + 2 * q), s1 = __ldg(sw4 + 2 * q + 1);
+          const float sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+          uint4 bv = make_uint4(0, 0, 0, 0);
+          if (bias != nullptr) bv = __ldg(bias4 + q);
+          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t hv = rowcol_scale_pack_bf16x2(r[8 * q + 2 * j], r[8 * q + 2 * j + 1], sa2,
+                                                   sw[2 * j], sw[2 * j + 1]);
+            if (bias != nullptr) hv = add_bf16x2(hv, bw[j]);
+            hv = gelu_bf16x2(hv, tab_base, gelu_tab);
+            tile_max = max_u16x2(tile_max, hv & 0x7FFF7FFFu);
+            o[j] = hv;
+          }
+          *reinterpret_cast<uint4*>(warp_staging + lane * kStageRowBytes + ((q ^ (lane & 7)) * 16)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        const uint32_t mag = max(tile_max & 0xFFFFu, tile_max >> 16);
+        if (row < m && mag != 0) atomicMax(row_amax + row, mag << 16);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_out, warp_staging, col0, mb * BM + quad * 32);
+          bulk_commit_group();
+        }
+      } else {
+        uint16_t* dst = out + static_cast<int64_t>(row) * n + col0;
+#pragma unroll
+        for (int c = 0; c < 64; c += 8) {
+          const float4 s0 = __ldg(sw4 + c / 4), s1 = __ldg(sw4 + c / 4 + 1);
+          const float sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+          uint4 bv = make_uint4(0, 0, 0, 0);
+          if (bias != nullptr) bv = __ldg(reinterpret_cast<const uint4*>(bias + col0 + c));
+          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t w = rowcol_scale_pack_bf16x2(r[c + 2 * j], r[c + 2 * j + 1], sa2, sw[2 * j],
+                                                  sw[2 * j + 1]);
+            if (bias != nullptr) w = add_bf16x2(w, bw[j]);
+            o[j] = w;
+          }
+          if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+    if (kEpi == 1 && lane == 0) bulk_wait_group0();  // stores complete before the CTA exits
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kF8TmemCols);
+}
+
 // GELU of bf16 values through the epilogue's path (test support): values
 // 2i and 2i+1 form one bf16x2 word, as in the epilogue; an odd last value
 // goes through the single-value path.
@@ -889,19 +1179,25 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 2-D map over an FP4 code matrix [rows, k/2 bytes], box = box_rows x 128 bytes, 128B swizzle.
-bool make_code_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t k,
+// 2-D map over a byte matrix [rows, row_bytes], box = box_rows x 128 bytes, 128B swizzle.
+bool make_byte_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t row_bytes,
                    uint32_t box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k / 2), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k / 2)};
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(BKB), box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// FP4 codes [rows, k/2 bytes]
+bool make_code_map(CUtensorMap* map, const uint8_t* base, int64_t rows, int64_t k,
+                   uint32_t box_rows) {
+  return make_byte_map(map, base, rows, k / 2, box_rows);
 }
 
 // 2-D map over a bf16 output [rows, n], box = 32 rows x 64 columns (128 B), 128B swizzle.
@@ -1000,7 +1296,53 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
                             out, m, n, k, wait_limit);
 }
 
+template <int kEpi>
+cudaError_t launch_fp8_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
+                              const float* sa, const float* sw, const uint16_t* bias, uint16_t* out,
+                              int m, int n, int k, uint32_t* row_amax, uint64_t wait_limit,
+                              cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  constexpr int kSmemBytes = F8Plan<kEpi>::kSmemBytes;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<kEpi>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int tiles = ((m + BM - 1) / BM) * (n / BN);
+  int grid = sm_count();
+  if (grid > tiles) grid = tiles;
+  fp8_gemm_kernel<kEpi><<<grid, kNumThreads, kSmemBytes, st>>>(ma, mb, mo, sa, sw, bias, out, m, n,
+                                                                k, row_amax, wait_limit);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w, const float* sw,
+                            const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
+                            int epilogue, uint32_t* row_amax, uint64_t wait_limit, cudaStream_t st,
+                            const char** why) {
+  alignas(64) CUtensorMap ma;
+  alignas(64) CUtensorMap mb;
+  if (!make_byte_map(&ma, a, m, k, BM) || !make_byte_map(&mb, w, n, k, BN)) {
+    if (why) *why = "cuTensorMapEncodeTiled failed for the E4M3 operands";
+    return cudaErrorInvalidValue;
+  }
+  alignas(64) CUtensorMap mo;
+  std::memset(&mo, 0, sizeof(mo));
+  const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
+  if (epilogue == 1) {
+    if (!make_out_map(&mo, out, m, n)) {
+      if (why) *why = "cuTensorMapEncodeTiled failed for the output";
+      return cudaErrorInvalidValue;
+    }
+    return launch_fp8_gemm_t<1>(ma, mb, mo, sa, sw, bias, out, mi, ni, ki, row_amax, wait_limit, st);
+  }
+  return launch_fp8_gemm_t<0>(ma, mb, mo, sa, sw, bias, out, mi, ni, ki, nullptr, wait_limit, st);
+}
 
 // GEMMs with replicated W scales and m % 256 == 0 run on SM pairs when enabled
 // (off by default: measured at the one-SM kernel's speed, both clock-limited by

@@ -74,6 +74,25 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
 void set_gemm_pairing(bool enabled);
 bool gemm_pairs(int64_t m, int epilogue);
 cudaError_t launch_gelu_probe(const uint16_t* in, uint16_t* out, int64_t count, cudaStream_t st);
+// E4M3 GEMM with per-row A scales and per-column W scales (fvq_gemm.cu); epilogue 1:
+// bias, GELU and per-row max |h| (fp32 bits) into row_amax.  k % 128 == 0, n % 256 == 0.
+cudaError_t launch_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w, const float* sw,
+                            const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
+                            int epilogue, uint32_t* row_amax, uint64_t wait_limit, cudaStream_t st,
+                            const char** why);
+
+// FP8 quantizers (fvq_fp8.cu).  Row: one scale per row, k % 8 == 0 and
+// k <= fp8_row_quant_max_k(); row_amax != NULL supplies each row's max |x| and is
+// zeroed; zero_rows != NULL gets zero in each row's word.  Tensor: one scale from a
+// device amax.
+int64_t fp8_row_quant_max_k();
+cudaError_t launch_fp8_row_quant(const uint16_t* x, int64_t rows, int64_t k, uint8_t* q,
+                                 float* scale, uint32_t* row_amax, uint32_t* zero_rows,
+                                 cudaStream_t st);
+cudaError_t launch_fp8_tensor_quant(const uint16_t* x, int64_t numel, const float* amax,
+                                    uint8_t* q, float* scale, cudaStream_t st);
+cudaError_t launch_div_full_probe(const float* a, const float* b, float* out, int64_t n,
+                                  cudaStream_t st);
 cudaError_t set_error_word(uint32_t v, cudaStream_t st);
 uint32_t* error_word_ptr();   // device address of the error word (current device)
 cudaError_t read_error_word(uint32_t* v, cudaStream_t st);

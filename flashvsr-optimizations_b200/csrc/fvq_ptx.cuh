@@ -274,6 +274,18 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64
       : "memory");
 }
 
+// D (+)= A * B^T with E4M3 (or other 8/6/4-bit) operands named by `idesc`,
+// no block scales; K = 32 per instruction.
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Copy 32 rows x 16 bytes from shared memory into TMEM lanes 0-31, replicated
 // to the four 32-lane sub-partitions (4 columns of 32 bits).
 __device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {

@@ -1,4 +1,4 @@
-"""Drop-in replacement of the reference's ``ffn_quantization.py`` NVFP4 path.
+"""Drop-in replacement of the reference's ``ffn_quantization.py`` (NVFP4 and FP8 modes).
 
 Same plugin API as the reference (ffn_quantization.py:35-86):
 
@@ -11,16 +11,18 @@ Same plugin API as the reference (ffn_quantization.py:35-86):
   ``ffn[2]`` and returns the same metadata dict.
 
 Additionally ``install_ffn`` (``fused=True``, the default) replaces each
-block's ``ffn`` ``nn.Sequential`` by :class:`NVFP4FFN`, a subclass that keeps
-the same children (``[0]`` and ``[2]`` are the ``QuantLinear`` modules, ``[1]``
-the GELU) but runs the whole Linear-GELU-Linear chain as one call into the
-library, with GELU and the intermediate's amax computed in GEMM1's epilogue.
-Its result follows the reference's roundings and global scales exactly.
+block's ``ffn`` ``nn.Sequential`` by :class:`NVFP4FFN` (or :class:`FP8FFN`), a
+subclass that keeps the same children (``[0]`` and ``[2]`` are the
+``QuantLinear`` modules, ``[1]`` the GELU) but runs the whole
+Linear-GELU-Linear chain as one call into the library, with GELU and the
+intermediate's amax (per tensor for NVFP4, per row for FP8) computed in
+GEMM1's epilogue.  Its result follows the reference's roundings and scales
+exactly.
 
-Modes: ``'nvfp4'`` (this path), ``'bf16'`` (no swap).  ``'fp8'`` is the
-reference's W8A8 adapter, which this library does not implement: it raises
-``NotImplementedError``.  Any other mode raises ``ValueError(mode)`` like the
-reference (ffn_quantization.py:50).
+Modes: ``'nvfp4'`` (E2M1 W4A4, ffn_quantization.py:47-48, :62-67), ``'fp8'``
+(E4M3 W8A8 with per-row scales, :44-46, :57-60), ``'bf16'`` (no swap).  Any
+other mode raises ``ValueError(mode)`` like the reference
+(ffn_quantization.py:50).
 """
 from __future__ import annotations
 
@@ -28,12 +30,17 @@ import torch
 
 from . import ops
 
-__all__ = ["global_scale", "QuantLinear", "NVFP4FFN", "install_ffn"]
+__all__ = ["global_scale", "row_quant", "QuantLinear", "NVFP4FFN", "FP8FFN", "install_ffn"]
 
 
 def global_scale(x: torch.Tensor) -> torch.Tensor:
     """ffn_quantization.py:29-32."""
     return ops.global_scale(x.contiguous())
+
+
+def row_quant(x: torch.Tensor):
+    """ffn_quantization.py:22-26: (float8_e4m3fn [M, K], fp32 [M, 1] row scales)."""
+    return ops.fp8_row_quant(x.contiguous())
 
 
 def _quantize_weight(w: torch.Tensor):
@@ -44,7 +51,8 @@ def _quantize_weight(w: torch.Tensor):
 
 
 class QuantLinear(torch.nn.Module):
-    """NVFP4 W4A4 replacement of one ``nn.Linear`` (ffn_quantization.py:35-70)."""
+    """W4A4 (``'nvfp4'``) or W8A8 (``'fp8'``) replacement of one ``nn.Linear``
+    (ffn_quantization.py:35-70)."""
 
     def __init__(self, linear: torch.nn.Linear, mode: str):
         super().__init__()
@@ -53,17 +61,16 @@ class QuantLinear(torch.nn.Module):
         self.in_features = linear.in_features
         bias = linear.bias.detach().clone().to(torch.bfloat16) if linear.bias is not None else None
         self.register_buffer("bias", bias)
-        if mode == "fp8":
-            raise NotImplementedError(
-                "QuantLinear(mode='fp8') (the reference's W8A8 adapter) is not implemented by "
-                "this NVFP4 library")
-        if mode != "nvfp4":
+        if mode not in ("fp8", "nvfp4"):
             raise ValueError(mode)
         w = linear.weight
         if not w.is_cuda:
             raise RuntimeError("QuantLinear: the weight must be on a CUDA device (no CPU path)")
-        q, s, g = _quantize_weight(w)
-        self.register_buffer("global_sf", g)
+        if mode == "fp8":
+            q, s = row_quant(w.detach().to(torch.bfloat16))
+        else:
+            q, s, g = _quantize_weight(w)
+            self.register_buffer("global_sf", g)
         self.register_buffer("qweight", q)
         self.register_buffer("scale", s)
 
@@ -87,7 +94,10 @@ class QuantLinear(torch.nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).contiguous()
-        out = ops.nvfp4_linear(x2, self.qweight, self.scale, self.global_sf, self.bias)
+        if self.mode == "fp8":
+            out = ops.fp8_linear(x2, self.qweight, self.scale, self.bias)
+        else:
+            out = ops.nvfp4_linear(x2, self.qweight, self.scale, self.global_sf, self.bias)
         return out.reshape(*shape[:-1], self.out_features)
 
     def extra_repr(self) -> str:
@@ -116,6 +126,32 @@ class NVFP4FFN(torch.nn.Sequential):
         return y.reshape(*shape[:-1], l2.out_features)
 
 
+class FP8FFN(torch.nn.Sequential):
+    """``nn.Sequential(QuantLinear('fp8'), GELU(tanh), QuantLinear('fp8'))`` run as one fused call.
+
+    Same contract as :class:`NVFP4FFN`: the children and state-dict keys of
+    the Sequential it replaces, and exactly the result of running them one
+    after another (four kernel launches instead of seven).
+    """
+
+    def __init__(self, lin1: QuantLinear, act: torch.nn.Module, lin2: QuantLinear):
+        super().__init__(lin1, act, lin2)
+        if lin1.mode != "fp8" or lin2.mode != "fp8":
+            raise ValueError("FP8FFN: both linears must be QuantLinear(mode='fp8')")
+        if lin1.out_features != lin2.in_features or lin2.out_features != lin1.in_features:
+            raise ValueError("FP8FFN: linear shapes do not chain")
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        l1, l2 = self[0], self[2]
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        y = ops.fp8_ffn(x2, l1.qweight, l1.scale, l1.bias, l2.qweight, l2.scale, l2.bias)
+        return y.reshape(*shape[:-1], l2.out_features)
+
+
+_FUSED = {"nvfp4": NVFP4FFN, "fp8": FP8FFN}
+
+
 def _is_gelu_tanh(m: torch.nn.Module) -> bool:
     return isinstance(m, torch.nn.GELU) and getattr(m, "approximate", "none") == "tanh"
 
@@ -130,15 +166,16 @@ def install_ffn(pipe, mode: str, fused: bool = True) -> dict:
             for idx in (0, 2):
                 block.ffn[idx] = QuantLinear(block.ffn[idx], mode)
                 count += 1
-            if fused and mode == "nvfp4" and len(block.ffn) == 3 and _is_gelu_tanh(block.ffn[1]):
-                block.ffn = NVFP4FFN(block.ffn[0], block.ffn[1], block.ffn[2])
+            if fused and len(block.ffn) == 3 and _is_gelu_tanh(block.ffn[1]):
+                block.ffn = _FUSED[mode](block.ffn[0], block.ffn[1], block.ffn[2])
                 fused_blocks += 1
     after = sum(t.numel() * t.element_size() for b in pipe.dit.blocks
                 for t in list(b.ffn.parameters()) + list(b.ffn.buffers()))
     return {
         "mode": mode, "quantized_linears": count, "ffn_bytes_before": before,
         "ffn_bytes_after": after,
-        "fp8": "E4M3 per-row W8A8; torch._scaled_mm; FP32 accumulation; BF16 output",
+        "fp8": ("E4M3 per-row W8A8; sm_100a tcgen05 kind::f8f6f4 GEMM with row-wise scales "
+                "(libfvq); FP32 accumulation; BF16 output"),
         "nvfp4": ("E2M1 W4A4; 16-element E4M3 scales + dynamic tensor FP32 scale; sm_100a "
                   "tcgen05 block-scaled GEMM (libfvq); BF16 output"),
         "scope": "Only dit.blocks.*.ffn.{0,2}; GELU, bias, attention, conditioning, decoder remain BF16",

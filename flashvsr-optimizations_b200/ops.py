@@ -1,4 +1,4 @@
-"""torch-facing NVFP4 operators over the C ABI (libfvq.so).
+"""torch-facing NVFP4 and FP8 operators over the C ABI (libfvq.so).
 
 Each function mirrors one call of the reference path and is registered as a
 ``torch.library`` custom op (namespace ``fvq``) with a fake implementation, so
@@ -22,6 +22,8 @@ from . import _lib
 __all__ = [
     "amax", "global_scale", "nvfp4_quantize", "mm_fp4", "nvfp4_gemm",
     "nvfp4_linear", "nvfp4_ffn", "rcp_approx_probe", "sf_rows", "read_device_error",
+    "fp8_row_quant", "fp8_quantize_activation", "fp8_scaled_mm", "fp8_linear", "fp8_ffn",
+    "div_full_probe",
 ]
 
 
@@ -79,10 +81,18 @@ class _Workspaces:
 
 
 _WS = _Workspaces()
+# Scratch with no zero-state protocol (the FP8 linear and FFN carve their
+# intermediates from it); kept apart from _WS, whose leading amax counters the
+# NVFP4 calls rely on staying zero.
+_SCRATCH = _Workspaces()
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     return _WS.get(device, nbytes)
+
+
+def scratch(device: torch.device, nbytes: int) -> torch.Tensor:
+    return _SCRATCH.get(device, nbytes)
 
 
 # ---------------------------------------------------------------- custom ops
@@ -251,6 +261,191 @@ def nvfp4_ffn(x: torch.Tensor, q1: torch.Tensor, s1: torch.Tensor, g1: torch.Ten
 @nvfp4_ffn.register_fake
 def _(x, q1, s1, g1, b1, q2, s2, g2, b2):
     return x.new_empty(x.shape, dtype=torch.bfloat16)
+
+
+# ---------------------------------------------------------------- FP8 (W8A8) mode
+def _check_fp8(name: str, *ts: torch.Tensor) -> None:
+    for t in ts:
+        if t.dtype != torch.float8_e4m3fn:
+            raise TypeError(f"{name}: expected float8_e4m3fn codes, got {t.dtype}")
+
+
+def _dense(x: torch.Tensor) -> bool:
+    """True when x's elements fill its storage span without gaps or overlaps
+    (any permutation of a contiguous layout, channels_last included), so
+    empty_like(x) has the same strides and both can be walked in memory order."""
+    if x.is_contiguous():
+        return True
+    dims = sorted((st, sz) for st, sz in zip(x.stride(), x.shape) if sz != 1)
+    expect = 1
+    for st, sz in dims:
+        if st != expect:
+            return False
+        expect *= sz
+    return True
+
+
+def _aligned16(x: torch.Tensor) -> torch.Tensor:
+    x = x.contiguous()
+    return x if x.data_ptr() % 16 == 0 else x.clone()
+
+
+@torch.library.custom_op("fvq::fp8_row_quant", mutates_args=())
+def fp8_row_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(q float8_e4m3fn [M, K], scale fp32 [M, 1]) -- the reference's row_quant
+    (ffn_quantization.py:22-26): scale = max(max|x_row| / 448, 1e-12), q = x / scale."""
+    _check_cuda("fp8_row_quant", x)
+    _check_bf16("fp8_row_quant", x)
+    if x.dim() != 2:
+        raise ValueError("fp8_row_quant: expected a 2-D [M, K] tensor")
+    m, k = x.shape
+    x = _aligned16(x)
+    q = torch.empty((m, k), dtype=torch.float8_e4m3fn, device=x.device)
+    scale = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    if m > 0:
+        _lib.call("fvq_fp8_row_quantize", _ptr(x), m, k, _ptr(q), _ptr(scale), _stream(x))
+    return q, scale
+
+
+@fp8_row_quant.register_fake
+def _(x):
+    m, k = x.shape
+    return (x.new_empty((m, k), dtype=torch.float8_e4m3fn),
+            x.new_empty((m, 1), dtype=torch.float32))
+
+
+@torch.library.custom_op("fvq::fp8_quantize_activation", mutates_args=())
+def fp8_quantize_activation(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(q float8_e4m3fn like x, scale fp32 [1]) with one scale for the whole tensor --
+    decoder_fp8.py:17-24 (and lq_fp8.py:24-31): scale = max(amax / 448, 1e-12),
+    q = clamp(x / scale, -448, 448).  x may be in any dense memory format
+    (channels_last included); q keeps it."""
+    _check_cuda("fp8_quantize_activation", x)
+    _check_bf16("fp8_quantize_activation", x)
+    if x.numel() == 0:
+        raise RuntimeError("fp8_quantize_activation: empty tensor (the reference's amax of no "
+                           "partials fails)")
+    if not _dense(x):
+        x = x.contiguous()
+    q = torch.empty_like(x, dtype=torch.float8_e4m3fn)
+    if x.data_ptr() % 16 != 0 or q.data_ptr() % 8 != 0:
+        x = x.clone()
+        q = torch.empty_like(x, dtype=torch.float8_e4m3fn)
+    scale = torch.empty(1, dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    ws = workspace(x.device, lib.fvq_fp8_tensor_quantize_workspace_bytes())
+    _lib.call("fvq_fp8_tensor_quantize", _ptr(x), x.numel(), _ptr(q), _ptr(scale), _ptr(ws),
+              ws.numel(), _stream(x))
+    return q, scale
+
+
+@fp8_quantize_activation.register_fake
+def _(x):
+    return torch.empty_like(x, dtype=torch.float8_e4m3fn), x.new_empty(1, dtype=torch.float32)
+
+
+@torch.library.custom_op("fvq::fp8_scaled_mm", mutates_args=())
+def fp8_scaled_mm(a: torch.Tensor, scale_a: torch.Tensor, w: torch.Tensor, scale_w: torch.Tensor,
+                  bias: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16((A @ W^T) * scale_a * scale_w) [+ bias] with E4M3 operands.
+
+    The reference calls ``torch._scaled_mm(q, qweight.t(), scale_a=s,
+    scale_b=scale.t(), out_dtype=bf16, use_fast_accum=False)``
+    (ffn_quantization.py:58-60); here W is given in its stored [N, K] layout and
+    the scales as [M, 1] / [N, 1] (or flat)."""
+    _check_cuda("fp8_scaled_mm", a, scale_a, w, scale_w, bias)
+    _check_fp8("fp8_scaled_mm", a, w)
+    m, k = a.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"fp8_scaled_mm: K mismatch ({k} vs {w.shape[1]})")
+    sa = scale_a.to(torch.float32).reshape(-1).contiguous()
+    sw = _aligned16(scale_w.to(torch.float32).reshape(-1))
+    if sa.numel() != m or sw.numel() != n:
+        raise ValueError("fp8_scaled_mm: expected one scale per row of A and per row of W")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    _lib.call("fvq_fp8_scaled_mm", _ptr(_aligned16(a)), _ptr(sa), _ptr(_aligned16(w)), _ptr(sw),
+              _ptr(None if bias is None else _aligned16(bias)), _ptr(out), m, n, k, _stream(a))
+    return out
+
+
+@fp8_scaled_mm.register_fake
+def _(a, scale_a, w, scale_w, bias=None):
+    return a.new_empty((a.shape[0], w.shape[0]), dtype=torch.bfloat16)
+
+
+def _fp8_linear_struct(qweight, scale, bias, in_f, out_f) -> _lib.FvqLinearFp8:
+    return _lib.FvqLinearFp8(_ptr(qweight), _ptr(scale), _ptr(bias), in_f, out_f)
+
+
+def _fp8_weight_args(name, qweight, scale, bias):
+    _check_fp8(name, qweight)
+    return (_aligned16(qweight), _aligned16(scale.to(torch.float32).reshape(-1)),
+            None if bias is None else _aligned16(bias))
+
+
+@torch.library.custom_op("fvq::fp8_linear", mutates_args=())
+def fp8_linear(x: torch.Tensor, qweight: torch.Tensor, scale: torch.Tensor,
+               bias: torch.Tensor | None = None) -> torch.Tensor:
+    """QuantLinear.forward in mode 'fp8' (ffn_quantization.py:54-60, :68-70) on a 2-D bf16 input."""
+    _check_cuda("fp8_linear", x, qweight, scale, bias)
+    _check_bf16("fp8_linear", x)
+    m, k = x.shape
+    n = qweight.shape[0]
+    if m == 0:
+        return x.new_empty((0, n))
+    x = _aligned16(x)
+    qweight, scale, bias = _fp8_weight_args("fp8_linear", qweight, scale, bias)
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    lib = _lib.load()
+    ws = scratch(x.device, lib.fvq_fp8_linear_workspace_bytes(m, k))
+    lin = _fp8_linear_struct(qweight, scale, bias, k, n)
+    _lib.call("fvq_fp8_linear", _ptr(x), m, ctypes.byref(lin), _ptr(y), _ptr(ws), ws.numel(),
+              _stream(x))
+    return y
+
+
+@fp8_linear.register_fake
+def _(x, qweight, scale, bias=None):
+    return x.new_empty((x.shape[0], qweight.shape[0]), dtype=torch.bfloat16)
+
+
+@torch.library.custom_op("fvq::fp8_ffn", mutates_args=())
+def fp8_ffn(x: torch.Tensor, q1: torch.Tensor, s1: torch.Tensor, b1: torch.Tensor | None,
+            q2: torch.Tensor, s2: torch.Tensor, b2: torch.Tensor | None) -> torch.Tensor:
+    """Linear -> GELU-tanh -> Linear in mode 'fp8', as the reference's QuantLinear modules compute it."""
+    _check_cuda("fp8_ffn", x, q1, s1, b1, q2, s2, b2)
+    _check_bf16("fp8_ffn", x)
+    m, d = x.shape
+    f = q1.shape[0]
+    if m == 0:
+        return x.new_empty((0, d))
+    x = _aligned16(x)
+    q1, s1, b1 = _fp8_weight_args("fp8_ffn", q1, s1, b1)
+    q2, s2, b2 = _fp8_weight_args("fp8_ffn", q2, s2, b2)
+    y = torch.empty((m, d), dtype=torch.bfloat16, device=x.device)
+    lib = _lib.load()
+    ws = scratch(x.device, lib.fvq_fp8_ffn_workspace_bytes(m, d, f))
+    l1 = _fp8_linear_struct(q1, s1, b1, d, f)
+    l2 = _fp8_linear_struct(q2, s2, b2, f, d)
+    _lib.call("fvq_fp8_ffn", _ptr(x), m, ctypes.byref(l1), ctypes.byref(l2), _ptr(y), _ptr(ws),
+              ws.numel(), _stream(x))
+    return y
+
+
+@fp8_ffn.register_fake
+def _(x, q1, s1, b1, q2, s2, b2):
+    return x.new_empty(x.shape, dtype=torch.bfloat16)
+
+
+def div_full_probe(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """div.full.f32(a, b) elementwise on the GPU, the FP8 quantizers' division (test support)."""
+    _check_cuda("div_full_probe", a, b)
+    a = a.to(torch.float32).contiguous()
+    b = b.to(torch.float32).expand_as(a).contiguous()
+    out = torch.empty_like(a)
+    _lib.call("fvq_div_full_probe", _ptr(a), _ptr(b), _ptr(out), a.numel(), _stream(a))
+    return out
 
 
 # ---------------------------------------------------------------- support

@@ -198,6 +198,98 @@ int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin
                           size_t workspace_bytes, void* stream, float* kernel_ms);
 
 /*
+ * ---------------------------------------------------------------------------
+ * FP8 (E4M3) W8A8 mode: the reference's QuantLinear(mode='fp8')
+ * (ffn_quantization.py:6-13, :22-26, :45-46, :57-60) and its per-tensor
+ * activation quantizer (decoder_fp8.py:9-24, shared by lq_fp8.py:24-31).
+ *
+ * E4M3 tensors are uint8 bytes of float8_e4m3fn values, row-major.  Row
+ * scales are fp32, one per row ([rows] -- the reference's [rows, 1]).  The
+ * reference divides with Triton's fp32 `/` (div.full.f32 on the GPU); these
+ * kernels issue the same instruction.
+ * ---------------------------------------------------------------------------
+ */
+
+/*
+ * Per-row quantization, the reference's row_quant(x) (ffn_quantization.py:22-26,
+ * Triton _row_quant :6-13):
+ *   scale[r] = max(max_k |x[r,k]| / 448, 1e-12);  q[r,k] = e4m3_rn_satfinite(x[r,k] / scale[r])
+ * k % 8 == 0 and k <= 16384; x and q 16-byte aligned.
+ */
+int fvq_fp8_row_quantize(const uint16_t* x, int64_t rows, int64_t k, uint8_t* q, float* scale,
+                         void* stream);
+
+/*
+ * Per-tensor quantization, the reference's quantize_activation(x)
+ * (decoder_fp8.py:17-24, and FP8Conv3d.quantize, lq_fp8.py:24-31): the amax of
+ * _partial_amax (the same kernel as fvq_amax), scale = max(amax / 448, 1e-12)
+ * evaluated as torch does (amax times the fp32 reciprocal of 448) and written
+ * to *scale, then
+ *   q = e4m3(min(max(x / scale, -448), 448))
+ * over `numel` elements in memory order (any dense layout, channels_last
+ * included).  The workspace (fvq_fp8_tensor_quantize_workspace_bytes) must be
+ * zeroed once before its first use; every call leaves it zeroed again.
+ * x 16-byte aligned, q 8-byte aligned.
+ */
+size_t fvq_fp8_tensor_quantize_workspace_bytes(void);
+int fvq_fp8_tensor_quantize(const uint16_t* x, int64_t numel, uint8_t* q, float* scale,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * E4M3 GEMM on tcgen05 tensor cores (kind::f8f6f4) with row-wise scales:
+ *   out[m, n] = bf16((sum_k A[m,k] W[n,k]) * scale_a[m] * scale_w[n]),  then
+ *   out = bf16(out + bias[n]) if bias
+ * Replaces torch._scaled_mm(q, qweight.t(), scale_a=s, scale_b=scale.t(),
+ * out_dtype=bf16, use_fast_accum=False) and the bias add that follows it
+ * (ffn_quantization.py:58-60, :68-69).  A [m, k], W [n, k] (the nn.Linear
+ * layout).  n % 256 == 0, k % 128 == 0, k <= 16384.
+ */
+int fvq_fp8_scaled_mm(const uint8_t* a, const float* scale_a, const uint8_t* w,
+                      const float* scale_w, const uint16_t* bias, uint16_t* out, int64_t m,
+                      int64_t n, int64_t k, void* stream);
+
+/* One nn.Linear replaced by QuantLinear(linear, 'fp8') (ffn_quantization.py:45-46). */
+typedef struct fvq_linear_fp8 {
+  const uint8_t* qweight;   /* E4M3 [out_features, in_features] */
+  const float* scale;       /* fp32 [out_features], the weight's row scales */
+  const uint16_t* bias;     /* bf16 [out_features] or NULL */
+  int64_t in_features;
+  int64_t out_features;
+} fvq_linear_fp8;
+
+/* QuantLinear.forward in mode 'fp8': y = bias + scaled_mm(row_quant(x), W). */
+size_t fvq_fp8_linear_workspace_bytes(int64_t rows, int64_t in_features);
+int fvq_fp8_linear(const uint16_t* x, int64_t rows, const fvq_linear_fp8* lin, uint16_t* y,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The whole FFN in mode 'fp8': y = QuantLinear2(bf16(gelu_tanh(QuantLinear1(x))))
+ * with the reference's row scales and roundings.  GELU and the per-row max |h|
+ * the second row quantizer needs are computed in GEMM1's epilogue.  Four
+ * launches; the workspace needs no initialisation.
+ */
+size_t fvq_fp8_ffn_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff);
+int fvq_fp8_ffn(const uint16_t* x, int64_t rows, const fvq_linear_fp8* lin1,
+                const fvq_linear_fp8* lin2, uint16_t* y, void* workspace, size_t workspace_bytes,
+                void* stream);
+
+/*
+ * Instrumentation with no reference counterpart: fvq_fp8_ffn with CUDA events
+ * around its four launches (quantize x, GEMM1 + bias + GELU + row maxima,
+ * quantize h, GEMM2 + bias); synchronises and writes the four device times in
+ * milliseconds to kernel_ms[0..3].
+ */
+int fvq_fp8_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear_fp8* lin1,
+                        const fvq_linear_fp8* lin2, uint16_t* y, void* workspace,
+                        size_t workspace_bytes, void* stream, float* kernel_ms);
+
+/*
+ * Test support: out[i] = div.full.f32(a[i], b[i]) on the device, the division
+ * the FP8 quantizers (and the reference's Triton `/`) use.
+ */
+int fvq_div_full_probe(const float* a, const float* b, float* out, int64_t n, void* stream);
+
+/*
  * Test support: out[i] = rcp.approx.ftz.f32(in[i]) on the device, the
  * reciprocal the quantizer uses (so a CPU checker can use measured values).
  */

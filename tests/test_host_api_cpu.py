@@ -36,9 +36,11 @@ def test_unknown_mode_raises_value_error():
         QuantLinear(torch.nn.Linear(256, 256), "int3")
 
 
-def test_fp8_mode_is_explicitly_unsupported():
-    with pytest.raises(NotImplementedError):
+def test_fp8_on_cpu_weights_raises_instead_of_falling_back():
+    with pytest.raises(RuntimeError):
         QuantLinear(torch.nn.Linear(256, 256), "fp8")
+    with pytest.raises(RuntimeError):
+        install_ffn(_Pipe(), "fp8")
 
 
 def test_nvfp4_on_cpu_weights_raises_instead_of_falling_back():
@@ -52,6 +54,10 @@ def test_ops_reject_cpu_tensors():
         ops.global_scale(x)
     with pytest.raises(RuntimeError):
         ops.nvfp4_quantize(x, torch.ones(1))
+    with pytest.raises(RuntimeError):
+        ops.fp8_row_quant(x)
+    with pytest.raises(RuntimeError):
+        ops.fp8_quantize_activation(x)
 
 
 def test_custom_ops_registered_with_fake_kernels():
@@ -65,3 +71,19 @@ def test_custom_ops_registered_with_fake_kernels():
                                     torch.empty(1536, 4480, dtype=torch.uint8),
                                     torch.empty(1536, 560, dtype=torch.uint8), torch.empty(1), None)
         assert y.shape == (300, 1536) and y.dtype == torch.bfloat16
+
+
+def test_fp8_custom_ops_have_fake_kernels():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        x = torch.empty(300, 1536, dtype=torch.bfloat16)
+        q, s = torch.ops.fvq.fp8_row_quant(x)
+        assert q.shape == (300, 1536) and q.dtype == torch.float8_e4m3fn and s.shape == (300, 1)
+        y = torch.ops.fvq.fp8_ffn(x, torch.empty(8960, 1536, dtype=torch.float8_e4m3fn),
+                                  torch.empty(8960, 1), None,
+                                  torch.empty(1536, 8960, dtype=torch.float8_e4m3fn),
+                                  torch.empty(1536, 1), None)
+        assert y.shape == (300, 1536) and y.dtype == torch.bfloat16
+        z = torch.empty(2, 16, 8, 8, dtype=torch.bfloat16).to(memory_format=torch.channels_last)
+        qz, sz = torch.ops.fvq.fp8_quantize_activation(z)
+        assert qz.shape == z.shape and qz.stride() == z.stride() and sz.shape == (1,)

@@ -98,3 +98,40 @@ def test_valid_call_without_gpu_fails_loudly():
     b = (ctypes.addressof(buf) + 31) // 32 * 32
     rc = _rc("fvq_nvfp4_quantize", b, 4, 64, b, b, b, None)
     assert rc in (_lib.FVQ_ECUDA, _lib.FVQ_EDEVICE)
+
+
+def test_fp8_entry_points_check_arguments():
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(4096 + 32)
+    b = (ctypes.addressof(buf) + 31) // 32 * 32
+    # row quantizer: k a multiple of 8 up to 16384, 16-byte x and q
+    assert _rc("fvq_fp8_row_quantize", b, 4, 100, b, b, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_fp8_row_quantize", b, 4, 16392, b, b, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_fp8_row_quantize", b, 0, 64, b, b, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_fp8_row_quantize", b + 8, 4, 64, b, b, None) == _lib.FVQ_EALIGN
+    assert _rc("fvq_fp8_row_quantize", b, 4, 64, b, b + 2, None) == _lib.FVQ_EALIGN
+    # tensor quantizer: workspace size, alignment
+    wsb = lib.fvq_fp8_tensor_quantize_workspace_bytes()
+    assert wsb >= lib.fvq_amax_workspace_bytes() + 4
+    assert _rc("fvq_fp8_tensor_quantize", b, 100, b, b, b, wsb - 1, None) == _lib.FVQ_EWORKSPACE
+    assert _rc("fvq_fp8_tensor_quantize", b, 0, b, b, b, wsb, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_fp8_tensor_quantize", b, 100, b + 4, b, b, wsb, None) == _lib.FVQ_EALIGN
+    # scaled_mm: n % 256, k % 128, 16-byte W scales
+    mm = lambda m, n, k, sw=b: _rc("fvq_fp8_scaled_mm", b, b, b, sw, None, b, m, n, k, None)  # noqa: E731
+    assert mm(128, 200, 256) == _lib.FVQ_EINVAL
+    assert mm(128, 256, 192) == _lib.FVQ_EINVAL
+    assert mm(0, 256, 256) == _lib.FVQ_EINVAL
+    assert mm(128, 256, 256, sw=b + 4) == _lib.FVQ_EALIGN
+    # linear / ffn descriptors and workspace sizes
+    assert lib.fvq_fp8_linear_workspace_bytes(7680, 1536) >= 7680 * 1536 + 7680 * 4
+    need = 7680 * 4 * 3 + 7680 * 1536 + 7680 * 8960 * 3
+    assert need <= lib.fvq_fp8_ffn_workspace_bytes(7680, 1536, 8960) <= need + 4096
+    bad = _lib.FvqLinearFp8(None, None, None, 1536, 8960)
+    assert _rc("fvq_fp8_linear", b, 4, ctypes.byref(bad), b, b, 1 << 20, None) == _lib.FVQ_EINVAL
+    l1 = _lib.FvqLinearFp8(b, b, None, 1536, 8960)
+    l2 = _lib.FvqLinearFp8(b, b, None, 8960, 1024)
+    assert _rc("fvq_fp8_ffn", b, 4, ctypes.byref(l1), ctypes.byref(l2), b, b, 1 << 30,
+               None) == _lib.FVQ_EINVAL
+    l2 = _lib.FvqLinearFp8(b, b, None, 8960, 1536)
+    assert _rc("fvq_fp8_ffn", b, 4, ctypes.byref(l1), ctypes.byref(l2), b, b, 16,
+               None) == _lib.FVQ_EWORKSPACE
