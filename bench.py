@@ -20,8 +20,10 @@ region); `roofline` describes the GEMM kernel; `cpu_baseline` times the
 reference arithmetic (the CPU oracle) on this host.  Two separate measurements
 follow the timed steps (skip them with --no-extras): `stack_30_layers`, the
 30-layer stack of distinct layers over 15360 tokens with rows sharded across the
-ranks and the outputs all-gathered, and `quantize_sweep` (rank 0), the
-activation quantizer on K in {1536, 8960} x M in {1024, 4096, 16384, 65536}.
+ranks and the outputs all-gathered, `quantize_sweep` (rank 0), the
+activation quantizer on K in {1536, 8960} x M in {1024, 4096, 16384, 65536}, and
+`fp8_mode` (rank 0), the same layer in the reference's other mode,
+QuantLinear('fp8') (E4M3 W8A8, per-row scales).
 
 `--impl reference` times the reference's NVFP4 FFN arithmetic on the host CPU
 (the oracle restatement; the reference itself needs FlashInfer on a GPU) with
@@ -348,6 +350,101 @@ def fp4_library_sustained(torch, dev, seconds=2.0) -> dict | None:
         return None
 
 
+FP8_ROTATE = 4
+
+
+def fp8_mode_timing(torch, ops, lib, dev, stream, tokens, fp8_peak, steps=200) -> dict:
+    """The reference's other FFN mode, QuantLinear('fp8') (E4M3 W8A8 with per-row scales),
+    through fvq_fp8_ffn on the same layer: device-timed tokens/s over `steps` layers
+    rotating over FP8_ROTATE distinct (activation, weight) sets (204 MB > L2), the
+    four launches' device times, and torch._scaled_mm (the reference's own GEMM call,
+    cuBLASLt) on the two GEMM shapes back to back for comparison."""
+    from flashvsr_optimizations_b200 import _lib, workloads as W
+    g = torch.Generator(device=dev).manual_seed(7)
+    sets = []
+    for i in range(FP8_ROTATE):
+        x = (0.5 * torch.randn(tokens, D_MODEL, device=dev, generator=g)).to(torch.bfloat16)
+        w1 = (0.02 * torch.randn(D_FF, D_MODEL, device=dev, generator=g)).to(torch.bfloat16)
+        w2 = (0.02 * torch.randn(D_MODEL, D_FF, device=dev, generator=g)).to(torch.bfloat16)
+        b1 = (0.01 * torch.randn(D_FF, device=dev, generator=g)).to(torch.bfloat16)
+        b2 = (0.01 * torch.randn(D_MODEL, device=dev, generator=g)).to(torch.bfloat16)
+        q1, s1 = ops.fp8_row_quant(w1)
+        q2, s2 = ops.fp8_row_quant(w2)
+        s1, s2 = s1.reshape(-1).contiguous(), s2.reshape(-1).contiguous()
+        l1 = _lib.FvqLinearFp8(q1.data_ptr(), s1.data_ptr(), b1.data_ptr(), D_MODEL, D_FF)
+        l2 = _lib.FvqLinearFp8(q2.data_ptr(), s2.data_ptr(), b2.data_ptr(), D_FF, D_MODEL)
+        sets.append((x, l1, l2, (q1, s1, b1, q2, s2, b2)))
+    ws_bytes = lib.fvq_fp8_ffn_workspace_bytes(tokens, D_MODEL, D_FF)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    y = torch.empty(tokens, D_MODEL, dtype=torch.bfloat16, device=dev)
+    sptr = stream.cuda_stream
+
+    def step(i):
+        x, l1, l2, _ = sets[i % FP8_ROTATE]
+        rc = lib.fvq_fp8_ffn(x.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2), y.data_ptr(),
+                             ws.data_ptr(), ws_bytes, sptr)
+        if rc != 0:
+            raise RuntimeError(lib.fvq_last_error().decode())
+
+    for i in range(5):
+        step(i)
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(steps):
+        step(i)
+    e.record(stream)
+    e.synchronize()
+    ms = s.elapsed_time(e) / steps
+    kms = (ctypes.c_float * 4)()
+    acc = [[] for _ in range(4)]
+    for i in range(60):
+        x, l1, l2, _ = sets[i % FP8_ROTATE]
+        rc = lib.fvq_fp8_ffn_profile(x.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2),
+                                     y.data_ptr(), ws.data_ptr(), ws_bytes, sptr, kms)
+        if rc != 0:
+            raise RuntimeError(lib.fvq_last_error().decode())
+        if i >= 10:
+            for j in range(4):
+                acc[j].append(kms[j])
+    med = [statistics.median(a) for a in acc]
+    gemm_ms = med[1] + med[3]
+    gemm_tflops = tokens * FLOP_PER_TOKEN / (gemm_ms * 1e-3) / 1e12
+    out = {"mode": "fp8 (QuantLinear(mode='fp8'): E4M3, per-row scales, fvq_fp8_ffn)",
+           "tokens_per_s": tokens / (ms * 1e-3), "ms_per_layer": ms,
+           "tflops": tokens * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12,
+           "kernels_ms": {"quant_x": med[0], "gemm1_bias_gelu_rowmax": med[1],
+                          "quant_h": med[2], "gemm2_bias": med[3]},
+           "quant_h_GBps": tokens * D_FF * 3 / (med[2] * 1e-3) / 1e9,
+           "roofline": {"bound": "tensor", "kernel": "fp8_gemm_kernel (GEMM1 + GEMM2)",
+                        "achieved": gemm_tflops, "peak": fp8_peak, "unit": "TFLOP/s",
+                        "frac": gemm_tflops / fp8_peak,
+                        "peak_source": "2 x measured cuBLAS bf16 sustained (dense FP8 = 2x bf16)"},
+           "l2": f"{FP8_ROTATE} distinct activation/weight sets (204 MB > 126 MB L2)"}
+    try:  # torch._scaled_mm with row-wise scales on the same GEMM shapes
+        lib_us = {}
+        x, _, _, (q1, s1, b1, q2, s2, b2) = sets[0]
+        qx, sx = ops.fp8_row_quant(x)
+        h = (0.1 * torch.randn(tokens, D_FF, device=dev, generator=g)).to(torch.bfloat16)
+        qh, sh = ops.fp8_row_quant(h)
+        for name, (a, sa, w, sw) in (("gemm1_7680x8960x1536", (qx, sx, q1, s1)),
+                                     ("gemm2_7680x1536x8960", (qh, sh, q2, s2))):
+            f = lambda: torch._scaled_mm(a, w.t(), scale_a=sa, scale_b=sw.reshape(1, -1),  # noqa: E731
+                                         out_dtype=torch.bfloat16, use_fast_accum=False)
+            for _ in range(10):
+                f()
+            s.record(stream)
+            for _ in range(100):
+                f()
+            e.record(stream)
+            e.synchronize()
+            lib_us[name] = round(s.elapsed_time(e) / 100 * 1e3, 2)
+        out["torch_scaled_mm_us"] = lib_us
+    except Exception as exc:  # noqa: BLE001
+        out["torch_scaled_mm_us"] = f"unavailable: {type(exc).__name__}"
+    return out
+
+
 def fp4_library_peak(torch, dev) -> float | None:
     """Dense NVFP4 throughput of cuBLASLt (torch._scaled_mm) at 8192^3, TFLOP/s, or None."""
     try:
@@ -509,6 +606,8 @@ def main():
         extras["stack_30_layers"] = stack
         if rank == 0:
             extras["quantize_sweep"] = quantize_sweep(torch, lib, dev, stream, hbm)
+            fp8_peak = 2.0 * (bf16_sustained or 1400.0)
+            extras["fp8_mode"] = fp8_mode_timing(torch, ops, lib, dev, stream, tokens, fp8_peak)
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,

@@ -627,7 +627,7 @@ int fp8_ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear_fp8* lin1,
                              FVQ_EPI_GELU_AMAX, row_amax, st))
     return rc;
   mark(2);
-  // 3. h -> E4M3 with per-row scales from row_amax (which it re-zeroes)
+  // 3. h -> E4M3 with per-row scales from row_amax (step 1 of the next call re-zeroes it)
   e = fvq::launch_fp8_row_quant(h, rows, f, q_h, s_h, row_amax, nullptr, st);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_fp8_ffn quantize(h) launch");
   mark(3);

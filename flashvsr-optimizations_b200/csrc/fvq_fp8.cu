@@ -15,11 +15,13 @@
 // rounded); these kernels issue that same instruction, so the codes match the
 // reference bit for bit on the GPU.
 //
-// The row quantizer runs one CTA of 256 threads per row: the row is read once
+// The row quantizer runs one CTA of 256 threads per row (one warp per row for
+// rows of at most 2048 elements): the row is read once
 // into registers (16-byte loads, up to 8 per thread, so K <= 16384), reduced to
 // its max |x|, then divided and converted in place.  With a precomputed row
-// maximum (the FP8 GEMM1 epilogue's per-row max |h|) it skips the reduction and
-// resets that word to zero for the next use.
+// maximum (the FP8 GEMM1 epilogue's per-row max |h|) it skips the reduction.
+// The per-element division is replaced by two multiplies whose E4M3 codes
+// bracket div.full's, with the division issued where they disagree (quantize8).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -50,10 +52,11 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   return v;
 }
 
-// max |bf16| of both halves (bit patterns; non-NaN magnitudes order as integers)
-__device__ __forceinline__ uint32_t absmax_pair(uint32_t m, uint32_t w) {
-  const uint32_t a = w & 0x7FFF7FFFu;
-  return max(m, max(a & 0xFFFFu, a >> 16));
+// per-halfword unsigned maximum; on |bf16| bit patterns (non-NaN) it orders magnitudes
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
 }
 
 // Two floats -> two E4M3 bytes (`lo` in bits 0-7), round to nearest even, satfinite.
@@ -63,30 +66,67 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
   return r;
 }
 
-// Eight bf16 values (one 16-byte word) divided by `scale` -> eight E4M3 bytes.
-__device__ __forceinline__ uint2 quantize8_row(uint4 v, float scale) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  uint32_t p[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xFFFF0000u);
-    p[j] = e4m3x2(div_full(lo, scale), div_full(hi, scale));
-  }
-  return make_uint2(p[0] | (p[1] << 16), p[2] | (p[3] << 16));
+// E4M3 codes of x / scale without a division per element.  With r =
+// rcp.rn(scale), the products x * r * (1 -+ 2^-18) (through per-row constants
+// r_lo, r_hi; three roundings of at most 2^-24 each) lie below and above every
+// value within 2^-22 (relative) of the exact quotient, and div.full.f32's
+// result is one of those (its documented maximum error is 2 ulp).  Round-to-nearest-even
+// conversion is monotonic, so when the two ends of the bracket convert to the
+// same code (one paired cvt per end), that is the code of div.full(x, scale);
+// otherwise -- a rounding midpoint lies inside the bracket, about 6e-5 of
+// Gaussian-like data -- the division itself is issued.  Zeros, fp32 subnormals
+// and saturating values need no special case: both ends agree on them.
+// kClamp (the tensor quantizer): quotients are clamped to [-448, 448] before
+// the conversion, as the reference does (NaN clamps to -448 like Triton's
+// NaN-ignoring maximum).
+constexpr float kBracketLo = 1.0f - 0x1p-18f;
+constexpr float kBracketHi = 1.0f + 0x1p-18f;
+
+// (lo, hi) * (r, r) in one mul.rn.f32x2
+__device__ __forceinline__ void mul2(float lo, float hi, float r, float& plo, float& phi) {
+  uint64_t v, rr, p;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(rr) : "f"(r));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(v), "l"(rr));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(plo), "=f"(phi) : "l"(p));
 }
 
-// The tensor quantizer's variant: the quotient is clamped to [-448, 448] first.
 __device__ __forceinline__ float clamp448(float v) { return fminf(fmaxf(v, -448.0f), 448.0f); }
 
-__device__ __forceinline__ uint2 quantize8_clamped(uint4 v, float scale) {
+template <bool kClamp>
+__device__ __forceinline__ uint32_t e4m3_pair(float lo, float hi) {
+  if (kClamp) {
+    lo = clamp448(lo);
+    hi = clamp448(hi);
+  }
+  return e4m3x2(lo, hi);
+}
+
+// Eight bf16 values (one 16-byte word) -> eight E4M3 codes of div.full(x, scale).
+template <bool kClamp>
+__device__ __forceinline__ uint2 quantize8(uint4 v, float scale, float r_lo, float r_hi) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  uint32_t p[4];
+  uint32_t c[4];
+  uint32_t differ = 0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xFFFF0000u);
-    p[j] = e4m3x2(clamp448(div_full(lo, scale)), clamp448(div_full(hi, scale)));
+    float dl, dh, ul, uh;
+    mul2(lo, hi, r_lo, dl, dh);
+    mul2(lo, hi, r_hi, ul, uh);
+    c[j] = e4m3_pair<kClamp>(dl, dh);
+    if (c[j] != e4m3_pair<kClamp>(ul, uh)) differ |= 1u << j;  // pair j unsettled
   }
-  return make_uint2(p[0] | (p[1] << 16), p[2] | (p[3] << 16));
+  if (__builtin_expect(differ != 0, 0)) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (differ & (1u << j)) {
+        const float lo = __uint_as_float(w[j] << 16), hi = __uint_as_float(w[j] & 0xFFFF0000u);
+        c[j] = e4m3_pair<kClamp>(div_full(lo, scale), div_full(hi, scale));
+      }
+    }
+  }
+  return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
 }
 
 // scale = max(div(amax, 448), 1e-12): _row_quant's `tl.maximum(tl.max(|x|)/448., 1.e-12)`.
@@ -95,19 +135,18 @@ __device__ __forceinline__ float row_scale(float amax) {
 }
 
 // One CTA per row.  kVec: 16-byte words per thread (the row has k/8 of them).
-// row_amax != nullptr: its word for the row holds max |x| (fp32 bits); the
-// reduction is skipped and the word is reset to zero after use.  zero_rows !=
-// nullptr: the row's word there is set to zero (arming the per-row maxima a
-// later GEMM epilogue accumulates).
+// row_amax != nullptr: its word for the row holds max |x| (fp32 bits) and the
+// reduction is skipped.  zero_rows != nullptr: the row's word there is set to
+// zero (arming the per-row maxima a later GEMM epilogue accumulates).
 template <int kVec>
 __global__ void __launch_bounds__(kRowThreads) fp8_row_quant_kernel(
     const uint16_t* __restrict__ x, int k, uint8_t* __restrict__ q, float* __restrict__ scale_out,
-    uint32_t* row_amax, uint32_t* zero_rows) {
+    const uint32_t* __restrict__ row_amax, uint32_t* zero_rows) {
   __shared__ uint32_t warp_max[kRowThreads / 32];
-  __shared__ float row_scale_s;
   const int64_t row = blockIdx.x;
   const int nvec = k / 8;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * k);
+  uint32_t amax_bits = row_amax != nullptr ? __ldg(row_amax + row) : 0u;
   uint4 v[kVec];
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
@@ -115,39 +154,74 @@ __global__ void __launch_bounds__(kRowThreads) fp8_row_quant_kernel(
     v[i] = j < nvec ? ld_nc_v4(xr + j) : make_uint4(0, 0, 0, 0);
   }
   if (row_amax == nullptr) {
-    uint32_t m = 0;
+    uint32_t m2 = 0;  // max |x| of the low and high halves, packed
 #pragma unroll
     for (int i = 0; i < kVec; ++i) {
-      m = absmax_pair(m, v[i].x);
-      m = absmax_pair(m, v[i].y);
-      m = absmax_pair(m, v[i].z);
-      m = absmax_pair(m, v[i].w);
+      m2 = max_u16x2(m2, max_u16x2(v[i].x & 0x7FFF7FFFu, v[i].y & 0x7FFF7FFFu));
+      m2 = max_u16x2(m2, max_u16x2(v[i].z & 0x7FFF7FFFu, v[i].w & 0x7FFF7FFFu));
     }
-    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    uint32_t m = __reduce_max_sync(0xFFFFFFFFu, max(m2 & 0xFFFFu, m2 >> 16));
     if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
     __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t t = warp_max[0];
+    m = warp_max[0];
 #pragma unroll
-      for (int w = 1; w < kRowThreads / 32; ++w) t = max(t, warp_max[w]);
-      const float s = row_scale(__uint_as_float(t << 16));
-      row_scale_s = s;
-      scale_out[row] = s;
-    }
-  } else if (threadIdx.x == 0) {
-    const float s = row_scale(__uint_as_float(row_amax[row]));
-    row_amax[row] = 0u;
-    row_scale_s = s;
-    scale_out[row] = s;
+    for (int w = 1; w < kRowThreads / 32; ++w) m = max(m, warp_max[w]);
+    amax_bits = m << 16;
   }
-  __syncthreads();
-  if (zero_rows != nullptr && threadIdx.x == 0) zero_rows[row] = 0u;
-  const float s = row_scale_s;
+  const float s = row_scale(__uint_as_float(amax_bits));
+  const float r = __frcp_rn(s);
+  const float r_lo = __fmul_rn(r, kBracketLo), r_hi = __fmul_rn(r, kBracketHi);
+  if (threadIdx.x == 0) {
+    scale_out[row] = s;
+    if (zero_rows != nullptr) zero_rows[row] = 0u;
+  }
   uint2* qr = reinterpret_cast<uint2*>(q + row * k);
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int j = threadIdx.x + i * kRowThreads;
-    if (j < nvec) qr[j] = quantize8_row(v[i], s);
+    if (j < nvec) qr[j] = quantize8<false>(v[i], s, r_lo, r_hi);
+  }
+}
+
+// Rows of at most 2048 elements: one warp per row, eight rows per CTA, the row
+// maximum reduced within the warp.  Same arithmetic as fp8_row_quant_kernel.
+template <int kVec>
+__global__ void __launch_bounds__(kRowThreads) fp8_row_quant_warp_kernel(
+    const uint16_t* __restrict__ x, int64_t rows, int k, uint8_t* __restrict__ q,
+    float* __restrict__ scale_out, const uint32_t* __restrict__ row_amax, uint32_t* zero_rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nvec = k / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * k);
+  uint32_t amax_bits = row_amax != nullptr ? __ldg(row_amax + row) : 0u;
+  uint4 v[kVec];
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int j = lane + i * 32;
+    v[i] = j < nvec ? ld_nc_v4(xr + j) : make_uint4(0, 0, 0, 0);
+  }
+  if (row_amax == nullptr) {
+    uint32_t m2 = 0;
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      m2 = max_u16x2(m2, max_u16x2(v[i].x & 0x7FFF7FFFu, v[i].y & 0x7FFF7FFFu));
+      m2 = max_u16x2(m2, max_u16x2(v[i].z & 0x7FFF7FFFu, v[i].w & 0x7FFF7FFFu));
+    }
+    amax_bits = __reduce_max_sync(0xFFFFFFFFu, max(m2 & 0xFFFFu, m2 >> 16)) << 16;
+  }
+  const float s = row_scale(__uint_as_float(amax_bits));
+  const float r = __frcp_rn(s);
+  const float r_lo = __fmul_rn(r, kBracketLo), r_hi = __fmul_rn(r, kBracketHi);
+  if (lane == 0) {
+    scale_out[row] = s;
+    if (zero_rows != nullptr) zero_rows[row] = 0u;
+  }
+  uint2* qr = reinterpret_cast<uint2*>(q + row * k);
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int j = lane + i * 32;
+    if (j < nvec) qr[j] = quantize8<false>(v[i], s, r_lo, r_hi);
   }
 }
 
@@ -159,6 +233,8 @@ __global__ void __launch_bounds__(kTensorThreads) fp8_tensor_quant_kernel(
     const uint16_t* __restrict__ x, int64_t numel, const float* __restrict__ amax,
     uint8_t* __restrict__ q, float* __restrict__ scale_out) {
   const float s = fmaxf(__fmul_rn(*amax, kInv448), 1e-12f);
+  const float r = __frcp_rn(s);
+  const float r_lo = __fmul_rn(r, kBracketLo), r_hi = __fmul_rn(r, kBracketHi);
   if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
   const int64_t nvec = numel / 8;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
@@ -175,7 +251,7 @@ __global__ void __launch_bounds__(kTensorThreads) fp8_tensor_quant_kernel(
 #pragma unroll
     for (int u = 0; u < kTensorUnroll; ++u) {
       const int64_t j = i + u * stride;
-      if (j < nvec) qv[j] = quantize8_clamped(v[u], s);
+      if (j < nvec) qv[j] = quantize8<true>(v[u], s, r_lo, r_hi);
     }
   }
   if (blockIdx.x == 0 && threadIdx.x < (numel & 7)) {
@@ -192,8 +268,17 @@ __global__ void div_full_probe_kernel(const float* a, const float* b, float* out
 }
 
 template <int kVec>
+void row_quant_warp_launch(const uint16_t* x, int64_t rows, int k, uint8_t* q, float* scale,
+                           const uint32_t* row_amax, uint32_t* zero_rows, cudaStream_t st) {
+  constexpr int kRowsPerCta = kRowThreads / 32;
+  const int64_t blocks = (rows + kRowsPerCta - 1) / kRowsPerCta;
+  fp8_row_quant_warp_kernel<kVec><<<static_cast<unsigned>(blocks), kRowThreads, 0, st>>>(
+      x, rows, k, q, scale, row_amax, zero_rows);
+}
+
+template <int kVec>
 void row_quant_launch(const uint16_t* x, int64_t rows, int k, uint8_t* q, float* scale,
-                      uint32_t* row_amax, uint32_t* zero_rows, cudaStream_t st) {
+                      const uint32_t* row_amax, uint32_t* zero_rows, cudaStream_t st) {
   fp8_row_quant_kernel<kVec><<<static_cast<unsigned>(rows), kRowThreads, 0, st>>>(
       x, k, q, scale, row_amax, zero_rows);
 }
@@ -203,11 +288,24 @@ void row_quant_launch(const uint16_t* x, int64_t rows, int k, uint8_t* q, float*
 int64_t fp8_row_quant_max_k() { return static_cast<int64_t>(kRowThreads) * kRowMaxVec * 8; }
 
 cudaError_t launch_fp8_row_quant(const uint16_t* x, int64_t rows, int64_t k, uint8_t* q,
-                                 float* scale, uint32_t* row_amax, uint32_t* zero_rows,
+                                 float* scale, const uint32_t* row_amax, uint32_t* zero_rows,
                                  cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  const int words = static_cast<int>((k / 8 + kRowThreads - 1) / kRowThreads);
   const int ki = static_cast<int>(k);
+  if (k <= 2048) {  // one warp per row
+    switch (static_cast<int>((k / 8 + 31) / 32)) {
+      case 0:
+      case 1: row_quant_warp_launch<1>(x, rows, ki, q, scale, row_amax, zero_rows, st); break;
+      case 2: row_quant_warp_launch<2>(x, rows, ki, q, scale, row_amax, zero_rows, st); break;
+      case 3:
+      case 4: row_quant_warp_launch<4>(x, rows, ki, q, scale, row_amax, zero_rows, st); break;
+      case 5:
+      case 6: row_quant_warp_launch<6>(x, rows, ki, q, scale, row_amax, zero_rows, st); break;
+      default: row_quant_warp_launch<8>(x, rows, ki, q, scale, row_amax, zero_rows, st); break;
+    }
+    return cudaGetLastError();
+  }
+  const int words = static_cast<int>((k / 8 + kRowThreads - 1) / kRowThreads);
   switch (words) {
     case 0:
     case 1: row_quant_launch<1>(x, rows, ki, q, scale, row_amax, zero_rows, st); break;

@@ -82,12 +82,12 @@ cudaError_t launch_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w,
                             const char** why);
 
 // FP8 quantizers (fvq_fp8.cu).  Row: one scale per row, k % 8 == 0 and
-// k <= fp8_row_quant_max_k(); row_amax != NULL supplies each row's max |x| and is
-// zeroed; zero_rows != NULL gets zero in each row's word.  Tensor: one scale from a
+// k <= fp8_row_quant_max_k(); row_amax != NULL supplies each row's max |x| (fp32
+// bits); zero_rows != NULL gets zero in each row's word.  Tensor: one scale from a
 // device amax.
 int64_t fp8_row_quant_max_k();
 cudaError_t launch_fp8_row_quant(const uint16_t* x, int64_t rows, int64_t k, uint8_t* q,
-                                 float* scale, uint32_t* row_amax, uint32_t* zero_rows,
+                                 float* scale, const uint32_t* row_amax, uint32_t* zero_rows,
                                  cudaStream_t st);
 cudaError_t launch_fp8_tensor_quant(const uint16_t* x, int64_t numel, const float* amax,
                                     uint8_t* q, float* scale, cudaStream_t st);

@@ -126,6 +126,45 @@ def test_row_quant_vs_oracle_with_measured_division(m, k):
     assert np.array_equal(_u8(q), oq)
 
 
+def _e4m3_midpoints() -> np.ndarray:
+    """Every value halfway between adjacent E4M3 magnitudes (the rounding ties)."""
+    mags = np.unique(np.abs(O.e4m3_to_f32(np.arange(0, 0x7F, dtype=np.uint8))))
+    return ((mags[1:] + mags[:-1]) / 2).astype(np.float32)
+
+
+def test_row_quant_ties_and_near_midpoints():
+    """Quotients on and next to E4M3 rounding midpoints: the one-multiply path must
+    hand these to div.full, and ties must round to even as the reference's do."""
+    mids = _e4m3_midpoints()
+    rows = []
+    # amax 448 -> scale exactly 1 and amax 7 -> scale 2^-6: every quotient is exact,
+    # so bf16 midpoints are exact ties
+    for amax, scale in ((448.0, 1.0), (7.0, 2.0 ** -6)):
+        r = np.zeros(256, np.float32)
+        r[0] = amax
+        ties = (mids * np.float32(scale)).astype(np.float32)
+        ties = ties[O.round_bf16(ties) == ties][:255]
+        r[1:1 + ties.size] = ties
+        r[1 + ties.size:] = -r[1:256 - ties.size]
+        rows.append(r)
+    # scales with long mantissas: quotients land within a few ulp of midpoints
+    rng = np.random.default_rng(3)
+    for amax in (3.0, 5.0, 11.0, 13.0, 0.1, 1e-3, 300.0, 97.0):
+        r = rng.standard_normal(256).astype(np.float32) * np.float32(amax / 4)
+        r[0] = amax
+        rows.append(np.clip(r, -amax, amax))
+    xb = O.f32_to_bf16_bits(np.stack(rows))
+    q, s = ops.fp8_row_quant(bits_to_dev(xb))
+    oq, os_ = F.row_quant(xb, _probe_div)
+    assert np.array_equal(_f32_bits(s), os_.view(np.uint32))
+    assert np.array_equal(_u8(q), oq)
+    # a large random case hits ~3e-5 of its quotients inside the fallback window
+    xb = W.student_t(512, 8960, seed=77)
+    q, s = ops.fp8_row_quant(bits_to_dev(xb))
+    oq, _ = F.row_quant(xb, _probe_div)
+    assert np.array_equal(_u8(q), oq)
+
+
 @pytest.mark.parametrize("numel", [1, 7, 8, 4099, 1 << 20])
 def test_tensor_quant_vs_oracle_with_measured_division(numel):
     xb = W.with_outliers(1, numel, seed=numel)
