@@ -79,6 +79,61 @@ def env_rank():
 
 
 # ---------------------------------------------------------------- clocks
+class NvmlClockSampler:
+    """SM clock, power and clock-event reasons read through NVML every 5 ms from a
+    thread of this process, so that even a timed region of a few tens of
+    milliseconds is sampled (nvidia-smi takes longer than that to start)."""
+
+    def __init__(self, gpu_id: str):
+        import pynvml
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        self.h = pynvml.nvmlDeviceGetHandleByUUID(gpu_id.encode())
+        self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        self.samples: list[tuple[float, float, int]] = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+                self.samples.append((sm, pw, rs))
+            except nv.NVMLError:
+                pass
+            self._stop.wait(0.005)
+
+    def start(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=2)
+        nv = self.nv
+        names = {nv.nvmlClocksEventReasonHwSlowdown: "hw_slowdown",
+                 nv.nvmlClocksEventReasonHwThermalSlowdown: "hw_thermal_slowdown",
+                 nv.nvmlClocksEventReasonSwThermalSlowdown: "sw_thermal_slowdown",
+                 nv.nvmlClocksEventReasonSwPowerCap: "sw_power_cap"}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.smax, "reasons": ["no samples"], "samples": 0}
+        reasons = sorted({nm for _, _, rs in self.samples for bit, nm in names.items() if rs & bit})
+        return {"sm_mhz": statistics.median(sm for sm, _, _ in self.samples), "sm_max_mhz": self.smax,
+                "reasons": reasons, "samples": len(self.samples),
+                "power_w_max": max(pw for _, pw, _ in self.samples), "source": "nvml"}
+
+
+def clock_sampler(gpu_id: str):
+    try:
+        return NvmlClockSampler(gpu_id)
+    except Exception:  # noqa: BLE001 - NVML missing or refused: fall back to nvidia-smi
+        return ClockSampler(gpu_id)
+
+
 class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons while the GPU is busy."""
 
@@ -525,9 +580,10 @@ def main():
         step(i)
     barrier_sync()
     gpu_uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-    sampler = ClockSampler(gpu_uuid)
+    sampler = clock_sampler(gpu_uuid)
     sampler.start()
-    time.sleep(0.15)
+    if isinstance(sampler, ClockSampler):
+        time.sleep(0.15)  # nvidia-smi's start-up
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier_sync()
     start.record(stream)

@@ -68,6 +68,7 @@ SIGNATURES = {
     "fvq_nvfp4_mm": (_c.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "fvq_w_scales_replicated_bytes": (_sz, [_i64, _i64]),
     "fvq_set_gemm_pairing": (_c.c_int, [_c.c_int]),
+    "fvq_set_fp8_gemm_pairing": (_c.c_int, [_c.c_int]),
     "fvq_replicate_w_scales": (_c.c_int, [_vp, _i64, _i64, _vp, _vp]),
     "fvq_nvfp4_gemm_wrep": (_c.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
                                        _vp]),

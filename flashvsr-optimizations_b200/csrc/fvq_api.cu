@@ -705,6 +705,13 @@ int fvq_set_gemm_pairing(int enabled) {
   return FVQ_OK;
 }
 
+int fvq_set_fp8_gemm_pairing(int mode) {
+  if (mode < 0 || mode > 2)
+    return fail(FVQ_EINVAL, "fvq_set_fp8_gemm_pairing: mode must be 0, 1 or 2 (got %d)", mode);
+  fvq::set_fp8_gemm_pairing(mode);
+  return FVQ_OK;
+}
+
 int fvq_set_wait_limit(uint64_t nanoseconds) {
   g_wait_limit = nanoseconds == 0 ? fvq::kDefaultWaitLimit : nanoseconds;
   return FVQ_OK;

@@ -863,9 +863,9 @@ constexpr uint32_t kF8TmemCols = 256;                 // the fp32 accumulator on
 template <int kEpi>
 struct F8Plan {
   static constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
-  static constexpr int kStages = kEpi == 0 ? 4 : 3;
+  static constexpr int kStages = 3;
   static constexpr int kStagingOff = kStages * kStageBytes;
-  static constexpr int kTableOff = kStagingOff + (kEpi == 1 ? kStagingBytes : 0);
+  static constexpr int kTableOff = kStagingOff + kStagingBytes;
   static constexpr int kBarrierOff = kTableOff + (kEpi == 1 ? kGeluTabBytes : 0);
   static constexpr int kSmemBytes = kBarrierOff + kBarrierBytes;
 };
@@ -1074,67 +1074,330 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       asm("mov.b64 %0, {%1, %1};" : "=l"(sa2) : "f"(sa));
       const int col0 = nb * BN + (half > 0 ? BN / 2 : 0) + col_base;
       const float4* sw4 = reinterpret_cast<const float4*>(sw_cols + col0);
-      if constexpr (kEpi == 1) {
-        if (lane == 0) bulk_wait_group_read0();  // previous store has read the staging
-        __syncwarp();
-        const uint4* bias4 = reinterpret_cast<const uint4*>(bias + col0);
-        uint32_t tile_max = 0;
+      if (lane == 0) bulk_wait_group_read0();  // previous store has read the staging
+      __syncwarp();
+      const uint4* bias4 = reinterpret_cast<const uint4*>(bias + col0);
+      uint32_t tile_max = 0;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 s0 = __ldg(sw4 + 2 * q), s1 = __ldg(sw4 + 2 * q + 1);
-          const float sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-          uint4 bv = make_uint4(0, 0, 0, 0);
-          if (bias != nullptr) bv = __ldg(bias4 + q);
-          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-          uint32_t o[4];
+      for (int q = 0; q < 8; ++q) {
+        const float4 s0 = __ldg(sw4 + 2 * q), s1 = __ldg(sw4 + 2 * q + 1);
+        const float sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        uint4 bv = make_uint4(0, 0, 0, 0);
+        if (bias != nullptr) bv = __ldg(bias4 + q);
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        uint32_t o[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t hv = rowcol_scale_pack_bf16x2(r[8 * q + 2 * j], r[8 * q + 2 * j + 1], sa2,
-                                                   sw[2 * j], sw[2 * j + 1]);
-            if (bias != nullptr) hv = add_bf16x2(hv, bw[j]);
+        for (int j = 0; j < 4; ++j) {
+          uint32_t hv = rowcol_scale_pack_bf16x2(r[8 * q + 2 * j], r[8 * q + 2 * j + 1], sa2,
+                                                 sw[2 * j], sw[2 * j + 1]);
+          if (bias != nullptr) hv = add_bf16x2(hv, bw[j]);
+          if constexpr (kEpi == 1) {
             hv = gelu_bf16x2(hv, tab_base, gelu_tab);
             tile_max = max_u16x2(tile_max, hv & 0x7FFF7FFFu);
-            o[j] = hv;
           }
-          *reinterpret_cast<uint4*>(warp_staging + lane * kStageRowBytes + ((q ^ (lane & 7)) * 16)) =
-              make_uint4(o[0], o[1], o[2], o[3]);
+          o[j] = hv;
         }
+        // 128B-swizzled staging (chunk c of row r at r*128 + ((c ^ (r & 7)) * 16)),
+        // the output tensor map's swizzle
+        *reinterpret_cast<uint4*>(warp_staging + lane * kStageRowBytes + ((q ^ (lane & 7)) * 16)) =
+            make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      if constexpr (kEpi == 1) {
         const uint32_t mag = max(tile_max & 0xFFFFu, tile_max >> 16);
         if (row < m && mag != 0) atomicMax(row_amax + row, mag << 16);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmap_out, warp_staging, col0, mb * BM + quad * 32);
-          bulk_commit_group();
-        }
-      } else {
-        uint16_t* dst = out + static_cast<int64_t>(row) * n + col0;
-#pragma unroll
-        for (int c = 0; c < 64; c += 8) {
-          const float4 s0 = __ldg(sw4 + c / 4), s1 = __ldg(sw4 + c / 4 + 1);
-          const float sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-          uint4 bv = make_uint4(0, 0, 0, 0);
-          if (bias != nullptr) bv = __ldg(reinterpret_cast<const uint4*>(bias + col0 + c));
-          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-          uint32_t o[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t w = rowcol_scale_pack_bf16x2(r[c + 2 * j], r[c + 2 * j + 1], sa2, sw[2 * j],
-                                                  sw[2 * j + 1]);
-            if (bias != nullptr) w = add_bf16x2(w, bw[j]);
-            o[j] = w;
-          }
-          if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
-        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && mb * BM + quad * 32 < m) {
+        tma_store_2d(&tmap_out, warp_staging, col0, mb * BM + quad * 32);
+        bulk_commit_group();
       }
     }
-    if (kEpi == 1 && lane == 0) bulk_wait_group0();  // stores complete before the CTA exits
+    if (lane == 0) bulk_wait_group0();  // stores complete before the CTA exits
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kF8TmemCols);
+}
+
+// ---------------------------------------------------------------- FP8 SM-pair GEMM
+// fp8_gemm_pair_kernel: fp8_gemm_kernel on clusters of two CTAs (the two SMs
+// of a pair) with tcgen05.mma.cta_group::2, M = 256 across the pair: one
+// 256 x 256 output tile per pair.  Per 128-deep K tile each CTA loads its 128
+// rows of A and 128 of the tile's 256 W rows (32 KB per SM instead of 48 KB:
+// each W tile crosses from L2 once per pair), all counted on the even CTA's
+// stage barrier, which only the even CTA arms.  The even CTA issues the MMAs
+// and commits "stage free" and "accumulator full" to both CTAs' barriers;
+// both CTAs run the epilogue on their own 128 accumulator rows and report a
+// drained accumulator to the even CTA.  Rows past m (a last pair tile over
+// the end of A) load as zeros and are not stored.
+constexpr int kF8PairStageBytes = kABytes + kBBytes / 2;  // 32 KB
+template <int kEpi>
+struct F8PairPlan {
+  static constexpr int kStages = kEpi == 0 ? 5 : 4;  // next to 64 KB of staging (+ GELU table)
+  static constexpr int kStagingOff = kStages * kF8PairStageBytes;
+  static constexpr int kTableOff = kStagingOff + kStagingBytes;
+  static constexpr int kBarrierOff = kTableOff + (kEpi == 1 ? kGeluTabBytes : 0);
+  static constexpr int kSmemBytes = kBarrierOff + kBarrierBytes;
+};
+static_assert(F8PairPlan<0>::kSmemBytes <= 232448, "FP8 pair plan exceeds shared memory");
+static_assert(F8PairPlan<1>::kSmemBytes <= 232448, "FP8 pair GEMM1 plan exceeds shared memory");
+constexpr uint32_t kIdescF8Pair = (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                  (static_cast<uint32_t>(2 * BM >> 4) << 24);
+
+template <int kStages>
+struct F8PairBarriers {
+  uint64_t full[kStages];    // even CTA: both CTAs' stage landed
+  uint64_t empty[kStages];   // the pair's MMAs on the stage completed
+  uint64_t acc_full;         // the pair's accumulator is complete
+  uint64_t acc_empty;        // even CTA: both epilogues drained their TMEM
+  uint64_t teardown;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(F8PairBarriers<6>) <= kBarrierBytes, "FP8 pair barrier area");
+
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                         const __grid_constant__ CUtensorMap tmap_b_half,
+                         const __grid_constant__ CUtensorMap tmap_out,
+                         const float* __restrict__ sa_rows, const float* __restrict__ sw_cols,
+                         const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m,
+                         int n, int k, uint32_t* row_amax, uint64_t wait_limit) {
+  using P = F8PairPlan<kEpi>;
+  constexpr int kStages = P::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicOr(&g_device_error, kErrSmemAlign);
+    return;  // both CTAs see the same layout, so both return here
+  }
+  auto* bars = reinterpret_cast<F8PairBarriers<kStages>*>(smem + P::kBarrierOff);
+  uint8_t* staging = smem + P::kStagingOff;
+  uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + P::kTableOff);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool even = rank == 0;
+  const int pairs = gridDim.x / 2, pair = blockIdx.x / 2;
+  const int num_m_pairs = (m + 2 * BM - 1) / (2 * BM);
+  const int num_n_blocks = n / BN;
+  const int tiles = num_m_pairs * num_n_blocks;
+  const int count = pair < tiles ? (tiles - 1 - pair) / pairs + 1 : 0;  // same in both CTAs
+  const int num_k_tiles = k / kF8BK;
+  const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 2 * kEpiWarps);
+    mbar_init(&bars->teardown, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b_half);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&bars->tmem_base, kF8TmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const auto even_addr = [&](const void* p) { return mapa_shared(smem_u32(p), 0); };
+  const auto odd_addr = [&](const void* p) { return mapa_shared(smem_u32(p), 1); };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0 && count > 0) {
+      uint32_t armed[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) armed[s] = 0;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int i = 0; i < count && !aborted(bars); ++i) {
+        const int t = pair + i * pairs;
+        const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
+        // this CTA's 128 rows; a block wholly past the last row loads the last
+        // block instead (its rows are never stored), so every box starts inside A
+        const int a_row = min((2 * mbp + static_cast<int>(rank)) * BM, ((m - 1) / BM) * BM);
+        for (int kt = 0; kt < num_k_tiles; ++kt) {
+          if (!mbar_wait_cluster_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
+            flag_error(bars, kErrWaitProducer);
+            break;
+          }
+          uint8_t* sa = smem + stage * kF8PairStageBytes;
+          uint8_t* sb = sa + kABytes;
+          const uint32_t bar = even_addr(&bars->full[stage]);
+          if (even) mbar_arrive_expect_tx(&bars->full[stage], 2 * kF8PairStageBytes);
+          tma_load_2d_pair(sa, &tmap_a, bar, kt * kF8BK, a_row);
+          tma_load_2d_pair(sb, &tmap_b_half, bar, kt * kF8BK,
+                           nb * BN + static_cast<int>(rank) * (BN / 2));
+          armed[stage] += 1;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // the even CTA's stage barriers count both CTAs' loads; the odd CTA's land
+      // before the even CTA's MMAs consume the stage, which the final cluster
+      // barrier waits for
+      for (int s = 0; even && s < kStages; ++s) {
+        if (armed[s] > 0 &&
+            !mbar_wait_cluster_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit))
+          flag_error(bars, kErrWaitTeardown);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && count > 0 && even) {
+      // ---------------------------------------------------------- MMA issuer (even CTA)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued_any = false;
+      bool ok = true;
+      for (int i = 0; ok && i < count && !aborted(bars); ++i) {
+        if (!mbar_wait_cluster_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
+                                       wait_limit)) {
+          flag_error(bars, kErrWaitMma);
+          break;
+        }
+        tc_fence_after();
+        for (int kt = 0; kt < num_k_tiles; ++kt) {
+          if (!mbar_wait_cluster_bounded(&bars->full[stage], phase, wait_limit)) {
+            flag_error(bars, kErrWaitMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* sa = smem + stage * kF8PairStageBytes;
+          uint8_t* sb = sa + kABytes;
+          const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
+          const uint64_t bdesc = make_smem_desc(smem_u32(sb), 16, 1024, 2);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            mma_f8_pair(tmem, adesc + static_cast<uint64_t>(2 * j),
+                        bdesc + static_cast<uint64_t>(2 * j), kIdescF8Pair,
+                        (kt > 0 || j > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          tc_commit_pair(smem_u32(&bars->empty[stage]));
+          tc_commit_pair(odd_addr(&bars->empty[stage]));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(smem_u32(&bars->acc_full));
+        tc_commit_pair(odd_addr(&bars->acc_full));
+      }
+      if (aborted(bars) && issued_any) {
+        tc_commit_pair(smem_u32(&bars->teardown));
+        if (!mbar_wait_bounded(&bars->teardown, 0, teardown_limit))
+          flag_error(bars, kErrWaitTeardown);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;
+    const int quarter = (warp - 2) >> 2;
+    const int col_base = quarter * 64;
+    const int trow = quad * 32 + lane;
+    if constexpr (kEpi == 1) {
+      gelu_table_init(gelu_tab, threadIdx.x - 64, kEpiThreads);
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+    }
+    const uint32_t tab_base = smem_u32(gelu_tab);
+    uint8_t* warp_staging = staging + (warp - 2) * kWarpStagingBytes;
+    const uint32_t acc_empty_addr = even_addr(&bars->acc_empty);
+    for (int i = 0; i < count; ++i) {
+      const int t = pair + i * pairs;
+      const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
+      const int row0 = mbp * 2 * BM + static_cast<int>(rank) * BM;  // this CTA's first row
+      const int row = row0 + trow;
+      const float sa = row < m ? __ldg(sa_rows + row) : 0.0f;
+      if (!mbar_wait_cluster_bounded(&bars->acc_full, static_cast<uint32_t>(i) & 1u, wait_limit)) {
+        flag_error(bars, kErrWaitEpilogue);
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[64];
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + col_base;
+      tmem_ld_32x32b_x32(taddr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_addr);
+      uint64_t sa2;
+      asm("mov.b64 %0, {%1, %1};" : "=l"(sa2) : "f"(sa));
+      const int col0 = nb * BN + col_base;
+      const float4* sw4 = reinterpret_cast<const float4*>(sw_cols + col0);
+      if (lane == 0) bulk_wait_group_read0();  // previous store has read the staging
+      __syncwarp();
+      const uint4* bias4 = reinterpret_cast<const uint4*>(bias + col0);
+      uint32_t tile_max = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 s0 = __ldg(sw4 + 2 * q), s1 = __ldg(sw4 + 2 * q + 1);
+        const float sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        uint4 bv = make_uint4(0, 0, 0, 0);
+        if (bias != nullptr) bv = __ldg(bias4 + q);
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t hv = rowcol_scale_pack_bf16x2(r[8 * q + 2 * j], r[8 * q + 2 * j + 1], sa2,
+                                                 sw[2 * j], sw[2 * j + 1]);
+          if (bias != nullptr) hv = add_bf16x2(hv, bw[j]);
+          if constexpr (kEpi == 1) {
+            hv = gelu_bf16x2(hv, tab_base, gelu_tab);
+            tile_max = max_u16x2(tile_max, hv & 0x7FFF7FFFu);
+          }
+          o[j] = hv;
+        }
+        // 128B-swizzled staging (chunk c of row r at r*128 + ((c ^ (r & 7)) * 16)),
+        // the output tensor map's swizzle
+        *reinterpret_cast<uint4*>(warp_staging + lane * kStageRowBytes + ((q ^ (lane & 7)) * 16)) =
+            make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      if constexpr (kEpi == 1) {
+        const uint32_t mag = max(tile_max & 0xFFFFu, tile_max >> 16);
+        if (row < m && mag != 0) atomicMax(row_amax + row, mag << 16);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && row0 + quad * 32 < m) {
+        tma_store_2d(&tmap_out, warp_staging, col0, row0 + quad * 32);
+        bulk_commit_group();
+      }
+    }
+    if (lane == 0) bulk_wait_group0();  // stores complete before the CTA exits
+  }
+
+  tc_fence_before();
+  cluster_sync();  // neither CTA leaves while the pair's MMAs or arrivals may touch it
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, kF8TmemCols);
 }
 
 // GELU of bf16 values through the epilogue's path (test support): values
@@ -1319,7 +1582,47 @@ cudaError_t launch_fp8_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, cons
   return cudaGetLastError();
 }
 
+template <int kEpi>
+cudaError_t launch_fp8_gemm_pair_t(const CUtensorMap& ma, const CUtensorMap& mb_half,
+                                   const CUtensorMap& mo, const float* sa, const float* sw,
+                                   const uint16_t* bias, uint16_t* out, int m, int n, int k,
+                                   uint32_t* row_amax, uint64_t wait_limit, cudaStream_t st) {
+  static bool attr_set[64] = {false};
+  constexpr int kSmemBytes = F8PairPlan<kEpi>::kSmemBytes;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_pair_kernel<kEpi>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * (n / BN);
+  int pairs = sm_count() / 2;
+  if (pairs > tiles) pairs = tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(kNumThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fp8_gemm_pair_kernel<kEpi>, ma, mb_half, mo, sa, sw, bias, out,
+                            m, n, k, row_amax, wait_limit);
+}
+
 }  // namespace
+
+// FP8 GEMMs on SM pairs (256 x 256 tiles): 0 never, 1 the plain-epilogue GEMMs only
+// (the default: the GELU epilogue measured faster on one SM per tile, the plain one
+// on pairs), 2 always.
+static int g_fp8_pairing = 1;
+void set_fp8_gemm_pairing(int mode) { g_fp8_pairing = mode; }
 
 cudaError_t launch_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w, const float* sw,
                             const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
@@ -1334,13 +1637,25 @@ cudaError_t launch_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w,
   alignas(64) CUtensorMap mo;
   std::memset(&mo, 0, sizeof(mo));
   const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
-  if (epilogue == 1) {
-    if (!make_out_map(&mo, out, m, n)) {
-      if (why) *why = "cuTensorMapEncodeTiled failed for the output";
+  if (!make_out_map(&mo, out, m, n)) {
+    if (why) *why = "cuTensorMapEncodeTiled failed for the output";
+    return cudaErrorInvalidValue;
+  }
+  const bool pairs = g_fp8_pairing == 2 || (g_fp8_pairing == 1 && epilogue == 0);
+  if (pairs && sm_count() >= 2) {
+    alignas(64) CUtensorMap mb_half;
+    if (!make_byte_map(&mb_half, w, n, k, BN / 2)) {
+      if (why) *why = "cuTensorMapEncodeTiled failed for the SM-pair W map";
       return cudaErrorInvalidValue;
     }
-    return launch_fp8_gemm_t<1>(ma, mb, mo, sa, sw, bias, out, mi, ni, ki, row_amax, wait_limit, st);
+    if (epilogue == 1)
+      return launch_fp8_gemm_pair_t<1>(ma, mb_half, mo, sa, sw, bias, out, mi, ni, ki, row_amax,
+                                       wait_limit, st);
+    return launch_fp8_gemm_pair_t<0>(ma, mb_half, mo, sa, sw, bias, out, mi, ni, ki, nullptr,
+                                     wait_limit, st);
   }
+  if (epilogue == 1)
+    return launch_fp8_gemm_t<1>(ma, mb, mo, sa, sw, bias, out, mi, ni, ki, row_amax, wait_limit, st);
   return launch_fp8_gemm_t<0>(ma, mb, mo, sa, sw, bias, out, mi, ni, ki, nullptr, wait_limit, st);
 }
 

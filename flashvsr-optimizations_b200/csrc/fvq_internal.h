@@ -81,6 +81,10 @@ cudaError_t launch_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w,
                             int epilogue, uint32_t* row_amax, uint64_t wait_limit, cudaStream_t st,
                             const char** why);
 
+// FP8 GEMMs on SM pairs (fp8_gemm_pair_kernel, 256 x 256 tiles) or one SM per tile:
+// 0 never pairs, 1 pairs the plain-epilogue GEMMs (default), 2 pairs all.
+void set_fp8_gemm_pairing(int mode);
+
 // FP8 quantizers (fvq_fp8.cu).  Row: one scale per row, k % 8 == 0 and
 // k <= fp8_row_quant_max_k(); row_amax != NULL supplies each row's max |x| (fp32
 // bits); zero_rows != NULL gets zero in each row's word.  Tensor: one scale from a

@@ -312,6 +312,16 @@ int fvq_gelu_bf16_probe(const uint16_t* in, uint16_t* out, int64_t count, void* 
 int fvq_set_gemm_pairing(int enabled);
 
 /*
+ * Library setting with no reference counterpart: which FP8 GEMMs (fvq_fp8_scaled_mm,
+ * fvq_fp8_linear, fvq_fp8_ffn) run on pairs of SMs (clusters of two CTAs sharing
+ * 256 x 256 tiles, tcgen05 cta_group::2) instead of one SM per 128 x 256 tile:
+ * mode 0 none, 1 those with the plain bias epilogue (the default; the GELU epilogue
+ * of fvq_fp8_ffn's first GEMM runs faster on one SM), 2 all.  Every mode gives the
+ * same bits.  Applies to later launches.
+ */
+int fvq_set_fp8_gemm_pairing(int mode);
+
+/*
  * Bounded device waits: a GEMM whose pipeline wait exceeds the limit sets a
  * device error word and returns early (after letting its own copies and MMAs
  * drain).  fvq_set_wait_limit changes the limit, in nanoseconds of wall time

@@ -316,3 +316,28 @@ def test_install_ffn_fp8_mode():
     assert isinstance(ffn, FP8FFN) and ffn[0].mode == "fp8"
     y = ffn(x)
     assert y.shape == x.shape and torch.equal(y, ffn[2](ffn[1](ffn[0](x))))
+
+
+@pytest.mark.parametrize("m", [1, 129, 300, 384, 1000, 7680])
+def test_fp8_sm_pair_and_single_sm_gemms_give_the_same_bits(fp8_layer, m):
+    """The SM-pair kernels (256 x 256 tiles, cta_group::2; the default) and the
+    one-SM kernels agree bit for bit, including pair tiles over the end of A
+    (m = 129: the odd CTA holds one row; m = 384: its rows are all past the end)."""
+    from flashvsr_optimizations_b200 import _lib
+    ffn, _ = fp8_layer
+    lib = _lib.load()
+    x = bits_to_dev(W.student_t(m, W.D_MODEL, seed=m))
+    l1, l2 = ffn[0], ffn[2]
+    outs = []
+    try:
+        for mode in (2, 1, 0):  # all GEMMs paired, the default split, none
+            lib.fvq_set_fp8_gemm_pairing(mode)
+            y = ops.fp8_ffn(x, l1.qweight, l1.scale, l1.bias, l2.qweight, l2.scale, l2.bias)
+            h = ffn[1](ffn[0](x))
+            outs.append((y, h))
+    finally:
+        lib.fvq_set_fp8_gemm_pairing(1)
+    assert ops.read_device_error() == 0
+    for y, h in outs[1:]:
+        assert torch.equal(outs[0][1], h) and torch.equal(outs[0][0], y)
+    assert lib.fvq_set_fp8_gemm_pairing(3) == _lib.FVQ_EINVAL
