@@ -23,7 +23,8 @@ follow the timed steps (skip them with --no-extras): `stack_30_layers`, the
 ranks and the outputs all-gathered, `quantize_sweep` (rank 0), the
 activation quantizer on K in {1536, 8960} x M in {1024, 4096, 16384, 65536}, and
 `fp8_mode` (rank 0), the same layer in the reference's other mode,
-QuantLinear('fp8') (E4M3 W8A8, per-row scales).
+QuantLinear('fp8') (E4M3 W8A8, per-row scales), and `pil_resize` (rank 0), the
+input pipeline's Pillow-exact 4x bicubic resize of 32-frame chunks.
 
 `--impl reference` times the reference's NVFP4 FFN arithmetic on the host CPU
 (the oracle restatement; the reference itself needs FlashInfer on a GPU) with
@@ -500,6 +501,52 @@ def fp8_mode_timing(torch, ops, lib, dev, stream, tokens, fp8_peak, steps=200) -
     return out
 
 
+def pil_resize_timing(torch, dev, stream, hbm_peak, frames=32, iters=50) -> dict:
+    """The input pipeline's Pillow-exact resize (reference pil_exact_gpu.py): 32-frame
+    chunks of 426x240 RGB -> 1704x960 bicubic -> crop 1664x896, as bf16 [T,3,896,1664]
+    (fused with the normalisation) and as uint8 [T,896,1664,3]; device-timed, against
+    Pillow itself on this host (resize + crop, per frame, one thread)."""
+    from flashvsr_optimizations_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(11)
+    src = torch.randint(0, 256, (frames, 240, 426, 3), dtype=torch.uint8, device=dev, generator=g)
+    outb = torch.empty((frames, 3, 896, 1664), dtype=torch.bfloat16, device=dev)
+    out8 = torch.empty((frames, 896, 1664, 3), dtype=torch.uint8, device=dev)
+    sptr = stream.cuda_stream
+    res = {"frames_per_call": frames, "geometry": "426x240 -> 1704x960 bicubic, crop (20,32)-(1684,928)"}
+    for name, (u8, bf) in (("fused_bf16", (None, outb)), ("u8", (out8, None))):
+        def call():
+            rc = lib.fvq_pil_resize(src.data_ptr(), frames, 240, 426, 960, 1704, 32, 20, 896, 1664,
+                                    None if u8 is None else u8.data_ptr(),
+                                    None if bf is None else bf.data_ptr(), sptr)
+            if rc != 0:
+                raise RuntimeError(lib.fvq_last_error().decode())
+        for _ in range(5):
+            call()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(iters):
+            call()
+        e.record(stream)
+        e.synchronize()
+        ms = s.elapsed_time(e) / iters
+        out_bytes = frames * 896 * 1664 * 3 * (2 if bf is not None else 1)
+        nbytes = out_bytes + src.numel()
+        res[name] = {"ms_per_call": ms, "frames_per_s": frames / (ms * 1e-3),
+                     "GBps": nbytes / (ms * 1e-3) / 1e9, "frac_of_hbm": nbytes / (ms * 1e-3) / 1e9 / hbm_peak}
+    try:
+        from PIL import Image
+        host = src[:4].cpu().numpy()
+        t0 = time.perf_counter()
+        for f in host:
+            np.asarray(Image.fromarray(f).resize((1704, 960), Image.BICUBIC).crop((20, 32, 1684, 928)))
+        dt = (time.perf_counter() - t0) / len(host)
+        res["cpu_pillow_frames_per_s"] = 1.0 / dt
+    except Exception as exc:  # noqa: BLE001
+        res["cpu_pillow_frames_per_s"] = f"unavailable: {type(exc).__name__}"
+    return res
+
+
 def fp4_library_peak(torch, dev) -> float | None:
     """Dense NVFP4 throughput of cuBLASLt (torch._scaled_mm) at 8192^3, TFLOP/s, or None."""
     try:
@@ -664,6 +711,7 @@ def main():
             extras["quantize_sweep"] = quantize_sweep(torch, lib, dev, stream, hbm)
             fp8_peak = 2.0 * (bf16_sustained or 1400.0)
             extras["fp8_mode"] = fp8_mode_timing(torch, ops, lib, dev, stream, tokens, fp8_peak)
+            extras["pil_resize"] = pil_resize_timing(torch, dev, stream, hbm)
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,

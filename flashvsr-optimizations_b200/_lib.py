@@ -95,6 +95,9 @@ SIGNATURES = {
                                        _c.POINTER(FvqLinearFp8), _vp, _vp, _sz, _vp,
                                        _c.POINTER(_c.c_float)]),
     "fvq_div_full_probe": (_c.c_int, [_vp, _vp, _vp, _i64, _vp]),
+    "fvq_pil_resize": (_c.c_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                  _vp, _vp, _vp]),
+    "fvq_pil_normalize": (_c.c_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
     "fvq_rcp_approx_probe": (_c.c_int, [_vp, _vp, _i64, _vp]),
     "fvq_gelu_bf16_probe": (_c.c_int, [_vp, _vp, _i64, _vp]),
     "fvq_set_wait_limit": (_c.c_int, [_c.c_uint64]),

@@ -683,6 +683,58 @@ int fvq_div_full_probe(const float* a, const float* b, float* out, int64_t n, vo
   return FVQ_OK;
 }
 
+// ---------------------------------------------------------------- Pillow-exact resize
+
+int fvq_pil_resize(const uint8_t* src, int64_t frames, int64_t in_h, int64_t in_w, int64_t out_h,
+                   int64_t out_w, int64_t crop_y, int64_t crop_x, int64_t crop_h, int64_t crop_w,
+                   uint8_t* dst_u8, uint16_t* dst_bf16, void* stream) {
+  if (frames <= 0 || frames > 65535)
+    return fail(FVQ_EINVAL, "fvq_pil_resize: frames must be in [1, 65535] (got %lld)",
+                (long long)frames);
+  if (in_h <= 0 || in_w <= 0 || out_h < in_h || out_w < in_w || out_h > 32768 || out_w > 32768)
+    return fail(FVQ_EINVAL, "fvq_pil_resize: only upscaling is supported, sizes in [1, 32768] "
+                "(got %lldx%lld -> %lldx%lld)", (long long)in_w, (long long)in_h,
+                (long long)out_w, (long long)out_h);
+  if (crop_y < 0 || crop_x < 0 || crop_h <= 0 || crop_w <= 0 || crop_y + crop_h > out_h ||
+      crop_x + crop_w > out_w)
+    return fail(FVQ_EINVAL, "fvq_pil_resize: the crop must lie inside the output");
+  if (crop_w % 8 != 0)
+    return fail(FVQ_EINVAL, "fvq_pil_resize: crop_w must be a multiple of 8 (got %lld)",
+                (long long)crop_w);
+  if (!src || (!dst_u8 && !dst_bf16)) return fail(FVQ_EINVAL, "fvq_pil_resize: NULL pointer");
+  if (!aligned16(dst_u8) || !aligned16(dst_bf16))
+    return fail(FVQ_EALIGN, "fvq_pil_resize: outputs must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  size_t smem = 0;
+  cudaError_t e = fvq::launch_pil_resize(
+      src, frames, static_cast<int>(in_h), static_cast<int>(in_w), static_cast<int>(out_h),
+      static_cast<int>(out_w), static_cast<int>(crop_y), static_cast<int>(crop_x),
+      static_cast<int>(crop_h), static_cast<int>(crop_w), dst_u8, dst_bf16, &smem,
+      static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue)
+    return fail(FVQ_EINVAL, "fvq_pil_resize: a tile needs %zu bytes of shared memory (input too "
+                "wide for its scale)", smem);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_pil_resize launch");
+  return FVQ_OK;
+}
+
+int fvq_pil_normalize(const uint8_t* src, int64_t frames, int64_t h, int64_t w,
+                      int64_t stride_frame, int64_t stride_row, int64_t stride_col, uint16_t* dst,
+                      void* stream) {
+  if (frames <= 0 || h <= 0 || w <= 0 || w % 8 != 0)
+    return fail(FVQ_EINVAL, "fvq_pil_normalize: frames, h > 0 and w a positive multiple of 8");
+  if (stride_col < 3 || stride_row < stride_col * w || stride_frame < stride_row * h)
+    return fail(FVQ_EINVAL, "fvq_pil_normalize: strides must describe non-overlapping HWC pixels");
+  if (!src || !dst) return fail(FVQ_EINVAL, "fvq_pil_normalize: NULL pointer");
+  if (!aligned16(dst)) return fail(FVQ_EALIGN, "fvq_pil_normalize: dst must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  cudaError_t e = fvq::launch_pil_normalize(src, frames, static_cast<int>(h), static_cast<int>(w),
+                                            stride_frame, stride_row, stride_col, dst,
+                                            static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_pil_normalize launch");
+  return FVQ_OK;
+}
+
 int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream) {
   if (n < 0 || (n > 0 && (!in || !out))) return fail(FVQ_EINVAL, "fvq_rcp_approx_probe: bad args");
   if (int rc = check_device()) return rc;

@@ -97,6 +97,15 @@ cudaError_t launch_fp8_tensor_quant(const uint16_t* x, int64_t numel, const floa
                                     uint8_t* q, float* scale, cudaStream_t st);
 cudaError_t launch_div_full_probe(const float* a, const float* b, float* out, int64_t n,
                                   cudaStream_t st);
+// Pillow-exact bicubic upscale + crop (+ bf16 normalisation), and the normalisation on
+// its own (fvq_resize.cu).  smem_needed receives the CTA's shared memory; a plan that does
+// not fit returns cudaErrorInvalidValue.
+cudaError_t launch_pil_resize(const uint8_t* src, int64_t frames, int in_h, int in_w, int out_h,
+                              int out_w, int crop_y, int crop_x, int crop_h, int crop_w,
+                              uint8_t* dst_u8, uint16_t* dst_bf16, size_t* smem_needed,
+                              cudaStream_t st);
+cudaError_t launch_pil_normalize(const uint8_t* src, int64_t frames, int h, int w, int64_t sb,
+                                 int64_t sy, int64_t sx, uint16_t* dst, cudaStream_t st);
 cudaError_t set_error_word(uint32_t v, cudaStream_t st);
 uint32_t* error_word_ptr();   // device address of the error word (current device)
 cudaError_t read_error_word(uint32_t* v, cudaStream_t st);

@@ -284,6 +284,37 @@ int fvq_fp8_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear_fp8* l
                         size_t workspace_bytes, void* stream, float* kernel_ms);
 
 /*
+ * ---------------------------------------------------------------------------
+ * Pillow-exact bicubic resize of the input pipeline (reference pil_exact_gpu.py:
+ * 30-150, used by chunked_input.py:111-113).
+ * ---------------------------------------------------------------------------
+ *
+ * RGB uint8 frames [frames, in_h, in_w, 3] resized to out_w x out_h exactly as
+ * Pillow's Image.resize(..., BICUBIC) does (22-bit fixed-point separable
+ * passes, horizontal first, each rounded and clipped to uint8), cropped to
+ * [crop_y, crop_y + crop_h) x [crop_x, crop_x + crop_w), and written as
+ *   dst_u8:   uint8 [frames, crop_h, crop_w, 3]        (resize_exact_gpu), and/or
+ *   dst_bf16: bf16 [frames, 3, crop_h, crop_w] of p / 255 * 2 - 1 (fp32, then
+ *             bf16) -- normalize_exact_gpu(resize_exact_gpu(frames)) in one pass.
+ * Either output may be NULL (not both).  Upscaling only (out_h >= in_h,
+ * out_w >= in_w); crop_w % 8 == 0; frames <= 65535; outputs 16-byte aligned.
+ * The reference's geometry is 426x240 -> 1704x960, crop (32, 20, 896, 1664).
+ */
+int fvq_pil_resize(const uint8_t* src, int64_t frames, int64_t in_h, int64_t in_w, int64_t out_h,
+                   int64_t out_w, int64_t crop_y, int64_t crop_x, int64_t crop_h, int64_t crop_w,
+                   uint8_t* dst_u8, uint16_t* dst_bf16, void* stream);
+
+/*
+ * normalize_exact_gpu on its own (pil_exact_gpu.py:115-150): uint8 pixels
+ * [frames, h, w, 3] at element strides (stride_frame, stride_row, stride_col;
+ * the three channels adjacent) -> bf16 [frames, 3, h, w] of p / 255 * 2 - 1.
+ * w % 8 == 0; dst 16-byte aligned.
+ */
+int fvq_pil_normalize(const uint8_t* src, int64_t frames, int64_t h, int64_t w,
+                      int64_t stride_frame, int64_t stride_row, int64_t stride_col, uint16_t* dst,
+                      void* stream);
+
+/*
  * Test support: out[i] = div.full.f32(a[i], b[i]) on the device, the division
  * the FP8 quantizers (and the reference's Triton `/`) use.
  */
