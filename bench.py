@@ -71,6 +71,9 @@ def parse():
                     help="skip the quantize sweep and the 30-layer stack (separate measurements)")
     ap.add_argument("--cpu-seconds", type=float, default=20.0,
                     help="wall-time budget of the CPU baseline sample")
+    ap.add_argument("--case", choices=("ffn", "fp8_ffn", "pil_resize"), default="ffn",
+                    help="ffn: the benchmark (default); fp8_ffn / pil_resize: only that separate "
+                         "measurement, --steps calls, one JSON line (e.g. under a profiler)")
     return ap.parse_args()
 
 
@@ -596,6 +599,17 @@ def main():
     from flashvsr_optimizations_b200.ffn_quantization import NVFP4FFN
     lib = _lib.load()
     tokens = args.tokens
+    if args.case != "ffn":
+        stream = torch.cuda.current_stream(dev)
+        hbm = measured_peaks().get("hbm_gbs") or 6650.0
+        if args.case == "fp8_ffn":
+            peak8 = 2.0 * (measured_peaks().get("bf16_tflops_sustained") or 1400.0)
+            out = fp8_mode_timing(torch, ops, lib, dev, stream, tokens, peak8, steps=args.steps)
+        else:
+            out = pil_resize_timing(torch, dev, stream, hbm, iters=args.steps)
+        if rank == 0:
+            print(json.dumps({"case": args.case, **out}), flush=True)
+        return
     sets = make_sets(torch, ops, dev, tokens, rank)
     ws_bytes = lib.fvq_nvfp4_ffn_workspace_bytes(tokens, D_MODEL, D_FF)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
