@@ -20,7 +20,7 @@ import torch
 from . import _lib
 
 __all__ = [
-    "amax", "global_scale", "nvfp4_quantize", "mm_fp4", "nvfp4_gemm",
+    "amax", "global_scale", "nvfp4_quantize", "nvfp4_quantize_from_amax", "mm_fp4", "nvfp4_gemm",
     "nvfp4_linear", "nvfp4_ffn", "rcp_approx_probe", "sf_rows", "read_device_error",
     "fp8_row_quant", "fp8_quantize_activation", "fp8_scaled_mm", "fp8_linear", "fp8_ffn",
     "div_full_probe",
@@ -155,6 +155,34 @@ def _(x, g):
     m, k = x.shape
     return (x.new_empty((m, k // 2), dtype=torch.uint8),
             x.new_empty((sf_rows(m), k // 16), dtype=torch.uint8))
+
+
+@torch.library.custom_op("fvq::nvfp4_quantize_from_amax", mutates_args=())
+def nvfp4_quantize_from_amax(x: torch.Tensor, amax: torch.Tensor
+                             ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(codes, scales, g) with g = 2688 / max(amax, 1e-12) from a given max |x| (e.g. one
+    all-reduced over ranks): ``nvfp4_quantize(x, global_scale(...))`` with the amax supplied."""
+    _check_cuda("nvfp4_quantize_from_amax", x, amax)
+    _check_bf16("nvfp4_quantize_from_amax", x)
+    if x.dim() != 2:
+        raise ValueError("nvfp4_quantize_from_amax: expected a 2-D [M, K] tensor")
+    m, k = x.shape
+    x = _aligned32(x)
+    a = amax.to(torch.float32).reshape(1).contiguous()
+    codes = torch.empty((m, k // 2), dtype=torch.uint8, device=x.device)
+    sf = torch.empty((sf_rows(m), k // 16), dtype=torch.uint8, device=x.device)
+    g = torch.empty(1, dtype=torch.float32, device=x.device)
+    _lib.call("fvq_nvfp4_quantize_dynamic", _ptr(x), m, k, _ptr(a), _ptr(g), _ptr(codes), _ptr(sf),
+              None, 0, _stream(x))
+    return codes, sf, g
+
+
+@nvfp4_quantize_from_amax.register_fake
+def _(x, amax):
+    m, k = x.shape
+    return (x.new_empty((m, k // 2), dtype=torch.uint8),
+            x.new_empty((sf_rows(m), k // 16), dtype=torch.uint8),
+            x.new_empty(1, dtype=torch.float32))
 
 
 @torch.library.custom_op("fvq::mm_fp4", mutates_args=())

@@ -4,15 +4,22 @@ Token rows are independent through the whole FFN, so the path partitions them:
 each rank runs the FFN on a contiguous block of rows with replicated weights,
 and no collective sits inside a layer.  Outputs are gathered with one
 all-gather (NCCL over NVLink on GPUs, gloo in the CPU tests) when a single
-rank needs all of them.  Global scales are per shard: each shard computes
-exactly what the reference computes when run on that shard.
+rank needs all of them.  By default global scales are per shard: each shard
+computes exactly what the reference computes when run on that shard.  With
+``global_scales=True`` an NVFP4 FFN instead all-reduces (MAX) the 4-byte amax
+of each activation it quantizes -- x, then the GELU output h -- so every shard
+uses the scale of the whole tensor and the gathered output equals the
+single-GPU result bit for bit (two tiny collectives per layer; off by
+default).  The FP8 mode's scales are per row, so its shards agree with the
+single-GPU result either way.
 """
 from __future__ import annotations
 
 import torch
 import torch.distributed as dist
 
-__all__ = ["row_range", "shard_rows", "gather_rows", "ShardedFFN"]
+__all__ = ["row_range", "shard_rows", "gather_rows", "global_amax", "nvfp4_ffn_global_scales",
+           "ShardedFFN"]
 
 
 def row_range(total: int, world: int, rank: int) -> tuple[int, int]:
@@ -58,17 +65,47 @@ def gather_rows(local: torch.Tensor, total: int, group=None) -> torch.Tensor:
     return torch.cat(parts, dim=0)
 
 
+def global_amax(amax: torch.Tensor, group=None) -> torch.Tensor:
+    """max over ranks of a per-rank amax (1-element fp32 tensor), in place; 4 bytes on the wire."""
+    dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+    return amax
+
+
+def nvfp4_ffn_global_scales(x: torch.Tensor, ffn, group=None,
+                            reduce_amax=global_amax) -> torch.Tensor:
+    """An NVFP4 FFN (NVFP4FFN or Sequential of QuantLinear, GELU, QuantLinear) on this
+    rank's rows with the global scales of the whole activation: amax(x) and amax(h) are
+    reduced over the ranks before each quantization (ffn_quantization.py:29-32 applied to
+    the full tensor).  `reduce_amax(amax, group)` is the reduction (all_reduce MAX)."""
+    from . import ops
+    l1, l2 = ffn[0], ffn[2]
+    a = ops.amax(x) if x.shape[0] > 0 else x.new_zeros(1, dtype=torch.float32)
+    a = reduce_amax(a, group)
+    if x.shape[0] == 0:  # this rank has no rows: it still takes part in both reductions
+        reduce_amax(x.new_zeros(1, dtype=torch.float32), group)
+        return x.new_empty((0, l2.out_features))
+    q, s, g = ops.nvfp4_quantize_from_amax(x, a)
+    h, amax_h = ops.nvfp4_gemm(q, s, g, l1.qweight, l1.scale, l1.global_sf, l1.bias, gelu=True)
+    amax_h = reduce_amax(amax_h, group)
+    qh, sh, gh = ops.nvfp4_quantize_from_amax(h, amax_h)
+    y, _ = ops.nvfp4_gemm(qh, sh, gh, l2.qweight, l2.scale, l2.global_sf, l2.bias, gelu=False)
+    return y
+
+
 class ShardedFFN(torch.nn.Module):
     """Run `ffn` on this rank's token rows and all-gather the result.
 
     `forward(x)` takes the full [tokens, d] activation (every rank holds it, as
     when a video chunk is broadcast) and returns the full output on every rank.
+    `global_scales=True` (NVFP4 FFNs): scales of the whole tensor, see
+    nvfp4_ffn_global_scales.
     """
 
-    def __init__(self, ffn: torch.nn.Module, group=None):
+    def __init__(self, ffn: torch.nn.Module, group=None, global_scales: bool = False):
         super().__init__()
         self.ffn = ffn
         self.group = group
+        self.global_scales = global_scales
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         world = dist.get_world_size(self.group)
@@ -76,6 +113,9 @@ class ShardedFFN(torch.nn.Module):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1])
         local = shard_rows(x2, world, rank)
-        y_local = self.ffn(local) if local.shape[0] > 0 else local.new_empty((0, shape[-1]))
+        if self.global_scales:
+            y_local = nvfp4_ffn_global_scales(local, self.ffn, self.group)
+        else:
+            y_local = self.ffn(local) if local.shape[0] > 0 else local.new_empty((0, shape[-1]))
         y = gather_rows(y_local, x2.shape[0], self.group)
         return y.reshape(*shape[:-1], y.shape[-1])

@@ -212,3 +212,31 @@ def test_ffn_same_bits_with_and_without_sm_pairs(ffn_layer):
         _lib.call("fvq_set_gemm_pairing", 0)
     torch.cuda.synchronize()
     assert torch.equal(paired, single)
+
+
+def test_global_scale_shards_reproduce_the_single_gpu_layer(ffn_layer):
+    """Sharding with global scales (sharding.nvfp4_ffn_global_scales): each shard quantizes
+    with the amax of the whole tensor, so the gathered rows equal the unsharded FFN bit for
+    bit.  The reductions are emulated in one process by a reducer that returns the
+    whole-tensor maxima (what all_reduce(MAX) over the shards yields)."""
+    from flashvsr_optimizations_b200.sharding import nvfp4_ffn_global_scales, row_range
+    ffn, _ = ffn_layer
+    x = bits_to_dev(W.student_t(1000, W.D_MODEL, seed=17))
+    l1 = ffn[0]
+    a_full = ops.amax(x)
+    q, s, g = ops.nvfp4_quantize_from_amax(x, a_full)
+    assert torch.equal(g, ops.global_scale(x))
+    _, amax_h_full = ops.nvfp4_gemm(q, s, g, l1.qweight, l1.scale, l1.global_sf, l1.bias, gelu=True)
+    want = ffn(x)
+    parts = []
+    for world in (2, 3):
+        parts = []
+        for rank in range(world):
+            lo, hi = row_range(x.shape[0], world, rank)
+            maxima = iter([a_full.clone(), amax_h_full.clone()])
+            parts.append(nvfp4_ffn_global_scales(x[lo:hi], ffn, reduce_amax=lambda a, grp: next(maxima)))
+        assert torch.equal(torch.cat(parts), want), world
+    # a rank without rows still takes part in both reductions
+    calls = []
+    empty = nvfp4_ffn_global_scales(x[:0], ffn, reduce_amax=lambda a, grp: calls.append(1) or a)
+    assert empty.shape == (0, W.D_MODEL) and len(calls) == 2

@@ -105,3 +105,30 @@ def test_dead_rank_makes_gather_fail_instead_of_hanging():
         if p.is_alive():
             p.kill()
     assert rank == 0 and outcome != "no error"
+
+
+def _amax_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+        from flashvsr_optimizations_b200.sharding import global_amax
+        a = torch.tensor([float(rank + 1) * 1.5])
+        global_amax(a)
+        q.put((rank, float(a.item())))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+
+
+def test_global_amax_is_the_max_over_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_amax_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(3)]
+    for p in procs:
+        p.join(timeout=60)
+    assert sorted(v for _, v in results) == [4.5, 4.5, 4.5]
