@@ -23,8 +23,10 @@ follow the timed steps (skip them with --no-extras): `stack_30_layers`, the
 ranks and the outputs all-gathered, `quantize_sweep` (rank 0), the
 activation quantizer on K in {1536, 8960} x M in {1024, 4096, 16384, 65536}, and
 `fp8_mode` (rank 0), the same layer in the reference's other mode,
-QuantLinear('fp8') (E4M3 W8A8, per-row scales), and `pil_resize` (rank 0), the
-input pipeline's Pillow-exact 4x bicubic resize of 32-frame chunks.
+QuantLinear('fp8') (E4M3 W8A8, per-row scales), `pil_resize` (rank 0), the
+input pipeline's Pillow-exact 4x bicubic resize of 32-frame chunks, and
+`dit_block` (rank 0), the DiT block's step around the layer (LayerNorm +
+modulation in, gated residual out) fused against torch's composition.
 
 `--impl reference` times the reference's NVFP4 FFN arithmetic on the host CPU
 (the oracle restatement; the reference itself needs FlashInfer on a GPU) with
@@ -71,9 +73,9 @@ def parse():
                     help="skip the quantize sweep and the 30-layer stack (separate measurements)")
     ap.add_argument("--cpu-seconds", type=float, default=20.0,
                     help="wall-time budget of the CPU baseline sample")
-    ap.add_argument("--case", choices=("ffn", "fp8_ffn", "pil_resize"), default="ffn",
-                    help="ffn: the benchmark (default); fp8_ffn / pil_resize: only that separate "
-                         "measurement, --steps calls, one JSON line (e.g. under a profiler)")
+    ap.add_argument("--case", choices=("ffn", "fp8_ffn", "pil_resize", "dit_block"), default="ffn",
+                    help="ffn: the benchmark (default); fp8_ffn / pil_resize / dit_block: only that "
+                         "separate measurement, --steps calls, one JSON line (e.g. under a profiler)")
     return ap.parse_args()
 
 
@@ -504,6 +506,78 @@ def fp8_mode_timing(torch, ops, lib, dev, stream, tokens, fp8_peak, steps=200) -
     return out
 
 
+def dit_block_timing(torch, lib, dev, stream, sets, tokens, hbm_peak, steps=200) -> dict:
+    """The DiT block's FFN step around the layer, x + gate * FFN(LN(x) * (1 + scale) + shift)
+    (LN without affine, eps 1e-6): fvq_nvfp4_ffn_block (the LayerNorm + modulation kernel,
+    the layer's four launches, the gated residual in GEMM2's epilogue) against the same
+    step composed of torch's layer_norm and elementwise ops around fvq_nvfp4_ffn, both
+    device-timed over `steps` calls rotating over the benchmark's sets; and the
+    LayerNorm + modulation kernel alone (one read of x, one write of u: 4 bytes a value)."""
+    from flashvsr_optimizations_b200 import _lib
+    import torch.nn.functional as F
+    g = torch.Generator(device=dev).manual_seed(13)
+    shift, scale, gate = ((s * torch.randn(D_MODEL, device=dev, generator=g)).to(torch.bfloat16)
+                          for s in (0.2, 0.2, 0.5))
+    eps = 1e-6
+    bound = []
+    for x, ((q1, s1, g1, b1), (q2, s2, g2, b2)) in sets:
+        l1 = _lib.FvqLinear(q1.data_ptr(), s1.data_ptr(), g1.data_ptr(), b1.data_ptr(), D_MODEL, D_FF)
+        l2 = _lib.FvqLinear(q2.data_ptr(), s2.data_ptr(), g2.data_ptr(), b2.data_ptr(), D_FF, D_MODEL)
+        bound.append((x, l1, l2))
+    n = len(bound)
+    bws = lib.fvq_nvfp4_ffn_block_workspace_bytes(tokens, D_MODEL, D_FF)
+    fws = lib.fvq_nvfp4_ffn_workspace_bytes(tokens, D_MODEL, D_FF)
+    ws = torch.zeros(bws, dtype=torch.uint8, device=dev)
+    out = torch.empty(tokens, D_MODEL, dtype=torch.bfloat16, device=dev)
+    y = torch.empty_like(out)
+    u = torch.empty_like(out)
+    sptr = stream.cuda_stream
+    ptrs = (shift.data_ptr(), scale.data_ptr(), gate.data_ptr())
+
+    def check(rc):
+        if rc != 0:
+            raise RuntimeError(lib.fvq_last_error().decode())
+
+    def fused(i):
+        x, l1, l2 = bound[i % n]
+        check(lib.fvq_nvfp4_ffn_block(x.data_ptr(), tokens, *ptrs, ctypes.c_float(eps),
+                                      ctypes.byref(l1), ctypes.byref(l2), out.data_ptr(),
+                                      ws.data_ptr(), bws, sptr))
+
+    def composed(i):
+        x, l1, l2 = bound[i % n]
+        v = F.layer_norm(x, (D_MODEL,), eps=eps) * (1 + scale) + shift
+        check(lib.fvq_nvfp4_ffn(v.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2),
+                                y.data_ptr(), ws.data_ptr(), fws, sptr))
+        torch.add(x, gate * y, out=out)
+
+    def ln_only(i):
+        x = bound[i % n][0]
+        check(lib.fvq_ln_modulate(x.data_ptr(), tokens, D_MODEL, ptrs[0], ptrs[1],
+                                  ctypes.c_float(eps), u.data_ptr(), sptr))
+
+    res = {"step": "x + gate * FFN(LN(x) * (1 + scale) + shift), LN without affine, eps 1e-6",
+           "tokens": tokens}
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for name, fn, k in (("fused_fvq_nvfp4_ffn_block", fused, steps),
+                        ("torch_ln_modulate_gate_around_fvq_nvfp4_ffn", composed, steps),
+                        ("ln_modulate_kernel", ln_only, 4 * steps)):
+        for i in range(5):
+            fn(i)
+        torch.cuda.synchronize(dev)
+        s.record(stream)
+        for i in range(k):
+            fn(i)
+        e.record(stream)
+        e.synchronize()
+        ms = s.elapsed_time(e) / k
+        res[name] = {"ms": ms, "tokens_per_s": tokens / (ms * 1e-3)}
+    gbs = 4 * tokens * D_MODEL / (res["ln_modulate_kernel"]["ms"] * 1e-3) / 1e9
+    res["ln_modulate_kernel"].update({"GBps": gbs, "peak_GBps": hbm_peak, "frac": gbs / hbm_peak})
+    res["l2"] = f"{n} rotating activation/weight sets"
+    return res
+
+
 def pil_resize_timing(torch, dev, stream, hbm_peak, frames=32, iters=50) -> dict:
     """The input pipeline's Pillow-exact resize (reference pil_exact_gpu.py): 32-frame
     chunks of 426x240 RGB -> 1704x960 bicubic -> crop 1664x896, as bf16 [T,3,896,1664]
@@ -605,6 +679,9 @@ def main():
         if args.case == "fp8_ffn":
             peak8 = 2.0 * (measured_peaks().get("bf16_tflops_sustained") or 1400.0)
             out = fp8_mode_timing(torch, ops, lib, dev, stream, tokens, peak8, steps=args.steps)
+        elif args.case == "dit_block":
+            out = dit_block_timing(torch, lib, dev, stream, make_sets(torch, ops, dev, tokens, rank)[:4],
+                                   tokens, hbm, steps=args.steps)
         else:
             out = pil_resize_timing(torch, dev, stream, hbm, iters=args.steps)
         if rank == 0:
@@ -726,6 +803,7 @@ def main():
             fp8_peak = 2.0 * (bf16_sustained or 1400.0)
             extras["fp8_mode"] = fp8_mode_timing(torch, ops, lib, dev, stream, tokens, fp8_peak)
             extras["pil_resize"] = pil_resize_timing(torch, dev, stream, hbm)
+            extras["dit_block"] = dit_block_timing(torch, lib, dev, stream, sets, tokens, hbm)
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,

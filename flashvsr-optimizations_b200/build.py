@@ -22,8 +22,8 @@ INCLUDE = HERE.parent / "include"
 BUILD = HERE / "_build"
 LIB = HERE / "libfvq.so"
 
-SOURCES = ["fvq_quant.cu", "fvq_fp8.cu", "fvq_resize.cu", "fvq_gemm.cu", "fvq_api.cu",
-           "fvq_noalloc.cu"]
+SOURCES = ["fvq_quant.cu", "fvq_fp8.cu", "fvq_resize.cu", "fvq_block.cu", "fvq_gemm.cu",
+           "fvq_api.cu", "fvq_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
     "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2",

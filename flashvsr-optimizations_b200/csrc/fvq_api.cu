@@ -98,10 +98,12 @@ int check_gemm_shape(int64_t m, int64_t n, int64_t k) {
 int gemm_impl(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
               const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w, const float* alpha,
               const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k, int epilogue,
-              float* amax_out, cudaStream_t st, const uint8_t* w_sf_rep = nullptr) {
+              float* amax_out, cudaStream_t st, const uint8_t* w_sf_rep = nullptr,
+              const uint16_t* residual = nullptr, const uint16_t* gate = nullptr) {
   const char* why = nullptr;
   cudaError_t e = fvq::launch_gemm(a_codes, a_sf, g_a, w_codes, w_sf, g_w, alpha, bias, out, m, n, k,
-                                   epilogue, amax_out, g_wait_limit, st, &why, w_sf_rep);
+                                   epilogue, amax_out, g_wait_limit, st, &why, w_sf_rep, residual,
+                                   gate);
   if (e != cudaSuccess) {
     if (why) return fail(FVQ_ECUDA, "fvq_nvfp4_gemm: %s", why);
     return cuda_fail(e, "fvq_nvfp4_gemm launch");
@@ -327,10 +329,11 @@ size_t fvq_nvfp4_ffn_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff
 namespace {
 
 // The FFN launch sequence.  ev: NULL, or 5 events recorded before the first
-// launch and after each of the four (for fvq_nvfp4_ffn_profile).
+// launch and after each of the four (for fvq_nvfp4_ffn_profile).  residual and
+// gate (both or neither): GEMM2 writes the gated residual residual + gate * FFN(x).
 int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
              uint16_t* y, void* workspace, size_t workspace_bytes, cudaStream_t st,
-             cudaEvent_t* ev) {
+             cudaEvent_t* ev, const uint16_t* residual = nullptr, const uint16_t* gate = nullptr) {
   if (int rc = check_linear(lin1, "fvq_nvfp4_ffn (linear 1)")) return rc;
   if (int rc = check_linear(lin2, "fvq_nvfp4_ffn (linear 2)")) return rc;
   if (lin1->out_features != lin2->in_features || lin2->out_features != lin1->in_features)
@@ -382,9 +385,10 @@ int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_
                            /*scratch_input=*/true);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(h) launch");
   mark(3);
-  // 4. y = bf16(bf16(alpha2 * acc) + b2)
+  // 4. y = bf16(bf16(alpha2 * acc) + b2)  [then bf16(residual + bf16(gate * y))]
   if (int rc = gemm_impl(codes_h, sf_h, g_h, lin2->qweight, lin2->scale, lin2->global_sf, nullptr,
-                         lin2->bias, y, rows, d, f, FVQ_EPI_BF16, nullptr, st, sf_w2_rep))
+                         lin2->bias, y, rows, d, f, residual ? 2 : FVQ_EPI_BF16, nullptr, st,
+                         sf_w2_rep, residual, gate))
     return rc;
   mark(4);
   return FVQ_OK;
@@ -396,6 +400,63 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
                   uint16_t* y, void* workspace, size_t workspace_bytes, void* stream) {
   return ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes,
                   static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int fvq_ln_modulate(const uint16_t* x, int64_t rows, int64_t d, const uint16_t* shift,
+                    const uint16_t* scale, float eps, uint16_t* u, void* stream) {
+  if (rows <= 0 || d <= 0 || d % 8 != 0 || d > 2048)
+    return fail(FVQ_EINVAL, "fvq_ln_modulate: rows > 0 and d a multiple of 8 up to 2048 "
+                "(got %lld, %lld)", (long long)rows, (long long)d);
+  if (!(eps >= 0.0f)) return fail(FVQ_EINVAL, "fvq_ln_modulate: eps must be >= 0");
+  if (!x || !shift || !scale || !u) return fail(FVQ_EINVAL, "fvq_ln_modulate: NULL pointer");
+  if (!aligned16(x) || !aligned16(shift) || !aligned16(scale) || !aligned16(u))
+    return fail(FVQ_EALIGN, "fvq_ln_modulate: pointers must be 16-byte aligned");
+  if (int rc = check_device()) return rc;
+  cudaError_t e = fvq::launch_ln_modulate(x, rows, d, shift, scale, eps, u,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_ln_modulate launch");
+  return FVQ_OK;
+}
+
+size_t fvq_nvfp4_ffn_block_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff) {
+  if (rows <= 0 || d_model <= 0 || d_ff <= 0) return 0;
+  return round_up(static_cast<size_t>(rows * d_model * 2)) +
+         fvq_nvfp4_ffn_workspace_bytes(rows, d_model, d_ff);
+}
+
+int fvq_nvfp4_ffn_block(const uint16_t* x, int64_t rows, const uint16_t* shift,
+                        const uint16_t* scale, const uint16_t* gate, float eps,
+                        const fvq_linear* lin1, const fvq_linear* lin2, uint16_t* out,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_linear(lin1, "fvq_nvfp4_ffn_block (linear 1)")) return rc;
+  if (int rc = check_linear(lin2, "fvq_nvfp4_ffn_block (linear 2)")) return rc;
+  const int64_t d = lin1->in_features;
+  if (lin2->out_features != d)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_block: the FFN must map d_model back to d_model");
+  if (d > 2048 || d % 8 != 0)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_block: d_model must be a multiple of 8 up to 2048 "
+                "(got %lld)", (long long)d);
+  if (!(eps >= 0.0f)) return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_block: eps must be >= 0");
+  if (!x || !shift || !scale || !gate || !out || !workspace)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_block: NULL pointer");
+  if (rows <= 0) return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_block: rows must be > 0");
+  const size_t need = fvq_nvfp4_ffn_block_workspace_bytes(rows, d, lin1->out_features);
+  if (workspace_bytes < need)
+    return fail(FVQ_EWORKSPACE, "fvq_nvfp4_ffn_block: workspace needs %zu bytes, got %zu", need,
+                workspace_bytes);
+  if (!aligned16(x) || !aligned16(shift) || !aligned16(scale) || !aligned16(gate) ||
+      !aligned16(out) || !aligned32(workspace))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_ffn_block: pointers must be 16-byte aligned, the "
+                "workspace 32-byte");
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the FFN's workspace first, so that its zero-state amax counters sit at offset 0
+  // whatever the row count; u after it
+  const size_t ffn_bytes = fvq_nvfp4_ffn_workspace_bytes(rows, d, lin1->out_features);
+  uint16_t* u = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + ffn_bytes);
+  cudaError_t e = fvq::launch_ln_modulate(x, rows, d, shift, scale, eps, u, st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn_block layer norm launch");
+  return ffn_impl(u, rows, lin1, lin2, out, workspace, ffn_bytes, st, nullptr, x, gate);
 }
 
 int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,

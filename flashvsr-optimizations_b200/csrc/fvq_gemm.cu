@@ -76,7 +76,7 @@ template <int kEpi, bool kResident, bool kRepSfb = false>
 struct Plan {
   static constexpr int kStageBytes =
       kABytes + kBBytes + kSfaBytes + (kResident ? 0 : (kRepSfb ? kSfbRepBytes : kSfbBytes));
-  static constexpr int kStages = kEpi == 0 ? (kRepSfb ? 3 : 4) : (kResident ? 3 : 2);
+  static constexpr int kStages = kEpi != 1 ? (kRepSfb ? 3 : 4) : (kResident ? 3 : 2);
   static constexpr bool kStaged = kEpi == 1;
   static constexpr int kStagingOff = kStages * kStageBytes;
   static constexpr int kTableOff = kStagingOff + (kStaged ? kStagingBytes : 0);
@@ -218,6 +218,14 @@ __device__ __forceinline__ uint32_t scale_pack_bf16x2(uint32_t lo_bits, uint32_t
   return pack_bf16x2(lo, hi);
 }
 
+// bf16x2 product, one rounding of the exact product (two 8-bit mantissas fit in fp32, so
+// torch's fp32 multiply followed by a bf16 rounding gives the same value).
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 // bf16x2 add, one rounding of the exact sum.  For two bf16 operands this equals
 // torch's fp32 add followed by a bf16 rounding: the fp32 sum is exact unless
 // the exponents differ by more than 16, and then it lies far from a bf16 tie.
@@ -285,7 +293,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                       const uint8_t* __restrict__ w_sf, const float* __restrict__ g_a,
                       const float* __restrict__ g_w, const float* __restrict__ alpha_in,
                       const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m, int n,
-                      int k, float* amax_out, uint64_t wait_limit) {
+                      int k, float* amax_out, uint64_t wait_limit,
+                      const uint16_t* __restrict__ residual, const uint16_t* __restrict__ gate) {
   using P = Plan<kEpi, kResident, kRepSfb>;
   constexpr int kStages = P::kStages;
   constexpr int kStageBytes = P::kStageBytes;
@@ -306,7 +315,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int num_k_tiles = k / BK;
   const int64_t sf_tile_stride = static_cast<int64_t>(k / 64) * 512;  // bytes per 128-row block
   const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
-  const TileSeq<kResident, kEpi == 0> seq(num_m_blocks, num_n_blocks);
+  const TileSeq<kResident, kEpi != 1> seq(num_m_blocks, num_n_blocks);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -579,6 +588,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             uint32_t w = y[c / 2 + j];
             if (bias != nullptr) w = add_bf16x2(w, bw[j]);
             o[j] = w;
+          }
+          if constexpr (kEpi == 2) {
+            // gated residual: out = bf16(x + bf16(gate * y)), each a single bf16 rounding
+            const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gate + col0 + c));
+            uint4 xv = make_uint4(0, 0, 0, 0);
+            if (row < m)
+              xv = __ldg(reinterpret_cast<const uint4*>(residual + static_cast<int64_t>(row) * n +
+                                                        col0 + c));
+            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] = add_bf16x2(xw[j], mul_bf16x2(gw[j], o[j]));
           }
           if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
         }
@@ -1482,7 +1502,8 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CU
                           const uint8_t* a_sf,
                           const uint8_t* w_sf, const float* g_a, const float* g_w,
                           const float* alpha, const uint16_t* bias, uint16_t* out, int m, int n,
-                          int k, float* amax_out, uint64_t wait_limit, cudaStream_t st) {
+                          int k, float* amax_out, uint64_t wait_limit, cudaStream_t st,
+                          const uint16_t* residual = nullptr, const uint16_t* gate = nullptr) {
   static bool attr_set[64] = {false};
   constexpr int kSmemBytes = Plan<kEpi, kResident, kRepSfb>::kSmemBytes;
   int dev = 0;
@@ -1497,7 +1518,8 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CU
   int grid = sm_count();
   if (grid > tiles) grid = tiles;
   nvfp4_gemm_kernel<kEpi, kResident, kRepSfb><<<grid, kNumThreads, kSmemBytes, st>>>(
-      ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit);
+      ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit, residual,
+      gate);
   return cudaGetLastError();
 }
 
@@ -1670,7 +1692,8 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
                         const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
                         int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
-                        const char** why, const uint8_t* w_sf_rep) {
+                        const char** why, const uint8_t* w_sf_rep, const uint16_t* residual,
+                        const uint16_t* gate) {
   alignas(64) CUtensorMap ma;
   alignas(64) CUtensorMap mb;
   if (!make_code_map(&ma, a_codes, m, k, BM) || !make_code_map(&mb, w_codes, n, k, BN)) {
@@ -1692,6 +1715,14 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                                     amax_out, wait_limit, st);
     return launch_gemm_t<1, false>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
                                    amax_out, wait_limit, st);
+  }
+  if (epilogue == 2) {
+    if (w_sf_rep == nullptr || residual == nullptr || gate == nullptr) {
+      if (why) *why = "the gated-residual epilogue needs replicated W scales, residual and gate";
+      return cudaErrorInvalidValue;
+    }
+    return launch_gemm_t<2, false, true>(ma, mb, mo, a_sf, w_sf_rep, g_a, g_w, alpha, bias, out, mi,
+                                         ni, ki, amax_out, wait_limit, st, residual, gate);
   }
   if (gemm_pairs(m, epilogue) && alpha == nullptr && w_sf_rep != nullptr) {
     alignas(64) CUtensorMap mb_half;

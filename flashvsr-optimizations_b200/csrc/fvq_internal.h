@@ -68,7 +68,10 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
                         const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
                         int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
-                        const char** why, const uint8_t* w_sf_rep = nullptr);
+                        const char** why, const uint8_t* w_sf_rep = nullptr,
+                        const uint16_t* residual = nullptr, const uint16_t* gate = nullptr);
+// epilogue 2 (replicated W scales only): out = bf16(residual + bf16(gate[n] * y)), y the
+// epilogue-0 result -- the gated residual of a DiT block around its FFN.
 // FVQ_EPI_BF16 GEMMs with replicated W scales, alpha from the global scales and
 // m % 256 == 0 run on SM pairs (nvfp4_gemm_pair_kernel) when enabled.
 void set_gemm_pairing(bool enabled);
@@ -106,6 +109,10 @@ cudaError_t launch_pil_resize(const uint8_t* src, int64_t frames, int in_h, int 
                               cudaStream_t st);
 cudaError_t launch_pil_normalize(const uint8_t* src, int64_t frames, int h, int w, int64_t sb,
                                  int64_t sy, int64_t sx, uint16_t* dst, cudaStream_t st);
+// u = bf16(bf16(LN(x) * bf16(1 + scale)) + shift), one warp per row, d % 8 == 0, d <= 2048
+// (fvq_block.cu).
+cudaError_t launch_ln_modulate(const uint16_t* x, int64_t rows, int64_t d, const uint16_t* shift,
+                               const uint16_t* scale, float eps, uint16_t* u, cudaStream_t st);
 cudaError_t set_error_word(uint32_t v, cudaStream_t st);
 uint32_t* error_word_ptr();   // device address of the error word (current device)
 cudaError_t read_error_word(uint32_t* v, cudaStream_t st);

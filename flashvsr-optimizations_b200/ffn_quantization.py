@@ -125,6 +125,19 @@ class NVFP4FFN(torch.nn.Sequential):
                           l2.qweight, l2.scale, l2.global_sf, l2.bias)
         return y.reshape(*shape[:-1], l2.out_features)
 
+    def modulated(self, x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
+                  gate: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+        """The DiT block's FFN step around this module: x + gate * self(LN(x) * (1 + scale) +
+        shift), LN without affine, each elementwise step in bf16 as torch rounds it; one library
+        call (the LayerNorm and modulation in one kernel, the gated residual in the second
+        GEMM's epilogue).  shift, scale, gate: bf16 vectors of d_model values."""
+        l1, l2 = self[0], self[2]
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        y = ops.nvfp4_ffn_block(x2, shift, scale, gate, eps, l1.qweight, l1.scale, l1.global_sf,
+                                l1.bias, l2.qweight, l2.scale, l2.global_sf, l2.bias)
+        return y.reshape(shape)
+
 
 class FP8FFN(torch.nn.Sequential):
     """``nn.Sequential(QuantLinear('fp8'), GELU(tanh), QuantLinear('fp8'))`` run as one fused call.

@@ -23,7 +23,7 @@ __all__ = [
     "amax", "global_scale", "nvfp4_quantize", "nvfp4_quantize_from_amax", "mm_fp4", "nvfp4_gemm",
     "nvfp4_linear", "nvfp4_ffn", "rcp_approx_probe", "sf_rows", "read_device_error",
     "fp8_row_quant", "fp8_quantize_activation", "fp8_scaled_mm", "fp8_linear", "fp8_ffn",
-    "div_full_probe",
+    "div_full_probe", "ln_modulate", "nvfp4_ffn_block",
 ]
 
 
@@ -289,6 +289,64 @@ def nvfp4_ffn(x: torch.Tensor, q1: torch.Tensor, s1: torch.Tensor, g1: torch.Ten
 @nvfp4_ffn.register_fake
 def _(x, q1, s1, g1, b1, q2, s2, g2, b2):
     return x.new_empty(x.shape, dtype=torch.bfloat16)
+
+
+# ---------------------------------------------------------------- the DiT block around the FFN
+def _vec(name: str, v: torch.Tensor, d: int) -> torch.Tensor:
+    v = v.reshape(-1)
+    if v.numel() != d or v.dtype != torch.bfloat16:
+        raise ValueError(f"{name}: expected a bf16 vector of {d} values")
+    return _aligned16(v)
+
+
+@torch.library.custom_op("fvq::ln_modulate", mutates_args=())
+def ln_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
+                eps: float = 1e-6) -> torch.Tensor:
+    """bf16(bf16(LN(x) * bf16(1 + scale)) + shift): the adaLN-modulated FFN input (LN without affine)."""
+    _check_cuda("ln_modulate", x, shift, scale)
+    _check_bf16("ln_modulate", x)
+    m, d = x.shape
+    x = _aligned16(x)
+    u = torch.empty_like(x)
+    if m:
+        _lib.call("fvq_ln_modulate", _ptr(x), m, d, _ptr(_vec("shift", shift, d)),
+                  _ptr(_vec("scale", scale, d)), float(eps), _ptr(u), _stream(x))
+    return u
+
+
+@ln_modulate.register_fake
+def _(x, shift, scale, eps=1e-6):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("fvq::nvfp4_ffn_block", mutates_args=())
+def nvfp4_ffn_block(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, gate: torch.Tensor,
+                    eps: float, q1: torch.Tensor, s1: torch.Tensor, g1: torch.Tensor,
+                    b1: torch.Tensor | None, q2: torch.Tensor, s2: torch.Tensor, g2: torch.Tensor,
+                    b2: torch.Tensor | None) -> torch.Tensor:
+    """x + gate * FFN(LN(x) * (1 + scale) + shift), bf16 steps, the gated residual fused
+    into the second GEMM (fvq_nvfp4_ffn_block)."""
+    _check_cuda("nvfp4_ffn_block", x, shift, scale, gate, q1, s1, g1, b1, q2, s2, g2, b2)
+    _check_bf16("nvfp4_ffn_block", x)
+    m, d = x.shape
+    f = q1.shape[0]
+    if m == 0:
+        return x.new_empty((0, d))
+    x = _aligned16(x)
+    out = torch.empty_like(x)
+    lib = _lib.load()
+    ws = workspace(x.device, lib.fvq_nvfp4_ffn_block_workspace_bytes(m, d, f))
+    l1 = _linear_struct(q1, s1, g1, b1, d, f)
+    l2 = _linear_struct(q2, s2, g2, b2, f, d)
+    _lib.call("fvq_nvfp4_ffn_block", _ptr(x), m, _ptr(_vec("shift", shift, d)),
+              _ptr(_vec("scale", scale, d)), _ptr(_vec("gate", gate, d)), float(eps),
+              ctypes.byref(l1), ctypes.byref(l2), _ptr(out), _ptr(ws), ws.numel(), _stream(x))
+    return out
+
+
+@nvfp4_ffn_block.register_fake
+def _(x, shift, scale, gate, eps, q1, s1, g1, b1, q2, s2, g2, b2):
+    return torch.empty_like(x)
 
 
 # ---------------------------------------------------------------- FP8 (W8A8) mode

@@ -187,6 +187,29 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
                   uint16_t* y, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The DiT block around the FFN -- the caller of block.ffn that the reference's
+ * installer patches (ffn_quantization.py:77-80); the block itself is upstream
+ * code, not part of the reference.  adaLN-modulated input and gated residual:
+ *   u   = bf16(bf16(LN(x) * bf16(1 + scale)) + shift)
+ *   out = bf16(x + bf16(gate * FFN(u)))
+ * LN without affine: bf16((x - mean) * rsqrtf(var + eps)), mean and biased
+ * variance of the row in fp32; shift, scale, gate: bf16 [d_model]; every
+ * elementwise step one bf16 rounding (torch's semantics on bf16 tensors).
+ * FFN(u) is fvq_nvfp4_ffn's result; the gated residual is applied in the
+ * second GEMM's epilogue.  d_model % 8 == 0 and <= 2048; pointers 16-byte
+ * aligned, the workspace (fvq_nvfp4_ffn_block_workspace_bytes, zeroed once)
+ * 32-byte aligned.
+ */
+size_t fvq_nvfp4_ffn_block_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff);
+/* The block's input step alone: u as above, [rows, d] bf16. */
+int fvq_ln_modulate(const uint16_t* x, int64_t rows, int64_t d, const uint16_t* shift,
+                    const uint16_t* scale, float eps, uint16_t* u, void* stream);
+int fvq_nvfp4_ffn_block(const uint16_t* x, int64_t rows, const uint16_t* shift,
+                        const uint16_t* scale, const uint16_t* gate, float eps,
+                        const fvq_linear* lin1, const fvq_linear* lin2, uint16_t* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Instrumentation with no reference counterpart: fvq_nvfp4_ffn with CUDA
  * events around its four launches (amax+quantize of x, GEMM1 with bias, GELU
  * and amax, quantize of the intermediate, GEMM2 with bias).  Synchronises on

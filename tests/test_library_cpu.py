@@ -89,6 +89,34 @@ def test_linear_and_ffn_check_descriptors():
                None) == _lib.FVQ_EWORKSPACE
 
 
+def test_block_entry_points_check_arguments():
+    buf = ctypes.create_string_buffer(256)
+    b = (ctypes.addressof(buf) + 31) // 32 * 32
+    eps = ctypes.c_float(1e-6)
+    assert _rc("fvq_ln_modulate", b, 4, 1532, b, b, eps, b, None) == _lib.FVQ_EINVAL   # d % 8
+    assert _rc("fvq_ln_modulate", b, 4, 2056, b, b, eps, b, None) == _lib.FVQ_EINVAL   # d > 2048
+    assert _rc("fvq_ln_modulate", b, 0, 1536, b, b, eps, b, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_ln_modulate", b, 4, 1536, b, b, ctypes.c_float(-1.0), b, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_ln_modulate", b, 4, 1536, None, b, eps, b, None) == _lib.FVQ_EINVAL
+    assert _rc("fvq_ln_modulate", b + 8, 4, 1536, b, b, eps, b, None) == _lib.FVQ_EALIGN
+    lib = _lib.load()
+    need = lib.fvq_nvfp4_ffn_block_workspace_bytes(4, 1536, 8960)
+    assert need >= lib.fvq_nvfp4_ffn_workspace_bytes(4, 1536, 8960) + 4 * 1536 * 2
+    assert lib.fvq_nvfp4_ffn_block_workspace_bytes(0, 1536, 8960) == 0
+    l1 = _lib.FvqLinear(b, b, b, None, 1536, 8960)
+    l2 = _lib.FvqLinear(b, b, b, None, 8960, 1536)
+    blk = lambda x=b, rows=4, l2=l2, ws=b, wsb=need, e=eps: _rc(  # noqa: E731
+        "fvq_nvfp4_ffn_block", x, rows, b, b, b, e, ctypes.byref(l1), ctypes.byref(l2), b, ws, wsb,
+        None)
+    assert blk(l2=_lib.FvqLinear(b, b, b, None, 8960, 1024)) == _lib.FVQ_EINVAL
+    assert blk(rows=0) == _lib.FVQ_EINVAL
+    assert blk(x=None) == _lib.FVQ_EINVAL
+    assert blk(e=ctypes.c_float(float("nan"))) == _lib.FVQ_EINVAL
+    assert blk(wsb=need - 1) == _lib.FVQ_EWORKSPACE
+    assert blk(x=b + 8) == _lib.FVQ_EALIGN
+    assert blk(ws=b + 16) == _lib.FVQ_EALIGN
+
+
 def test_valid_call_without_gpu_fails_loudly():
     """A well-formed call on a machine without a usable GPU returns an error, never computes on CPU."""
     import torch
