@@ -120,6 +120,19 @@ __device__ __forceinline__ bool aborted(B* bars) {
   return *reinterpret_cast<volatile int*>(&bars->abort_flag) != 0;
 }
 
+// aborted() as lane 0 of a converged warp sees it, for every lane.
+template <class B>
+__device__ __forceinline__ bool warp_aborted(B* bars) {
+  return __shfl_sync(0xFFFFFFFFu, aborted(bars) ? 1 : 0, 0) != 0;
+}
+
+// flag_error from one lane of a converged warp.
+template <class B>
+__device__ __forceinline__ void warp_flag_error(B* bars, uint32_t bit) {
+  if (elect_one()) flag_error(bars, bit);
+  __syncwarp();
+}
+
 __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
@@ -308,7 +321,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint8_t* staging = smem + P::kStagingOff;
   uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + P::kTableOff);
 
-  const int warp = threadIdx.x >> 5;
+  const int warp = warp_index_uniform();
   const int lane = threadIdx.x & 31;
   const int num_m_blocks = (m + BM - 1) / BM;
   const int num_n_blocks = n / BN;
@@ -343,15 +356,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && seq.count > 0) {
+    // (the whole warp runs the loop; one elected lane issues the copies)
+    if (seq.count > 0) {
       bool sfb_armed = false;
       if (kResident) {
         // the W scales of this CTA's N block, all K: two contiguous 128-row runs
-        mbar_arrive_expect_tx(&bars->sfb_full, static_cast<uint32_t>(2 * sf_tile_stride));
-        bulk_load(staging, w_sf + (2 * seq.nb_fixed) * sf_tile_stride,
-                  static_cast<uint32_t>(sf_tile_stride), &bars->sfb_full);
-        bulk_load(staging + sf_tile_stride, w_sf + (2 * seq.nb_fixed + 1) * sf_tile_stride,
-                  static_cast<uint32_t>(sf_tile_stride), &bars->sfb_full);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&bars->sfb_full, static_cast<uint32_t>(2 * sf_tile_stride));
+          bulk_load(staging, w_sf + (2 * seq.nb_fixed) * sf_tile_stride,
+                    static_cast<uint32_t>(sf_tile_stride), &bars->sfb_full);
+          bulk_load(staging + sf_tile_stride, w_sf + (2 * seq.nb_fixed + 1) * sf_tile_stride,
+                    static_cast<uint32_t>(sf_tile_stride), &bars->sfb_full);
+        }
+        __syncwarp();
         sfb_armed = true;
       }
       uint32_t armed[kStages];
@@ -359,32 +376,35 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (int s = 0; s < kStages; ++s) armed[s] = 0;
       int stage = 0;
       uint32_t phase = 0;
-      for (int i = 0; i < seq.count && !aborted(bars); ++i) {
+      for (int i = 0; i < seq.count && !warp_aborted(bars); ++i) {
         int mb, nb, half;
         seq.at(i, mb, nb, half);  // a half tile loads the whole W tile
         for (int kt = 0; kt < num_k_tiles; ++kt) {
-          if (!mbar_wait_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
-            flag_error(bars, kErrWaitProducer);
+          if (!warp_wait_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
+            warp_flag_error(bars, kErrWaitProducer);
             break;
           }
           uint8_t* sa = smem + stage * kStageBytes;
           uint8_t* sb = sa + kABytes;
           uint8_t* ssfa = sb + kBBytes;
-          mbar_arrive_expect_tx(&bars->full[stage], kStageBytes);
-          tma_load_2d(sa, &tmap_a, &bars->full[stage], kt * BKB, mb * BM);
-          tma_load_2d(sb, &tmap_b, &bars->full[stage], kt * BKB, nb * BN);
-          bulk_load(ssfa, a_sf + mb * sf_tile_stride + kt * 2048, kSfaBytes, &bars->full[stage]);
-          if (kRepSfb) {
-            // replicated layout: K tile kt of N block nb is 16 KB contiguous
-            bulk_load(ssfa + kSfaBytes,
-                      w_sf + (static_cast<int64_t>(nb) * (k / 64) + kt * 4) * (2 * 2048),
-                      kSfbRepBytes, &bars->full[stage]);
-          } else if (!kResident) {
-            uint8_t* ssfb = ssfa + kSfaBytes;
-            bulk_load(ssfb, w_sf + (2 * nb) * sf_tile_stride + kt * 2048, 2048, &bars->full[stage]);
-            bulk_load(ssfb + 2048, w_sf + (2 * nb + 1) * sf_tile_stride + kt * 2048, 2048,
-                      &bars->full[stage]);
+          uint64_t* full = &bars->full[stage];
+          if (elect_one()) {
+            mbar_arrive_expect_tx(full, kStageBytes);
+            tma_load_2d(sa, &tmap_a, full, kt * BKB, mb * BM);
+            tma_load_2d(sb, &tmap_b, full, kt * BKB, nb * BN);
+            bulk_load(ssfa, a_sf + mb * sf_tile_stride + kt * 2048, kSfaBytes, full);
+            if (kRepSfb) {
+              // replicated layout: K tile kt of N block nb is 16 KB contiguous
+              bulk_load(ssfa + kSfaBytes,
+                        w_sf + (static_cast<int64_t>(nb) * (k / 64) + kt * 4) * (2 * 2048),
+                        kSfbRepBytes, full);
+            } else if (!kResident) {
+              uint8_t* ssfb = ssfa + kSfaBytes;
+              bulk_load(ssfb, w_sf + (2 * nb) * sf_tile_stride + kt * 2048, 2048, full);
+              bulk_load(ssfb + 2048, w_sf + (2 * nb + 1) * sf_tile_stride + kt * 2048, 2048, full);
+            }
           }
+          __syncwarp();
           armed[stage] += 1;
           if (++stage == kStages) {
             stage = 0;
@@ -396,38 +416,43 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // these waits keep the default limit even when a short one was requested
       for (int s = 0; s < kStages; ++s) {
         if (armed[s] > 0 &&
-            !mbar_wait_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit)) {
-          flag_error(bars, kErrWaitTeardown);
+            !warp_wait_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit)) {
+          warp_flag_error(bars, kErrWaitTeardown);
         }
       }
-      if (sfb_armed && !mbar_wait_bounded(&bars->sfb_full, 0, teardown_limit))
-        flag_error(bars, kErrWaitTeardown);
+      if (sfb_armed && !warp_wait_bounded(&bars->sfb_full, 0, teardown_limit))
+        warp_flag_error(bars, kErrWaitTeardown);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && seq.count > 0) {
+    // (the whole warp runs the loop; one elected lane issues the tcgen05 work,
+    // always the same lane, so its commits cover its own copies and MMAs)
+    if (seq.count > 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool issued_any = false;
       bool ok = true;
       const uint32_t acc = tmem;
       if (kResident) {
-        if (!mbar_wait_bounded(&bars->sfb_full, 0, wait_limit)) {
-          flag_error(bars, kErrWaitMma);
+        if (!warp_wait_bounded(&bars->sfb_full, 0, wait_limit)) {
+          warp_flag_error(bars, kErrWaitMma);
           ok = false;
         } else {
           tc_fence_after();
-          for (int s = 0; s < k / 64; ++s) {
-            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * s,
-                               make_smem_desc(smem_u32(staging + 512 * s), 16, 128, 0));
-            tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * s + 4,
-                               make_smem_desc(smem_u32(staging + sf_tile_stride + 512 * s), 16, 128,
-                                              0));
+          if (elect_one()) {
+            for (int s = 0; s < k / 64; ++s) {
+              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * s,
+                                 make_smem_desc(smem_u32(staging + 512 * s), 16, 128, 0));
+              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * s + 4,
+                                 make_smem_desc(smem_u32(staging + sf_tile_stride + 512 * s), 16,
+                                                128, 0));
+            }
           }
+          __syncwarp();
           issued_any = true;
         }
       }
-      for (int i = 0; ok && i < seq.count && !aborted(bars); ++i) {
+      for (int i = 0; ok && i < seq.count && !warp_aborted(bars); ++i) {
         int mb_unused, nb_unused, half;
         seq.at(i, mb_unused, nb_unused, half);
         // a half tile: N = 128 MMAs on W rows [128 * half, +128) of the stage and
@@ -435,15 +460,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint32_t idesc = half < 0 ? kIdesc : kIdescHalf;
         const uint32_t b_off = half > 0 ? static_cast<uint32_t>(kBBytes / 2) : 0u;
         const uint32_t sfb_off = half > 0 ? 4u : 0u;
-        if (!mbar_wait_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
+        if (!warp_wait_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
                                wait_limit)) {
-          flag_error(bars, kErrWaitMma);
+          warp_flag_error(bars, kErrWaitMma);
           break;
         }
         tc_fence_after();
         for (int kt = 0; kt < num_k_tiles; ++kt) {
-          if (!mbar_wait_bounded(&bars->full[stage], phase, wait_limit)) {
-            flag_error(bars, kErrWaitMma);
+          if (!warp_wait_bounded(&bars->full[stage], phase, wait_limit)) {
+            warp_flag_error(bars, kErrWaitMma);
             ok = false;
             break;
           }
@@ -451,46 +476,52 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sa = smem + stage * kStageBytes;
           uint8_t* sb = sa + kABytes;
           uint8_t* ssfa = sb + kBBytes;
-          // scales: one 512-byte atom (32 rows x 16 B) per 64-deep K step
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            tmem_cp_32x128b_x4(tmem + kSfaCol + 4 * j,
-                               make_smem_desc(smem_u32(ssfa + 512 * j), 16, 128, 0));
-            if (kRepSfb) {
-              // row i of the 4 KB source: line i % 32 of the rows 0-127 atom
-              // (first 2 KB) and of the rows 128-255 atom (LBO = 2 KB later)
-              tmem_cp_128x256b(tmem + kSfbCol + 8 * j,
-                               make_smem_desc(smem_u32(ssfa + kSfaBytes + 4096 * j), 2048, 128, 0));
-            } else if (!kResident) {
-              uint8_t* ssfb = ssfa + kSfaBytes;
-              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j,
-                                 make_smem_desc(smem_u32(ssfb + 512 * j), 16, 128, 0));
-              tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j + 4,
-                                 make_smem_desc(smem_u32(ssfb + 2048 + 512 * j), 16, 128, 0));
-            }
-          }
           const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
           const uint64_t bdesc = make_smem_desc(smem_u32(sb) + b_off, 16, 1024, 2);
+          if (elect_one()) {
+            // scales: one 512-byte atom (32 rows x 16 B) per 64-deep K step
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t sfb = tmem + kSfbCol + 8 * (kResident ? kt * 4 + j : j) + sfb_off;
-            mma_nvf4(acc, adesc + static_cast<uint64_t>(2 * j), bdesc + static_cast<uint64_t>(2 * j),
-                     idesc, tmem + kSfaCol + 4 * j, sfb, (kt > 0 || j > 0) ? 1u : 0u);
+            for (int j = 0; j < 4; ++j) {
+              tmem_cp_32x128b_x4(tmem + kSfaCol + 4 * j,
+                                 make_smem_desc(smem_u32(ssfa + 512 * j), 16, 128, 0));
+              if (kRepSfb) {
+                // row i of the 4 KB source: line i % 32 of the rows 0-127 atom
+                // (first 2 KB) and of the rows 128-255 atom (LBO = 2 KB later)
+                tmem_cp_128x256b(tmem + kSfbCol + 8 * j,
+                                 make_smem_desc(smem_u32(ssfa + kSfaBytes + 4096 * j), 2048, 128, 0));
+              } else if (!kResident) {
+                uint8_t* ssfb = ssfa + kSfaBytes;
+                tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j,
+                                   make_smem_desc(smem_u32(ssfb + 512 * j), 16, 128, 0));
+                tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * j + 4,
+                                   make_smem_desc(smem_u32(ssfb + 2048 + 512 * j), 16, 128, 0));
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t sfb = tmem + kSfbCol + 8 * (kResident ? kt * 4 + j : j) + sfb_off;
+              mma_nvf4(acc, adesc + static_cast<uint64_t>(2 * j),
+                       bdesc + static_cast<uint64_t>(2 * j), idesc, tmem + kSfaCol + 4 * j, sfb,
+                       (kt > 0 || j > 0) ? 1u : 0u);
+            }
+            tc_commit(&bars->empty[stage]);
           }
+          __syncwarp();
           issued_any = true;
-          tc_commit(&bars->empty[stage]);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(&bars->acc_full);
+        if (elect_one()) tc_commit(&bars->acc_full);
+        __syncwarp();
       }
-      if (aborted(bars) && issued_any) {
-        tc_commit(&bars->teardown);
-        if (!mbar_wait_bounded(&bars->teardown, 0, teardown_limit))
-          flag_error(bars, kErrWaitTeardown);
+      if (warp_aborted(bars) && issued_any) {
+        if (elect_one()) tc_commit(&bars->teardown);
+        __syncwarp();
+        if (!warp_wait_bounded(&bars->teardown, 0, teardown_limit))
+          warp_flag_error(bars, kErrWaitTeardown);
       }
     }
   } else {
@@ -668,7 +699,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     return;  // both CTAs see the same layout, so both return here
   }
   auto* bars = reinterpret_cast<PairBarriers*>(smem + kPairBarrierOff);
-  const int warp = threadIdx.x >> 5;
+  const int warp = warp_index_uniform();
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool even = rank == 0;
@@ -710,19 +741,20 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
-    if (lane == 0 && count > 0) {
+    // (the whole warp runs the loop; one elected lane issues the copies)
+    if (count > 0) {
       uint32_t armed[kPairStages];
 #pragma unroll
       for (int s = 0; s < kPairStages; ++s) armed[s] = 0;
       int stage = 0;
       uint32_t phase = 0;
-      for (int i = 0; i < count && !aborted(bars); ++i) {
+      for (int i = 0; i < count && !warp_aborted(bars); ++i) {
         const int t = pair + i * pairs;
         const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
         const int a_block = 2 * mbp + static_cast<int>(rank);  // this CTA's 128 rows
         for (int kt = 0; kt < num_k_tiles; ++kt) {
-          if (!mbar_wait_cluster_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
-            flag_error(bars, kErrWaitProducer);
+          if (!warp_wait_cluster_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
+            warp_flag_error(bars, kErrWaitProducer);
             break;
           }
           uint8_t* sa = smem + stage * kPairStageBytes;
@@ -730,14 +762,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* ssfa = sb + kPairBBytes;
           uint8_t* ssfb = ssfa + kSfaBytes;
           const uint32_t bar = even_addr(&bars->full[stage]);
-          if (even) mbar_arrive_expect_tx(&bars->full[stage], 2 * kPairStageBytes);
-          tma_load_2d_pair(sa, &tmap_a, bar, kt * BKB, a_block * BM);
-          tma_load_2d_pair(sb, &tmap_b_half, bar, kt * BKB,
-                           nb * BN + static_cast<int>(rank) * (BN / 2));
-          // A scales: atoms 4kt..4kt+3 of 128-row block a_block; W scales: the
-          // 32 replicated atoms of K steps 4kt..4kt+3 of N block nb
-          tma_load_3d_pair(ssfa, &tmap_sfa, bar, 0, kt * 4, a_block);
-          tma_load_3d_pair(ssfb, &tmap_sfb, bar, 0, 0, nb * (k / 64) + kt * 4);
+          if (elect_one()) {
+            if (even) mbar_arrive_expect_tx(&bars->full[stage], 2 * kPairStageBytes);
+            tma_load_2d_pair(sa, &tmap_a, bar, kt * BKB, a_block * BM);
+            tma_load_2d_pair(sb, &tmap_b_half, bar, kt * BKB,
+                             nb * BN + static_cast<int>(rank) * (BN / 2));
+            // A scales: atoms 4kt..4kt+3 of 128-row block a_block; W scales: the
+            // 32 replicated atoms of K steps 4kt..4kt+3 of N block nb
+            tma_load_3d_pair(ssfa, &tmap_sfa, bar, 0, kt * 4, a_block);
+            tma_load_3d_pair(ssfb, &tmap_sfb, bar, 0, 0, nb * (k / 64) + kt * 4);
+          }
+          __syncwarp();
           armed[stage] += 1;
           if (++stage == kPairStages) {
             stage = 0;
@@ -750,27 +785,28 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // barrier waits for
       for (int s = 0; even && s < kPairStages; ++s) {
         if (armed[s] > 0 &&
-            !mbar_wait_cluster_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit))
-          flag_error(bars, kErrWaitTeardown);
+            !warp_wait_cluster_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit))
+          warp_flag_error(bars, kErrWaitTeardown);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && count > 0 && even) {
+    if (count > 0 && even) {
       // ---------------------------------------------------------- MMA issuer (even CTA)
+      // (the whole warp runs the loop; the same elected lane issues everything)
       int stage = 0;
       uint32_t phase = 0;
       bool issued_any = false;
       bool ok = true;
-      for (int i = 0; ok && i < count && !aborted(bars); ++i) {
-        if (!mbar_wait_cluster_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
+      for (int i = 0; ok && i < count && !warp_aborted(bars); ++i) {
+        if (!warp_wait_cluster_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
                                        wait_limit)) {
-          flag_error(bars, kErrWaitMma);
+          warp_flag_error(bars, kErrWaitMma);
           break;
         }
         tc_fence_after();
         for (int kt = 0; kt < num_k_tiles; ++kt) {
-          if (!mbar_wait_cluster_bounded(&bars->full[stage], phase, wait_limit)) {
-            flag_error(bars, kErrWaitMma);
+          if (!warp_wait_cluster_bounded(&bars->full[stage], phase, wait_limit)) {
+            warp_flag_error(bars, kErrWaitMma);
             ok = false;
             break;
           }
@@ -779,37 +815,46 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sb = sa + kABytes;
           uint8_t* ssfa = sb + kPairBBytes;
           uint8_t* ssfb = ssfa + kSfaBytes;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            tmem_cp_32x128b_x4_pair(tmem + kSfaCol + 4 * j,
-                                    make_smem_desc(smem_u32(ssfa + 512 * j), 16, 128, 0));
-            tmem_cp_128x256b_pair(tmem + kSfbCol + 8 * j,
-                                  make_smem_desc(smem_u32(ssfb + 4096 * j), 2048, 128, 0));
-          }
           const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
           const uint64_t bdesc = make_smem_desc(smem_u32(sb), 16, 1024, 2);
+          const uint32_t empty_odd = odd_addr(&bars->empty[stage]);
+          if (elect_one()) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            mma_nvf4_pair(tmem, adesc + static_cast<uint64_t>(2 * j),
-                          bdesc + static_cast<uint64_t>(2 * j), kIdescPair, tmem + kSfaCol + 4 * j,
-                          tmem + kSfbCol + 8 * j, (kt > 0 || j > 0) ? 1u : 0u);
+            for (int j = 0; j < 4; ++j) {
+              tmem_cp_32x128b_x4_pair(tmem + kSfaCol + 4 * j,
+                                      make_smem_desc(smem_u32(ssfa + 512 * j), 16, 128, 0));
+              tmem_cp_128x256b_pair(tmem + kSfbCol + 8 * j,
+                                    make_smem_desc(smem_u32(ssfb + 4096 * j), 2048, 128, 0));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              mma_nvf4_pair(tmem, adesc + static_cast<uint64_t>(2 * j),
+                            bdesc + static_cast<uint64_t>(2 * j), kIdescPair, tmem + kSfaCol + 4 * j,
+                            tmem + kSfbCol + 8 * j, (kt > 0 || j > 0) ? 1u : 0u);
+            }
+            tc_commit_pair(smem_u32(&bars->empty[stage]));
+            tc_commit_pair(empty_odd);
           }
+          __syncwarp();
           issued_any = true;
-          tc_commit_pair(smem_u32(&bars->empty[stage]));
-          tc_commit_pair(odd_addr(&bars->empty[stage]));
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit_pair(smem_u32(&bars->acc_full));
-        tc_commit_pair(odd_addr(&bars->acc_full));
+        const uint32_t acc_odd = odd_addr(&bars->acc_full);
+        if (elect_one()) {
+          tc_commit_pair(smem_u32(&bars->acc_full));
+          tc_commit_pair(acc_odd);
+        }
+        __syncwarp();
       }
-      if (aborted(bars) && issued_any) {
-        tc_commit_pair(smem_u32(&bars->teardown));
-        if (!mbar_wait_bounded(&bars->teardown, 0, teardown_limit))
-          flag_error(bars, kErrWaitTeardown);
+      if (warp_aborted(bars) && issued_any) {
+        if (elect_one()) tc_commit_pair(smem_u32(&bars->teardown));
+        __syncwarp();
+        if (!warp_wait_bounded(&bars->teardown, 0, teardown_limit))
+          warp_flag_error(bars, kErrWaitTeardown);
       }
     }
   } else {
@@ -936,7 +981,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint8_t* staging = smem + P::kStagingOff;
   uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + P::kTableOff);
 
-  const int warp = threadIdx.x >> 5;
+  const int warp = warp_index_uniform();
   const int lane = threadIdx.x & 31;
   const int num_m_blocks = (m + BM - 1) / BM;
   const int num_n_blocks = n / BN;
@@ -969,25 +1014,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && seq.count > 0) {
+    // (the whole warp runs the loop; one elected lane issues the copies)
+    if (seq.count > 0) {
       uint32_t armed[kStages];
 #pragma unroll
       for (int s = 0; s < kStages; ++s) armed[s] = 0;
       int stage = 0;
       uint32_t phase = 0;
-      for (int i = 0; i < seq.count && !aborted(bars); ++i) {
+      for (int i = 0; i < seq.count && !warp_aborted(bars); ++i) {
         int mb, nb, half;
         seq.at(i, mb, nb, half);  // a half tile loads the whole W tile
         for (int kt = 0; kt < num_k_tiles; ++kt) {
-          if (!mbar_wait_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
-            flag_error(bars, kErrWaitProducer);
+          if (!warp_wait_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
+            warp_flag_error(bars, kErrWaitProducer);
             break;
           }
           uint8_t* sa = smem + stage * kStageBytes;
           uint8_t* sb = sa + kABytes;
-          mbar_arrive_expect_tx(&bars->full[stage], kStageBytes);
-          tma_load_2d(sa, &tmap_a, &bars->full[stage], kt * kF8BK, mb * BM);
-          tma_load_2d(sb, &tmap_b, &bars->full[stage], kt * kF8BK, nb * BN);
+          uint64_t* full = &bars->full[stage];
+          if (elect_one()) {
+            mbar_arrive_expect_tx(full, kStageBytes);
+            tma_load_2d(sa, &tmap_a, full, kt * kF8BK, mb * BM);
+            tma_load_2d(sb, &tmap_b, full, kt * kF8BK, nb * BN);
+          }
+          __syncwarp();
           armed[stage] += 1;
           if (++stage == kStages) {
             stage = 0;
@@ -997,32 +1047,33 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       for (int s = 0; s < kStages; ++s) {
         if (armed[s] > 0 &&
-            !mbar_wait_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit)) {
-          flag_error(bars, kErrWaitTeardown);
+            !warp_wait_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit)) {
+          warp_flag_error(bars, kErrWaitTeardown);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && seq.count > 0) {
+    // (the whole warp runs the loop; the same elected lane issues everything)
+    if (seq.count > 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool issued_any = false;
       bool ok = true;
-      for (int i = 0; ok && i < seq.count && !aborted(bars); ++i) {
+      for (int i = 0; ok && i < seq.count && !warp_aborted(bars); ++i) {
         int mb_unused, nb_unused, half;
         seq.at(i, mb_unused, nb_unused, half);
         const uint32_t idesc = half < 0 ? kIdescF8 : kIdescF8Half;
         const uint32_t b_off = half > 0 ? static_cast<uint32_t>(kBBytes / 2) : 0u;
-        if (!mbar_wait_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
+        if (!warp_wait_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
                                wait_limit)) {
-          flag_error(bars, kErrWaitMma);
+          warp_flag_error(bars, kErrWaitMma);
           break;
         }
         tc_fence_after();
         for (int kt = 0; kt < num_k_tiles; ++kt) {
-          if (!mbar_wait_bounded(&bars->full[stage], phase, wait_limit)) {
-            flag_error(bars, kErrWaitMma);
+          if (!warp_wait_bounded(&bars->full[stage], phase, wait_limit)) {
+            warp_flag_error(bars, kErrWaitMma);
             ok = false;
             break;
           }
@@ -1031,25 +1082,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sb = sa + kABytes;
           const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
           const uint64_t bdesc = make_smem_desc(smem_u32(sb) + b_off, 16, 1024, 2);
+          if (elect_one()) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {  // 32-byte K steps inside the 128B swizzle atom
-            mma_f8(tmem, adesc + static_cast<uint64_t>(2 * j), bdesc + static_cast<uint64_t>(2 * j),
-                   idesc, (kt > 0 || j > 0) ? 1u : 0u);
+            for (int j = 0; j < 4; ++j) {  // 32-byte K steps inside the 128B swizzle atom
+              mma_f8(tmem, adesc + static_cast<uint64_t>(2 * j),
+                     bdesc + static_cast<uint64_t>(2 * j), idesc, (kt > 0 || j > 0) ? 1u : 0u);
+            }
+            tc_commit(&bars->empty[stage]);
           }
+          __syncwarp();
           issued_any = true;
-          tc_commit(&bars->empty[stage]);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(&bars->acc_full);
+        if (elect_one()) tc_commit(&bars->acc_full);
+        __syncwarp();
       }
-      if (aborted(bars) && issued_any) {
-        tc_commit(&bars->teardown);
-        if (!mbar_wait_bounded(&bars->teardown, 0, teardown_limit))
-          flag_error(bars, kErrWaitTeardown);
+      if (warp_aborted(bars) && issued_any) {
+        if (elect_one()) tc_commit(&bars->teardown);
+        __syncwarp();
+        if (!warp_wait_bounded(&bars->teardown, 0, teardown_limit))
+          warp_flag_error(bars, kErrWaitTeardown);
       }
     }
   } else {
@@ -1208,7 +1264,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   auto* bars = reinterpret_cast<F8PairBarriers<kStages>*>(smem + P::kBarrierOff);
   uint8_t* staging = smem + P::kStagingOff;
   uint16_t* gelu_tab = reinterpret_cast<uint16_t*>(smem + P::kTableOff);
-  const int warp = threadIdx.x >> 5;
+  const int warp = warp_index_uniform();
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool even = rank == 0;
@@ -1247,30 +1303,34 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
-    if (lane == 0 && count > 0) {
+    // (the whole warp runs the loop; one elected lane issues the copies)
+    if (count > 0) {
       uint32_t armed[kStages];
 #pragma unroll
       for (int s = 0; s < kStages; ++s) armed[s] = 0;
       int stage = 0;
       uint32_t phase = 0;
-      for (int i = 0; i < count && !aborted(bars); ++i) {
+      for (int i = 0; i < count && !warp_aborted(bars); ++i) {
         const int t = pair + i * pairs;
         const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
         // this CTA's 128 rows; a block wholly past the last row loads the last
         // block instead (its rows are never stored), so every box starts inside A
         const int a_row = min((2 * mbp + static_cast<int>(rank)) * BM, ((m - 1) / BM) * BM);
         for (int kt = 0; kt < num_k_tiles; ++kt) {
-          if (!mbar_wait_cluster_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
-            flag_error(bars, kErrWaitProducer);
+          if (!warp_wait_cluster_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
+            warp_flag_error(bars, kErrWaitProducer);
             break;
           }
           uint8_t* sa = smem + stage * kF8PairStageBytes;
           uint8_t* sb = sa + kABytes;
           const uint32_t bar = even_addr(&bars->full[stage]);
-          if (even) mbar_arrive_expect_tx(&bars->full[stage], 2 * kF8PairStageBytes);
-          tma_load_2d_pair(sa, &tmap_a, bar, kt * kF8BK, a_row);
-          tma_load_2d_pair(sb, &tmap_b_half, bar, kt * kF8BK,
-                           nb * BN + static_cast<int>(rank) * (BN / 2));
+          if (elect_one()) {
+            if (even) mbar_arrive_expect_tx(&bars->full[stage], 2 * kF8PairStageBytes);
+            tma_load_2d_pair(sa, &tmap_a, bar, kt * kF8BK, a_row);
+            tma_load_2d_pair(sb, &tmap_b_half, bar, kt * kF8BK,
+                             nb * BN + static_cast<int>(rank) * (BN / 2));
+          }
+          __syncwarp();
           armed[stage] += 1;
           if (++stage == kStages) {
             stage = 0;
@@ -1283,27 +1343,28 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // barrier waits for
       for (int s = 0; even && s < kStages; ++s) {
         if (armed[s] > 0 &&
-            !mbar_wait_cluster_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit))
-          flag_error(bars, kErrWaitTeardown);
+            !warp_wait_cluster_bounded(&bars->full[s], (armed[s] - 1) & 1u, teardown_limit))
+          warp_flag_error(bars, kErrWaitTeardown);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && count > 0 && even) {
+    if (count > 0 && even) {
       // ---------------------------------------------------------- MMA issuer (even CTA)
+      // (the whole warp runs the loop; the same elected lane issues everything)
       int stage = 0;
       uint32_t phase = 0;
       bool issued_any = false;
       bool ok = true;
-      for (int i = 0; ok && i < count && !aborted(bars); ++i) {
-        if (!mbar_wait_cluster_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
+      for (int i = 0; ok && i < count && !warp_aborted(bars); ++i) {
+        if (!warp_wait_cluster_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
                                        wait_limit)) {
-          flag_error(bars, kErrWaitMma);
+          warp_flag_error(bars, kErrWaitMma);
           break;
         }
         tc_fence_after();
         for (int kt = 0; kt < num_k_tiles; ++kt) {
-          if (!mbar_wait_cluster_bounded(&bars->full[stage], phase, wait_limit)) {
-            flag_error(bars, kErrWaitMma);
+          if (!warp_wait_cluster_bounded(&bars->full[stage], phase, wait_limit)) {
+            warp_flag_error(bars, kErrWaitMma);
             ok = false;
             break;
           }
@@ -1312,28 +1373,37 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* sb = sa + kABytes;
           const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, 2);
           const uint64_t bdesc = make_smem_desc(smem_u32(sb), 16, 1024, 2);
+          const uint32_t empty_odd = odd_addr(&bars->empty[stage]);
+          if (elect_one()) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            mma_f8_pair(tmem, adesc + static_cast<uint64_t>(2 * j),
-                        bdesc + static_cast<uint64_t>(2 * j), kIdescF8Pair,
-                        (kt > 0 || j > 0) ? 1u : 0u);
+            for (int j = 0; j < 4; ++j) {
+              mma_f8_pair(tmem, adesc + static_cast<uint64_t>(2 * j),
+                          bdesc + static_cast<uint64_t>(2 * j), kIdescF8Pair,
+                          (kt > 0 || j > 0) ? 1u : 0u);
+            }
+            tc_commit_pair(smem_u32(&bars->empty[stage]));
+            tc_commit_pair(empty_odd);
           }
+          __syncwarp();
           issued_any = true;
-          tc_commit_pair(smem_u32(&bars->empty[stage]));
-          tc_commit_pair(odd_addr(&bars->empty[stage]));
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit_pair(smem_u32(&bars->acc_full));
-        tc_commit_pair(odd_addr(&bars->acc_full));
+        const uint32_t acc_odd = odd_addr(&bars->acc_full);
+        if (elect_one()) {
+          tc_commit_pair(smem_u32(&bars->acc_full));
+          tc_commit_pair(acc_odd);
+        }
+        __syncwarp();
       }
-      if (aborted(bars) && issued_any) {
-        tc_commit_pair(smem_u32(&bars->teardown));
-        if (!mbar_wait_bounded(&bars->teardown, 0, teardown_limit))
-          flag_error(bars, kErrWaitTeardown);
+      if (warp_aborted(bars) && issued_any) {
+        if (elect_one()) tc_commit_pair(smem_u32(&bars->teardown));
+        __syncwarp();
+        if (!warp_wait_bounded(&bars->teardown, 0, teardown_limit))
+          warp_flag_error(bars, kErrWaitTeardown);
       }
     }
   } else {

@@ -55,16 +55,85 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// try_wait suspends the thread until the phase completes or for at most
+// `hint_ns` (the hardware may return earlier); a completed phase wakes it at once.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity,
+                                                   uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Suspend hint for a wait bounded by `limit_ns`: never longer than the limit,
+// so a short limit is honoured however fast the awaited work is.
+__device__ __forceinline__ uint32_t wait_hint_ns(uint64_t limit_ns) {
+  return limit_ns < (1u << 20) ? static_cast<uint32_t>(limit_ns) : (1u << 20);
+}
+
+// Non-blocking: has the phase with `parity` completed?
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Limits shorter than this are below what %globaltimer resolves (and try_wait
+// may sleep longer than its hint): such a wait is one non-blocking test.
+constexpr uint64_t kTimerResolutionNs = 1000;
+
 // Wait until the phase with `parity` completes, for at most `limit_ns`
-// nanoseconds of wall time.  Returns false on timeout.
+// nanoseconds of wall time (plus at most one suspend hint).  Returns false on
+// timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (limit_ns < kTimerResolutionNs) return mbar_test_wait(bar, parity);
+  const uint32_t hint = wait_hint_ns(limit_ns);
+  if (mbar_try_wait_hint(bar, parity, hint)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_hint(bar, parity, hint)) return true;
     if (global_timer_ns() - start > limit_ns) return false;
   }
+}
+
+// ---------------------------------------------------------------- warp-uniform issue
+// tcgen05 and TMA instructions take their operands from the warp's uniform
+// registers.  Issuing them from one lane of a diverged branch moves every
+// operand there instruction by instruction (measured: ~300 cycles per 4-MMA K
+// step); the issuing warps therefore run their loops converged, wait in every
+// lane, and let one elected lane issue.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(p));
+  return p != 0;
+}
+
+// Warp index the compiler can see is uniform across the warp.
+__device__ __forceinline__ int warp_index_uniform() {
+  return __shfl_sync(0xFFFFFFFFu, static_cast<int>(threadIdx.x >> 5), 0);
+}
+
+// mbar_wait_bounded by every lane of a converged warp; lane 0's outcome for all.
+__device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit_ns) {
+  const bool ok = mbar_wait_bounded(bar, parity, limit_ns);
+  return __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
 }
 
 // ---------------------------------------------------------------- TMA / bulk copy
@@ -125,15 +194,47 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return done != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cluster_hint(uint64_t* bar, uint32_t parity,
+                                                           uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait on a local mbarrier that other CTAs of the cluster arrive on.
 __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity,
                                                           uint64_t limit_ns) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
+  if (limit_ns < kTimerResolutionNs) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+  }
+  const uint32_t hint = wait_hint_ns(limit_ns);
+  if (mbar_try_wait_cluster_hint(bar, parity, hint)) return true;
   const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait_cluster(bar, parity)) {
+  while (!mbar_try_wait_cluster_hint(bar, parity, hint)) {
     if (global_timer_ns() - t0 > limit_ns) return false;
   }
   return true;
+}
+
+// mbar_wait_cluster_bounded by every lane of a converged warp; lane 0's outcome for all.
+__device__ __forceinline__ bool warp_wait_cluster_bounded(uint64_t* bar, uint32_t parity,
+                                                          uint64_t limit_ns) {
+  const bool ok = mbar_wait_cluster_bounded(bar, parity, limit_ns);
+  return __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
 }
 
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
