@@ -813,8 +813,10 @@ int fvq_gelu_bf16_probe(const uint16_t* in, uint16_t* out, int64_t count, void* 
   return FVQ_OK;
 }
 
-int fvq_set_gemm_pairing(int enabled) {
-  fvq::set_gemm_pairing(enabled != 0);
+int fvq_set_gemm_pairing(int mode) {
+  if (mode < 0 || mode > 2)
+    return fail(FVQ_EINVAL, "fvq_set_gemm_pairing: mode must be 0, 1 or 2 (got %d)", mode);
+  fvq::set_gemm_pairing(mode);
   return FVQ_OK;
 }
 

@@ -651,31 +651,42 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 }
 
 // ---------------------------------------------------------------- SM-pair GEMM
-// nvfp4_gemm_pair_kernel: the FVQ_EPI_BF16 GEMM with replicated W scales on
-// clusters of two CTAs (the two SMs of a pair) and tcgen05.mma.cta_group::2: a
-// 256 x 256 output tile per pair.  Each CTA loads its 128 rows of A, 128 of the
-// tile's 256 W rows, its A scales and the replicated W scales of all 256 rows;
-// the even CTA issues the scale copies and MMAs for both (one copy instruction
-// fills both SMs' TMEM, so per SM a K tile costs half the copy instructions).  The odd CTA's warp 1 relays "my stage
-// landed" to the even CTA; the even CTA commits "stage free" and "accumulator
-// full" to both CTAs' barriers; both epilogues report a drained accumulator
-// to the even CTA.  All loads of both CTAs (codes, and the scales through 3-D
-// tensor maps over their 512-byte atoms) count their bytes on the even CTA's
-// stage barrier, which only the even CTA arms, so the MMA issuer needs no
-// message from the odd CTA.  Rows per pair tile: 256, so the host uses it for
-// m % 256 == 0.
-constexpr int kPairStages = 4;
+// nvfp4_gemm_pair_kernel: the FVQ_EPI_BF16 GEMM on clusters of two CTAs (the
+// two SMs of a pair) and tcgen05.mma.cta_group::2: a 256 x 256 output tile per
+// pair.  Each CTA loads its 128 rows of A, 128 of the tile's 256 W rows, its A
+// scales and the W scales of all 256 rows (kRawSfb: the library layout, 4 KB
+// per K tile, moved to TMEM with two 32x128b.warpx4 copies per K step;
+// otherwise replicated four times, 16 KB, one 128x256b copy per K step).  The
+// even CTA issues the scale copies and MMAs for both (one copy instruction
+// fills both SMs' TMEM) and commits "stage free" and "accumulator full" to both
+// CTAs' barriers; both epilogues report a drained accumulator to the even
+// CTA.  All loads of both CTAs (codes, and the scales through 3-D tensor maps
+// over their 512-byte atoms) count their bytes on the even CTA's stage
+// barrier, which only the even CTA arms, so the MMA issuer needs no message
+// from the odd CTA.  Rows per pair tile: 256, so the host uses it for
+// m % 256 == 0.  The L2-to-SM traffic per K tile and CTA (38 KB with raw
+// scales, 50 KB replicated) is what bounds this kernel.
 constexpr int kPairBBytes = kBBytes / 2;  // 128 W rows per CTA
-constexpr int kPairStageBytes = kABytes + kPairBBytes + kSfaBytes + kSfbRepBytes;  // 50 KB
-constexpr int kPairBarrierOff = kPairStages * kPairStageBytes;
-constexpr int kPairSmemBytes = kPairBarrierOff + kBarrierBytes;
-static_assert(kPairSmemBytes <= 232448, "pair plan exceeds shared memory");
+constexpr int kPairMaxStages = 6;
+
+template <bool kRawSfb>
+struct PairPlan {
+  static constexpr int kStageBytes =
+      kABytes + kPairBBytes + kSfaBytes + (kRawSfb ? kSfbBytes : kSfbRepBytes);  // 38 / 50 KB
+  static constexpr int kStages = kRawSfb ? 5 : 4;
+  static constexpr int kBarrierOff = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kBarrierOff + kBarrierBytes;
+};
+static_assert(PairPlan<true>::kSmemBytes <= 232448, "pair plan exceeds shared memory");
+static_assert(PairPlan<false>::kSmemBytes <= 232448, "pair plan exceeds shared memory");
+static_assert(PairPlan<true>::kStages <= kPairMaxStages && PairPlan<false>::kStages <= kPairMaxStages,
+              "pair barrier arrays");
 constexpr uint32_t kIdescPair = (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
                                 (static_cast<uint32_t>(2 * BM >> 4) << 24);
 
 struct PairBarriers {
-  uint64_t full[kPairStages];       // even CTA: both CTAs' stage landed
-  uint64_t empty[kPairStages];      // the pair's MMAs on the stage completed
+  uint64_t full[kPairMaxStages];    // even CTA: both CTAs' stage landed
+  uint64_t empty[kPairMaxStages];   // the pair's MMAs on the stage completed
   uint64_t acc_full;                // the pair's accumulator is complete
   uint64_t acc_empty;               // even CTA: both epilogues drained their TMEM
   uint64_t teardown;
@@ -684,6 +695,7 @@ struct PairBarriers {
 };
 static_assert(sizeof(PairBarriers) <= kBarrierBytes, "pair barrier area");
 
+template <bool kRawSfb>
 __global__ void __launch_bounds__(kNumThreads, 1)
     nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                            const __grid_constant__ CUtensorMap tmap_b_half,
@@ -698,7 +710,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (threadIdx.x == 0) atomicOr(&g_device_error, kErrSmemAlign);
     return;  // both CTAs see the same layout, so both return here
   }
-  auto* bars = reinterpret_cast<PairBarriers*>(smem + kPairBarrierOff);
+  using P = PairPlan<kRawSfb>;
+  constexpr int kPairStages = P::kStages;
+  constexpr int kPairStageBytes = P::kStageBytes;
+  auto* bars = reinterpret_cast<PairBarriers*>(smem + P::kBarrierOff);
   const int warp = warp_index_uniform();
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -768,9 +783,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             tma_load_2d_pair(sb, &tmap_b_half, bar, kt * BKB,
                              nb * BN + static_cast<int>(rank) * (BN / 2));
             // A scales: atoms 4kt..4kt+3 of 128-row block a_block; W scales: the
-            // 32 replicated atoms of K steps 4kt..4kt+3 of N block nb
+            // same atoms of 128-row blocks 2nb and 2nb+1 (raw), or the 32
+            // replicated atoms of K steps 4kt..4kt+3 of N block nb
             tma_load_3d_pair(ssfa, &tmap_sfa, bar, 0, kt * 4, a_block);
-            tma_load_3d_pair(ssfb, &tmap_sfb, bar, 0, 0, nb * (k / 64) + kt * 4);
+            if (kRawSfb)
+              tma_load_3d_pair(ssfb, &tmap_sfb, bar, 0, kt * 4, 2 * nb);
+            else
+              tma_load_3d_pair(ssfb, &tmap_sfb, bar, 0, 0, nb * (k / 64) + kt * 4);
           }
           __syncwarp();
           armed[stage] += 1;
@@ -823,8 +842,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             for (int j = 0; j < 4; ++j) {
               tmem_cp_32x128b_x4_pair(tmem + kSfaCol + 4 * j,
                                       make_smem_desc(smem_u32(ssfa + 512 * j), 16, 128, 0));
-              tmem_cp_128x256b_pair(tmem + kSfbCol + 8 * j,
-                                    make_smem_desc(smem_u32(ssfb + 4096 * j), 2048, 128, 0));
+              if (kRawSfb) {
+                tmem_cp_32x128b_x4_pair(tmem + kSfbCol + 8 * j,
+                                        make_smem_desc(smem_u32(ssfb + 512 * j), 16, 128, 0));
+                tmem_cp_32x128b_x4_pair(tmem + kSfbCol + 8 * j + 4,
+                                        make_smem_desc(smem_u32(ssfb + 2048 + 512 * j), 16, 128, 0));
+              } else {
+                tmem_cp_128x256b_pair(tmem + kSfbCol + 8 * j,
+                                      make_smem_desc(smem_u32(ssfb + 4096 * j), 2048, 128, 0));
+              }
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -1596,8 +1622,13 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CU
 // 3-D maps over 512-byte scale atoms (128 x u32): A scales [blocks][k/64 atoms][128],
 // box 4 atoms (one K tile); replicated W scales [n/256 * k/64][8 atoms][128], box
 // 4 x 8 atoms (one K tile of one N block).
+// 3-D maps over the 512-byte scale atoms (u32 elements): A scales as
+// [row block][K step][atom], box = 4 K steps of one block; W scales raw the
+// same way with a box of two blocks (the 256 rows of an N block), or, when
+// `w_rep` is set, the replicated layout [N block * K step][8][atom] with a box
+// of 4 K steps.
 bool make_scale_maps(CUtensorMap* sfa, CUtensorMap* sfb, const uint8_t* a_sf, int64_t a_blocks,
-                     const uint8_t* w_sf_rep, int64_t n, int64_t k) {
+                     const uint8_t* w_sf, bool w_rep, int64_t n, int64_t k) {
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return false;
   const cuuint64_t k64 = static_cast<cuuint64_t>(k / 64);
@@ -1609,15 +1640,25 @@ bool make_scale_maps(CUtensorMap* sfa, CUtensorMap* sfb, const uint8_t* a_sf, in
                    strides_a, box_a, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
+  if (!w_rep) {
+    cuuint64_t dims_b[3] = {128, k64, static_cast<cuuint64_t>(n / 128)};
+    cuuint64_t strides_b[2] = {512, k64 * 512};
+    cuuint32_t box_b[3] = {128, 4, 2};
+    r = enc(sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(w_sf), dims_b, strides_b,
+            box_b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+  }
   cuuint64_t dims_b[3] = {128, 8, static_cast<cuuint64_t>(n / BN) * k64};
   cuuint64_t strides_b[2] = {512, 4096};
   cuuint32_t box_b[3] = {128, 8, 4};
-  r = enc(sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(w_sf_rep), dims_b, strides_b,
+  r = enc(sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(w_sf), dims_b, strides_b,
           box_b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
+template <bool kRawSfb>
 cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
                              const CUtensorMap& msfa, const CUtensorMap& msfb, const float* g_a,
                              const float* g_w,
@@ -1627,8 +1668,9 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_pair_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_pair_kernel<kRawSfb>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         PairPlan<kRawSfb>::kSmemBytes);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
@@ -1638,7 +1680,7 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
   cfg.blockDim = dim3(kNumThreads);
-  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.dynamicSmemBytes = PairPlan<kRawSfb>::kSmemBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1647,8 +1689,8 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, nvfp4_gemm_pair_kernel, ma, mb_half, msfa, msfb, g_a, g_w, bias,
-                            out, m, n, k, wait_limit);
+  return cudaLaunchKernelEx(&cfg, nvfp4_gemm_pair_kernel<kRawSfb>, ma, mb_half, msfa, msfb, g_a,
+                            g_w, bias, out, m, n, k, wait_limit);
 }
 
 template <int kEpi>
@@ -1754,9 +1796,9 @@ cudaError_t launch_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w,
 // GEMMs with replicated W scales and m % 256 == 0 run on SM pairs when enabled
 // (off by default: measured at the one-SM kernel's speed, both clock-limited by
 // the power cap under sustained tensor load).
-static bool g_pairing = false;
-void set_gemm_pairing(bool enabled) { g_pairing = enabled; }
-bool gemm_pairs(int64_t m, int epilogue) { return g_pairing && epilogue == 0 && m % (2 * BM) == 0; }
+static int g_pairing = 1;  // SM pairs with W scales in the library layout
+void set_gemm_pairing(int mode) { g_pairing = mode; }
+bool gemm_pairs(int64_t m, int epilogue) { return g_pairing != 0 && epilogue == 0 && m % (2 * BM) == 0; }
 
 cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
@@ -1794,16 +1836,25 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
     return launch_gemm_t<2, false, true>(ma, mb, mo, a_sf, w_sf_rep, g_a, g_w, alpha, bias, out, mi,
                                          ni, ki, amax_out, wait_limit, st, residual, gate);
   }
-  if (gemm_pairs(m, epilogue) && alpha == nullptr && w_sf_rep != nullptr) {
+  // SM pairs: mode 1 reads the W scales in the library layout, mode 2 the
+  // replicated copy; each falls back to the other form when the caller has
+  // only that one
+  const bool have_raw = w_sf != nullptr, have_rep = w_sf_rep != nullptr;
+  const bool pair_rep = have_rep && (g_pairing == 2 || !have_raw);
+  if (gemm_pairs(m, epilogue) && alpha == nullptr && (have_raw || have_rep)) {
     alignas(64) CUtensorMap mb_half;
     alignas(64) CUtensorMap msfa;
     alignas(64) CUtensorMap msfb;
     if (!make_code_map(&mb_half, w_codes, n, k, BN / 2) ||
-        !make_scale_maps(&msfa, &msfb, a_sf, m / BM, w_sf_rep, n, k)) {
+        !make_scale_maps(&msfa, &msfb, a_sf, m / BM, pair_rep ? w_sf_rep : w_sf, pair_rep, n, k)) {
       if (why) *why = "cuTensorMapEncodeTiled failed for the SM-pair GEMM";
       return cudaErrorInvalidValue;
     }
-    return launch_gemm_pair(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki, wait_limit, st);
+    if (pair_rep)
+      return launch_gemm_pair<false>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
+                                     wait_limit, st);
+    return launch_gemm_pair<true>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
+                                  wait_limit, st);
   }
   if (w_sf_rep != nullptr)
     return launch_gemm_t<0, false, true>(ma, mb, mo, a_sf, w_sf_rep, g_a, g_w, alpha, bias, out, mi,

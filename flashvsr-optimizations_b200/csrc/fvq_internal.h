@@ -74,7 +74,7 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
 // epilogue-0 result -- the gated residual of a DiT block around its FFN.
 // FVQ_EPI_BF16 GEMMs with replicated W scales, alpha from the global scales and
 // m % 256 == 0 run on SM pairs (nvfp4_gemm_pair_kernel) when enabled.
-void set_gemm_pairing(bool enabled);
+void set_gemm_pairing(int mode);  // 0 off, 1 pairs (raw W scales), 2 pairs (replicated)
 bool gemm_pairs(int64_t m, int epilogue);
 cudaError_t launch_gelu_probe(const uint16_t* in, uint16_t* out, int64_t count, cudaStream_t st);
 // E4M3 GEMM with per-row A scales and per-column W scales (fvq_gemm.cu); epilogue 1:

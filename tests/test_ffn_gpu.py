@@ -198,18 +198,20 @@ def test_ffn_profile_entry_point_same_output_and_times(ffn_layer):
     assert all(t > 0 for t in ms), list(ms)
 
 
-def test_ffn_same_bits_with_and_without_sm_pairs(ffn_layer):
-    """With fvq_set_gemm_pairing(1), GEMM2 of the FFN runs on SM pairs at 7680
-    tokens; the output bits equal the default one-SM kernel's."""
+@pytest.mark.parametrize("mode", [1, 2])
+def test_ffn_same_bits_with_and_without_sm_pairs(ffn_layer, mode):
+    """With fvq_set_gemm_pairing(1 or 2), GEMM2 of the FFN runs on SM pairs at 7680
+    tokens (raw or replicated W scales); the output bits equal the one-SM kernel's."""
     from flashvsr_optimizations_b200 import _lib
     ffn, _ = ffn_layer
     x = bits_to_dev(W.student_t(W.M_ONE_LAYER, W.D_MODEL, seed=9))
-    single = ffn(x)
     try:
-        _lib.call("fvq_set_gemm_pairing", 1)
+        _lib.call("fvq_set_gemm_pairing", 0)
+        single = ffn(x)
+        _lib.call("fvq_set_gemm_pairing", mode)
         paired = ffn(x)
     finally:
-        _lib.call("fvq_set_gemm_pairing", 0)
+        _lib.call("fvq_set_gemm_pairing", 1)   # the library default
     torch.cuda.synchronize()
     assert torch.equal(paired, single)
 

@@ -198,11 +198,12 @@ def test_replicated_w_scales_layout(n, k):
 @pytest.mark.parametrize("m,n,k", [(1, 256, 256), (200, 512, 512), (300, 256, 1536),
                                    (513, 768, 768), (256, 256, 256), (512, 768, 512),
                                    (768, 256, 1536), (2560, 2048, 512), (7680, 1536, 8960)])
-@pytest.mark.parametrize("pairing", [0, 1])
+@pytest.mark.parametrize("pairing", [0, 1, 2])
 def test_gemm_with_replicated_w_scales_is_bit_identical(m, n, k, pairing):
     """fvq_nvfp4_gemm_wrep (four 128x256b W-scale copies per K tile; on SM pairs
-    when pairing is on and m % 256 == 0) gives the same bits as fvq_nvfp4_gemm
-    (one SM per tile, eight 32x128b.warpx4 copies), bias included."""
+    when pairing is on and m % 256 == 0) and, with pairing on, fvq_nvfp4_gemm on
+    SM pairs with the W scales in the library layout, give the same bits as
+    fvq_nvfp4_gemm on one SM per tile (eight 32x128b.warpx4 copies), bias included."""
     from flashvsr_optimizations_b200 import _lib
     lib = _lib.load()
     rng = np.random.default_rng(m + 3 * n + k)
@@ -216,15 +217,21 @@ def test_gemm_with_replicated_w_scales_is_bit_identical(m, n, k, pairing):
     ref = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
     got = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
     rep = torch.empty(lib.fvq_w_scales_replicated_bytes(n, k), dtype=torch.uint8, device="cuda")
-    _lib.call("fvq_nvfp4_gemm", ta.data_ptr(), tas.data_ptr(), ga.data_ptr(), tw.data_ptr(),
-              tws.data_ptr(), gw.data_ptr(), bias.data_ptr(), ref.data_ptr(), m, n, k,
-              _lib.EPI_BF16, None, st)
-    _lib.call("fvq_replicate_w_scales", tws.data_ptr(), n, k, rep.data_ptr(), st)
+    raw = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
     try:
+        _lib.call("fvq_set_gemm_pairing", 0)
+        _lib.call("fvq_nvfp4_gemm", ta.data_ptr(), tas.data_ptr(), ga.data_ptr(), tw.data_ptr(),
+                  tws.data_ptr(), gw.data_ptr(), bias.data_ptr(), ref.data_ptr(), m, n, k,
+                  _lib.EPI_BF16, None, st)
+        _lib.call("fvq_replicate_w_scales", tws.data_ptr(), n, k, rep.data_ptr(), st)
         _lib.call("fvq_set_gemm_pairing", pairing)
         _lib.call("fvq_nvfp4_gemm_wrep", ta.data_ptr(), tas.data_ptr(), ga.data_ptr(), tw.data_ptr(),
                   rep.data_ptr(), gw.data_ptr(), bias.data_ptr(), got.data_ptr(), m, n, k, st)
+        _lib.call("fvq_nvfp4_gemm", ta.data_ptr(), tas.data_ptr(), ga.data_ptr(), tw.data_ptr(),
+                  tws.data_ptr(), gw.data_ptr(), bias.data_ptr(), raw.data_ptr(), m, n, k,
+                  _lib.EPI_BF16, None, st)
     finally:
-        _lib.call("fvq_set_gemm_pairing", 0)
+        _lib.call("fvq_set_gemm_pairing", 1)   # the library default
     torch.cuda.synchronize()
     assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    assert torch.equal(raw.view(torch.int16), ref.view(torch.int16))

@@ -117,6 +117,13 @@ def test_block_entry_points_check_arguments():
     assert blk(ws=b + 16) == _lib.FVQ_EALIGN
 
 
+def test_pairing_modes_checked():
+    assert _rc("fvq_set_gemm_pairing", 3) == _lib.FVQ_EINVAL
+    assert _rc("fvq_set_gemm_pairing", -1) == _lib.FVQ_EINVAL
+    assert _rc("fvq_set_gemm_pairing", 0) == _lib.FVQ_OK
+    assert _rc("fvq_set_gemm_pairing", 1) == _lib.FVQ_OK   # back to the default
+
+
 def test_valid_call_without_gpu_fails_loudly():
     """A well-formed call on a machine without a usable GPU returns an error, never computes on CPU."""
     import torch
