@@ -203,21 +203,33 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
   return r;
 }
 
-// GELU of both halves of a bf16x2 word.  Both magnitude offsets are formed in
-// one 32-bit subtraction and clamped to the last entry in one min.u16x2, so
-// the two lookups stay inside the table whatever the input; when either half
-// was clamped (outside [2^-12, 8), or a borrow from the low half) the pair is
-// recomputed on the slow path.  tab_base is the table's shared-memory address.
-__device__ __forceinline__ uint32_t gelu_bf16x2(uint32_t hv, uint32_t tab_base,
-                                                const uint16_t* tab) {
-  const uint32_t d = (hv & 0x7FFF7FFFu) - ((kGeluTabLo << 16) | kGeluTabLo);
-  const uint32_t c = min_u16x2(d, ((kGeluTabSpan - 1) << 16) | (kGeluTabSpan - 1));
-  // byte offsets of both entries: 2 * ((sign << 11) | offset) per half
-  const uint32_t off2 = (c << 1) | ((hv >> 3) & 0x10001000u);
-  const uint32_t r_lo = lds_u16(tab_base + (off2 & 0xFFFFu));
-  const uint32_t r_hi = lds_u16(tab_base + (off2 >> 16));
-  if (c != d) return gelu_bf16x2_slow(hv, tab);
-  return __byte_perm(r_lo, r_hi, 0x5410);
+// GELU of four bf16x2 words.  Per word both magnitude offsets are formed in one
+// 32-bit subtraction and clamped to the last entry in one min.u16x2, so the two
+// lookups stay inside the table whatever the input; the sign is bit 11 of the
+// index.  There is no branch between the eight lookups, so all can be in flight
+// at once; a word with a half that was clamped (outside [2^-12, 8), or a borrow
+// from the low half) is redone on the exact path afterwards.  tab_base is the
+// table's shared-memory address.
+__device__ __forceinline__ void gelu_bf16x2_x4(uint32_t (&w)[4], uint32_t tab_base,
+                                               const uint16_t* tab) {
+  uint32_t res[4];
+  uint32_t slow = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t d = (w[j] & 0x7FFF7FFFu) - ((kGeluTabLo << 16) | kGeluTabLo);
+    const uint32_t c = min_u16x2(d, ((kGeluTabSpan - 1) << 16) | (kGeluTabSpan - 1));
+    const uint32_t off2 = (c << 1) | ((w[j] >> 3) & 0x10001000u);
+    res[j] = __byte_perm(lds_u16(tab_base + (off2 & 0xFFFFu)), lds_u16(tab_base + (off2 >> 16)),
+                         0x5410);
+    slow |= static_cast<uint32_t>(c != d) << j;
+  }
+  if (slow != 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if ((slow >> j) & 1u) res[j] = gelu_bf16x2_slow(w[j], tab);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) w[j] = res[j];
 }
 
 // alpha * (lo, hi) with one mul.rn.f32x2 (two IEEE products), rounded to a bf16x2 pair.
@@ -589,12 +601,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint32_t o[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            uint32_t hv = y[4 * q + j];
-            if (bias != nullptr) hv = add_bf16x2(hv, bw[j]);
-            hv = gelu_bf16x2(hv, tab_base, gelu_tab);
-            tile_max = max_u16x2(tile_max, hv & 0x7FFF7FFFu);
-            o[j] = hv;
+            o[j] = y[4 * q + j];
+            if (bias != nullptr) o[j] = add_bf16x2(o[j], bw[j]);
           }
+          gelu_bf16x2_x4(o, tab_base, gelu_tab);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tile_max = max_u16x2(tile_max, o[j] & 0x7FFF7FFFu);
           *reinterpret_cast<uint4*>(warp_staging + lane * kStageRowBytes + ((q ^ (lane & 7)) * 16)) =
               make_uint4(o[0], o[1], o[2], o[3]);
         }
@@ -1190,14 +1202,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint32_t o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          uint32_t hv = rowcol_scale_pack_bf16x2(r[8 * q + 2 * j], r[8 * q + 2 * j + 1], sa2,
-                                                 sw[2 * j], sw[2 * j + 1]);
-          if (bias != nullptr) hv = add_bf16x2(hv, bw[j]);
-          if constexpr (kEpi == 1) {
-            hv = gelu_bf16x2(hv, tab_base, gelu_tab);
-            tile_max = max_u16x2(tile_max, hv & 0x7FFF7FFFu);
-          }
-          o[j] = hv;
+          o[j] = rowcol_scale_pack_bf16x2(r[8 * q + 2 * j], r[8 * q + 2 * j + 1], sa2, sw[2 * j],
+                                          sw[2 * j + 1]);
+          if (bias != nullptr) o[j] = add_bf16x2(o[j], bw[j]);
+        }
+        if constexpr (kEpi == 1) {
+          gelu_bf16x2_x4(o, tab_base, gelu_tab);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tile_max = max_u16x2(tile_max, o[j] & 0x7FFF7FFFu);
         }
         // 128B-swizzled staging (chunk c of row r at r*128 + ((c ^ (r & 7)) * 16)),
         // the output tensor map's swizzle
@@ -1482,14 +1494,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint32_t o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          uint32_t hv = rowcol_scale_pack_bf16x2(r[8 * q + 2 * j], r[8 * q + 2 * j + 1], sa2,
-                                                 sw[2 * j], sw[2 * j + 1]);
-          if (bias != nullptr) hv = add_bf16x2(hv, bw[j]);
-          if constexpr (kEpi == 1) {
-            hv = gelu_bf16x2(hv, tab_base, gelu_tab);
-            tile_max = max_u16x2(tile_max, hv & 0x7FFF7FFFu);
-          }
-          o[j] = hv;
+          o[j] = rowcol_scale_pack_bf16x2(r[8 * q + 2 * j], r[8 * q + 2 * j + 1], sa2, sw[2 * j],
+                                          sw[2 * j + 1]);
+          if (bias != nullptr) o[j] = add_bf16x2(o[j], bw[j]);
+        }
+        if constexpr (kEpi == 1) {
+          gelu_bf16x2_x4(o, tab_base, gelu_tab);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tile_max = max_u16x2(tile_max, o[j] & 0x7FFF7FFFu);
         }
         // 128B-swizzled staging (chunk c of row r at r*128 + ((c ^ (r & 7)) * 16)),
         // the output tensor map's swizzle
@@ -1525,16 +1537,24 @@ __global__ void __launch_bounds__(256) gelu_probe_kernel(const uint16_t* in, uin
   gelu_table_init(tab, threadIdx.x, blockDim.x);
   __syncthreads();
   const uint32_t tab_base = smem_u32(tab);
-  const int64_t pairs = count / 2;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < pairs;
+  // four words (eight values) per step through the epilogues' gelu_bf16x2_x4,
+  // the tail of fewer than eight values one at a time
+  const int64_t groups = count / 8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < groups;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint32_t w = static_cast<uint32_t>(in[2 * i]) | (static_cast<uint32_t>(in[2 * i + 1]) << 16);
-    const uint32_t g = gelu_bf16x2(w, tab_base, tab);
-    out[2 * i] = static_cast<uint16_t>(g & 0xFFFFu);
-    out[2 * i + 1] = static_cast<uint16_t>(g >> 16);
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = static_cast<uint32_t>(in[8 * i + 2 * j]) | (static_cast<uint32_t>(in[8 * i + 2 * j + 1]) << 16);
+    gelu_bf16x2_x4(w, tab_base, tab);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      out[8 * i + 2 * j] = static_cast<uint16_t>(w[j] & 0xFFFFu);
+      out[8 * i + 2 * j + 1] = static_cast<uint16_t>(w[j] >> 16);
+    }
   }
-  if ((count & 1) && blockIdx.x == 0 && threadIdx.x == 0)
-    out[count - 1] = static_cast<uint16_t>(gelu_bf16(in[count - 1], tab));
+  if (blockIdx.x == 0 && threadIdx.x == 0)
+    for (int64_t e = groups * 8; e < count; ++e) out[e] = static_cast<uint16_t>(gelu_bf16(in[e], tab));
 }
 
 // ---------------------------------------------------------------- host side
