@@ -133,19 +133,12 @@ __device__ __forceinline__ void warp_flag_error(B* bars, uint32_t bit) {
   __syncwarp();
 }
 
-__device__ __forceinline__ float bf16_round(float v) {
-  return __bfloat162float(__float2bfloat16_rn(v));
-}
-
 // Two floats -> two bf16 (round to nearest even) in one cvt.rn.bf16x2.f32.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
-
-__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // GELU, tanh approximation, evaluated in fp32 as torch does for bf16 inputs.
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -736,7 +729,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int tiles = num_m_pairs * num_n_blocks;
   const int count = pair < tiles ? (tiles - 1 - pair) / pairs + 1 : 0;  // same in both CTAs
   const int num_k_tiles = k / BK;
-  const int64_t sf_tile_stride = static_cast<int64_t>(k / 64) * 512;
   const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
 
   if (threadIdx.x == 0) {

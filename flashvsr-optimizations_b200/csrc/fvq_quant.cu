@@ -72,8 +72,6 @@ __device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2,
   return r;
 }
 
-__device__ __forceinline__ int64_t pad_up_dev(int64_t r) { return (r + 127) / 128 * 128; }
-
 // g = reciprocal(max(amax, 1e-12)) * 2688 with IEEE rounding at each step,
 // as torch evaluates 2688. / t on a device tensor.
 __device__ __forceinline__ float encode_scale(float amax) {
