@@ -870,7 +870,7 @@ def kernel_timing(lib, structs, ys, ws, ws_bytes, tokens, sptr, steps) -> dict:
             "gemm_ms": g1t + g2t, "quant_h_gbs": qh_bytes / (qh * 1e-3) / 1e9,
             "gemm1_tflops": tokens * 2 * d * f / (g1t * 1e-3) / 1e12,
             "gemm2_tflops": tokens * 2 * d * f / (g2t * 1e-3) / 1e12, "steps": steps,
-            "note": "quant_x includes the W2 scale replication; launches timed one layer at a time"}
+            "note": "quant_x also writes the replicated W2 scales when GEMM2 runs on one SM per tile (not with the default SM pairs); launches timed one layer at a time"}
 
 
 def e2e_timing(torch, dist, fvq, NVFP4FFN, sets, tokens, dev, stream, world, steps, warmup) -> dict:

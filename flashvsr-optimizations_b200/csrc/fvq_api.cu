@@ -359,6 +359,8 @@ int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_
   uint8_t* codes_h = c.take(static_cast<size_t>(rows * f / 2));
   uint8_t* sf_h = c.take(fvq::sf_bytes(rows, f));
   uint8_t* sf_w2_rep = c.take(static_cast<size_t>(4 * d * (f / 16)));
+  // GEMM2 on SM pairs reads W2's scales as they are: skip the replicated copy
+  if (residual == nullptr && fvq::gemm_pairs_raw_scales(rows)) sf_w2_rep = nullptr;
   float* g_x = &scalars[0];
   float* g_h = &scalars[1];
   float* amax_h = &scalars[2];
@@ -367,8 +369,8 @@ int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_
   };
   mark(0);
   // 1. amax(x) -> g_x -> x in NVFP4, one launch; it also zeroes amax_h before GEMM1
-  //    accumulates into it and writes the W2 scales in the layout of GEMM2's
-  //    128x256b scale copies
+  //    accumulates into it and, when GEMM2 runs on one SM per tile, writes the W2
+  //    scales in the layout of its 128x256b scale copies
   cudaError_t e = fvq::launch_amax_quantize(x, rows, d, g_x, codes_x, sf_x, amax_ws, amax_h,
                                             lin2->scale, d, f, sf_w2_rep, g_wait_limit,
                                             fvq::error_word_ptr(), st);

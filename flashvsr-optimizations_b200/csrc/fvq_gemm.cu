@@ -1811,6 +1811,7 @@ cudaError_t launch_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w,
 static int g_pairing = 1;  // SM pairs with W scales in the library layout
 void set_gemm_pairing(int mode) { g_pairing = mode; }
 bool gemm_pairs(int64_t m, int epilogue) { return g_pairing != 0 && epilogue == 0 && m % (2 * BM) == 0; }
+bool gemm_pairs_raw_scales(int64_t m) { return g_pairing == 1 && m % (2 * BM) == 0; }
 
 cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,

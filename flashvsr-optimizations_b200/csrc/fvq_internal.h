@@ -76,6 +76,9 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
 // m % 256 == 0 run on SM pairs (nvfp4_gemm_pair_kernel) when enabled.
 void set_gemm_pairing(int mode);  // 0 off, 1 pairs (raw W scales), 2 pairs (replicated)
 bool gemm_pairs(int64_t m, int epilogue);
+// The plain-epilogue GEMM of m rows runs on SM pairs reading W scales in their
+// library layout (pairing mode 1), so it needs no replicated copy of them.
+bool gemm_pairs_raw_scales(int64_t m);
 cudaError_t launch_gelu_probe(const uint16_t* in, uint16_t* out, int64_t count, cudaStream_t st);
 // E4M3 GEMM with per-row A scales and per-column W scales (fvq_gemm.cu); epilogue 1:
 // bias, GELU and per-row max |h| (fp32 bits) into row_amax.  k % 128 == 0, n % 256 == 0.
