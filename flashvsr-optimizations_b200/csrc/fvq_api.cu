@@ -360,7 +360,7 @@ int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_
   uint8_t* sf_h = c.take(fvq::sf_bytes(rows, f));
   uint8_t* sf_w2_rep = c.take(static_cast<size_t>(4 * d * (f / 16)));
   // GEMM2 on SM pairs reads W2's scales as they are: skip the replicated copy
-  if (residual == nullptr && fvq::gemm_pairs_raw_scales(rows)) sf_w2_rep = nullptr;
+  if (fvq::gemm_pairs_raw_scales(rows)) sf_w2_rep = nullptr;
   float* g_x = &scalars[0];
   float* g_h = &scalars[1];
   float* amax_h = &scalars[2];

@@ -700,7 +700,9 @@ struct PairBarriers {
 };
 static_assert(sizeof(PairBarriers) <= kBarrierBytes, "pair barrier area");
 
-template <bool kRawSfb>
+// kEpi 0: bf16(alpha*acc) + bias; kEpi 2 adds the gated residual of the DiT
+// block, out = bf16(residual + bf16(gate * y)), as the one-SM kernel does.
+template <int kEpi, bool kRawSfb>
 __global__ void __launch_bounds__(kNumThreads, 1)
     nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                            const __grid_constant__ CUtensorMap tmap_b_half,
@@ -708,7 +710,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                            const __grid_constant__ CUtensorMap tmap_sfb,
                            const float* __restrict__ g_a, const float* __restrict__ g_w,
                            const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m,
-                           int n, int k, uint64_t wait_limit) {
+                           int n, int k, uint64_t wait_limit, const uint16_t* __restrict__ residual,
+                           const uint16_t* __restrict__ gate) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
   if ((smem_u32(smem) & 1023u) != 0) {
@@ -930,6 +933,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint32_t w = y[c / 2 + j];
           if (bias != nullptr) w = add_bf16x2(w, bw[j]);
           o[j] = w;
+        }
+        if constexpr (kEpi == 2) {
+          // gated residual: out = bf16(x + bf16(gate * y)), each a single bf16 rounding
+          const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gate + col0 + c));
+          uint4 xv = make_uint4(0, 0, 0, 0);
+          if (row < m)
+            xv = __ldg(reinterpret_cast<const uint4*>(residual + static_cast<int64_t>(row) * n +
+                                                      col0 + c));
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] = add_bf16x2(xw[j], mul_bf16x2(gw[j], o[j]));
         }
         if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
       }
@@ -1670,17 +1684,18 @@ bool make_scale_maps(CUtensorMap* sfa, CUtensorMap* sfb, const uint8_t* a_sf, in
   return r == CUDA_SUCCESS;
 }
 
-template <bool kRawSfb>
+template <int kEpi, bool kRawSfb>
 cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
                              const CUtensorMap& msfa, const CUtensorMap& msfb, const float* g_a,
                              const float* g_w,
                              const uint16_t* bias, uint16_t* out, int m, int n, int k,
-                             uint64_t wait_limit, cudaStream_t st) {
+                             uint64_t wait_limit, cudaStream_t st,
+                             const uint16_t* residual = nullptr, const uint16_t* gate = nullptr) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_pair_kernel<kRawSfb>,
+    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_pair_kernel<kEpi, kRawSfb>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          PairPlan<kRawSfb>::kSmemBytes);
     if (e != cudaSuccess) return e;
@@ -1701,8 +1716,8 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, nvfp4_gemm_pair_kernel<kRawSfb>, ma, mb_half, msfa, msfb, g_a,
-                            g_w, bias, out, m, n, k, wait_limit);
+  return cudaLaunchKernelEx(&cfg, nvfp4_gemm_pair_kernel<kEpi, kRawSfb>, ma, mb_half, msfa, msfb,
+                            g_a, g_w, bias, out, m, n, k, wait_limit, residual, gate);
 }
 
 template <int kEpi>
@@ -1842,8 +1857,24 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                                    amax_out, wait_limit, st);
   }
   if (epilogue == 2) {
-    if (w_sf_rep == nullptr || residual == nullptr || gate == nullptr) {
-      if (why) *why = "the gated-residual epilogue needs replicated W scales, residual and gate";
+    if (residual == nullptr || gate == nullptr) {
+      if (why) *why = "the gated-residual epilogue needs the residual and the gate";
+      return cudaErrorInvalidValue;
+    }
+    if (gemm_pairs_raw_scales(m) && alpha == nullptr && w_sf != nullptr) {
+      alignas(64) CUtensorMap mb_half;
+      alignas(64) CUtensorMap msfa;
+      alignas(64) CUtensorMap msfb;
+      if (!make_code_map(&mb_half, w_codes, n, k, BN / 2) ||
+          !make_scale_maps(&msfa, &msfb, a_sf, m / BM, w_sf, false, n, k)) {
+        if (why) *why = "cuTensorMapEncodeTiled failed for the SM-pair GEMM";
+        return cudaErrorInvalidValue;
+      }
+      return launch_gemm_pair<2, true>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
+                                       wait_limit, st, residual, gate);
+    }
+    if (w_sf_rep == nullptr) {
+      if (why) *why = "the one-SM gated-residual epilogue needs replicated W scales";
       return cudaErrorInvalidValue;
     }
     return launch_gemm_t<2, false, true>(ma, mb, mo, a_sf, w_sf_rep, g_a, g_w, alpha, bias, out, mi,
@@ -1864,10 +1895,10 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
       return cudaErrorInvalidValue;
     }
     if (pair_rep)
-      return launch_gemm_pair<false>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
+      return launch_gemm_pair<0, false>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
+                                        wait_limit, st);
+    return launch_gemm_pair<0, true>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
                                      wait_limit, st);
-    return launch_gemm_pair<true>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
-                                  wait_limit, st);
   }
   if (w_sf_rep != nullptr)
     return launch_gemm_t<0, false, true>(ma, mb, mo, a_sf, w_sf_rep, g_a, g_w, alpha, bias, out, mi,

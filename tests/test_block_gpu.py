@@ -145,3 +145,21 @@ def test_block_rejects_bad_modulation_vectors(ffn):
         ffn.modulated(x, shift, scale.float(), gate, EPS)
     with pytest.raises(ValueError):
         ops.ln_modulate(x, shift, scale[:100], EPS)
+
+
+@pytest.mark.parametrize("m", [7680, 512, 300])
+def test_block_same_bits_on_one_sm_and_on_sm_pairs(ffn, m):
+    """The gated-residual GEMM runs on SM pairs by default when m % 256 == 0 and on one SM per
+    tile with pairing off (or for other row counts); both give the same bits."""
+    from flashvsr_optimizations_b200 import _lib
+    x = _x(m, W.D_MODEL, seed=m)
+    shift, scale, gate = _modulation(W.D_MODEL, seed=m)
+    try:
+        _lib.call("fvq_set_gemm_pairing", 0)
+        single = ffn.modulated(x, shift, scale, gate, EPS)
+        _lib.call("fvq_set_gemm_pairing", 1)
+        paired = ffn.modulated(x, shift, scale, gate, EPS)
+    finally:
+        _lib.call("fvq_set_gemm_pairing", 1)   # the library default
+    torch.cuda.synchronize()
+    assert torch.equal(paired, single)
