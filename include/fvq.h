@@ -358,13 +358,13 @@ int fvq_gelu_bf16_probe(const uint16_t* in, uint16_t* out, int64_t count, void* 
 
 /*
  * Library setting with no reference counterpart: NVFP4 GEMMs with the plain
- * bf16 epilogue whose m is a multiple of 256 (fvq_nvfp4_gemm, fvq_nvfp4_mm
- * without alpha, fvq_nvfp4_gemm_wrep, the second GEMM of fvq_nvfp4_ffn) run
- * on pairs of SMs (clusters of two CTAs sharing 256 x 256 tiles, tcgen05
- * cta_group::2).  mode 0 selects the one-SM kernel, 1 (the default) the pair
- * kernel reading the W scales in their library layout, 2 the pair kernel
- * reading the replicated copy where the caller has one.  All modes give the
- * same bits.
+ * bf16 epilogue whose m is a multiple of 256 (fvq_nvfp4_gemm with
+ * FVQ_EPI_BF16, fvq_nvfp4_gemm_wrep, the second GEMM of fvq_nvfp4_ffn and,
+ * in mode 1, the gated-residual GEMM of fvq_nvfp4_ffn_block) run on pairs of
+ * SMs (clusters of two CTAs sharing 256 x 256 tiles, tcgen05 cta_group::2).
+ * mode 0 selects the one-SM kernel, 1 (the default) the pair kernel reading
+ * the W scales in their library layout, 2 the pair kernel reading the
+ * replicated copy where the caller has one.  All modes give the same bits.
  * Applies to later launches from any thread; FVQ_EINVAL for other modes.
  */
 int fvq_set_gemm_pairing(int mode);
