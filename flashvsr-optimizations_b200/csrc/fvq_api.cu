@@ -331,9 +331,18 @@ namespace {
 // The FFN launch sequence.  ev: NULL, or 5 events recorded before the first
 // launch and after each of the four (for fvq_nvfp4_ffn_profile).  residual and
 // gate (both or neither): GEMM2 writes the gated residual residual + gate * FFN(x).
+// The DiT block's input step, applied to x inside the first launch.
+struct LnModulate {
+  const uint16_t* shift;
+  const uint16_t* scale;
+  float eps;
+  float* stats;  // [2 * rows] floats of scratch
+};
+
 int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
              uint16_t* y, void* workspace, size_t workspace_bytes, cudaStream_t st,
-             cudaEvent_t* ev, const uint16_t* residual = nullptr, const uint16_t* gate = nullptr) {
+             cudaEvent_t* ev, const uint16_t* residual = nullptr, const uint16_t* gate = nullptr,
+             const LnModulate* ln = nullptr) {
   if (int rc = check_linear(lin1, "fvq_nvfp4_ffn (linear 1)")) return rc;
   if (int rc = check_linear(lin2, "fvq_nvfp4_ffn (linear 2)")) return rc;
   if (lin1->out_features != lin2->in_features || lin2->out_features != lin1->in_features)
@@ -371,9 +380,14 @@ int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_
   // 1. amax(x) -> g_x -> x in NVFP4, one launch; it also zeroes amax_h before GEMM1
   //    accumulates into it and, when GEMM2 runs on one SM per tile, writes the W2
   //    scales in the layout of its 128x256b scale copies
-  cudaError_t e = fvq::launch_amax_quantize(x, rows, d, g_x, codes_x, sf_x, amax_ws, amax_h,
-                                            lin2->scale, d, f, sf_w2_rep, g_wait_limit,
-                                            fvq::error_word_ptr(), st);
+  //    (for the DiT block: of u = LN(x) * (1 + scale) + shift, computed on the fly)
+  cudaError_t e =
+      ln == nullptr
+          ? fvq::launch_amax_quantize(x, rows, d, g_x, codes_x, sf_x, amax_ws, amax_h, lin2->scale,
+                                      d, f, sf_w2_rep, g_wait_limit, fvq::error_word_ptr(), st)
+          : fvq::launch_amax_quantize_ln(x, rows, d, ln->shift, ln->scale, ln->eps, ln->stats, g_x,
+                                         codes_x, sf_x, amax_ws, amax_h, lin2->scale, d, f,
+                                         sf_w2_rep, g_wait_limit, fvq::error_word_ptr(), st);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(x) launch");
   mark(1);
   // 2. h = bf16(gelu(bf16(bf16(alpha1 * acc) + b1))), amax_h = max |h|
@@ -422,8 +436,9 @@ int fvq_ln_modulate(const uint16_t* x, int64_t rows, int64_t d, const uint16_t* 
 
 size_t fvq_nvfp4_ffn_block_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff) {
   if (rows <= 0 || d_model <= 0 || d_ff <= 0) return 0;
-  return round_up(static_cast<size_t>(rows * d_model * 2)) +
-         fvq_nvfp4_ffn_workspace_bytes(rows, d_model, d_ff);
+  // the FFN's workspace, then (mean, rstd) of every row
+  return fvq_nvfp4_ffn_workspace_bytes(rows, d_model, d_ff) +
+         round_up(static_cast<size_t>(rows) * 2 * sizeof(float));
 }
 
 int fvq_nvfp4_ffn_block(const uint16_t* x, int64_t rows, const uint16_t* shift,
@@ -453,12 +468,12 @@ int fvq_nvfp4_ffn_block(const uint16_t* x, int64_t rows, const uint16_t* shift,
   if (int rc = check_device()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // the FFN's workspace first, so that its zero-state amax counters sit at offset 0
-  // whatever the row count; u after it
+  // whatever the row count; the rows' LayerNorm statistics after it.  u itself is
+  // never stored: the first launch normalises, modulates and quantizes x in one go.
   const size_t ffn_bytes = fvq_nvfp4_ffn_workspace_bytes(rows, d, lin1->out_features);
-  uint16_t* u = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + ffn_bytes);
-  cudaError_t e = fvq::launch_ln_modulate(x, rows, d, shift, scale, eps, u, st);
-  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn_block layer norm launch");
-  return ffn_impl(u, rows, lin1, lin2, out, workspace, ffn_bytes, st, nullptr, x, gate);
+  float* stats = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ffn_bytes);
+  const LnModulate ln{shift, scale, eps, stats};
+  return ffn_impl(x, rows, lin1, lin2, out, workspace, ffn_bytes, st, nullptr, x, gate, &ln);
 }
 
 int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,

@@ -58,6 +58,16 @@ cudaError_t launch_amax_quantize(const uint16_t* x, int64_t rows, int64_t k, flo
                                  const uint8_t* rep_src, int64_t rep_n, int64_t rep_k,
                                  uint8_t* rep_dst, uint64_t wait_limit, uint32_t* err_word,
                                  cudaStream_t st);
+// launch_amax_quantize of u = bf16(bf16(LN(x) * bf16(1 + scale)) + shift) (LayerNorm
+// without affine, as launch_ln_modulate) without writing u: pass 1 keeps each row's
+// (mean, rstd) in stats[2 * rows] and takes max |u|, pass 2 recomputes u from x.
+// k % 64 == 0 and k <= 2048.
+cudaError_t launch_amax_quantize_ln(const uint16_t* x, int64_t rows, int64_t k,
+                                    const uint16_t* shift, const uint16_t* scale, float eps,
+                                    float* stats, float* g_out, uint8_t* codes, uint8_t* sf,
+                                    uint32_t* ws, float* zero_word, const uint8_t* rep_src,
+                                    int64_t rep_n, int64_t rep_k, uint8_t* rep_dst,
+                                    uint64_t wait_limit, uint32_t* err_word, cudaStream_t st);
 // W scales (128x4 layout, n % 256 == 0, k % 256 == 0) -> the replicated layout the
 // GEMM's 128x256b scale copies read; 4 * n * k / 16 bytes.
 cudaError_t launch_replicate_w_scales(const uint8_t* sf, int64_t n, int64_t k, uint8_t* rep,

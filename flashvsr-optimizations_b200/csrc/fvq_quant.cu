@@ -174,17 +174,25 @@ __device__ __forceinline__ void discard_l2_line(const void* p) {
   asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
 }
 
+// Element transform applied to each 16-value block of x before it is quantized
+// (block index b in row-major block order, the block's eight bf16x2 words).
+struct NoXform {
+  __device__ __forceinline__ void operator()(uint32_t, uint32_t (&)[8]) const {}
+};
+
 // Quantize x with encode scale g.  The work is cut into chunks of 32 blocks
 // (1 KB of x, one per warp step); this warp takes chunks warp_first,
 // warp_first + warp_stride, ...  kReverse walks the chunks from the end of x
 // (the part a producer kernel wrote last, most likely still in L2).
 // kDiscard drops each fully read 128-byte line of x from L2 without a
 // write-back: only for a scratch input that nothing reads afterwards.
-template <bool kReverse, bool kDiscard>
+// Xform (NoXform unless given) maps each real block before its maximum is taken.
+template <bool kReverse, bool kDiscard, class Xform = NoXform>
 __device__ __forceinline__ void quantize_blocks(const uint16_t* __restrict__ x, uint32_t rows,
                                                 uint32_t bpr, float g, uint8_t* __restrict__ codes,
                                                 uint8_t* __restrict__ sf, uint32_t warp_first,
-                                                uint32_t warp_stride, Div31 div) {
+                                                uint32_t warp_stride, Div31 div,
+                                                const Xform& xf = Xform()) {
   const float r6 = rcp_approx_ftz(6.0f);
   const float rg = rcp_approx_ftz(g);
 
@@ -228,7 +236,10 @@ __device__ __forceinline__ void quantize_blocks(const uint16_t* __restrict__ x, 
     for (int u = 0; u < kQuantUnroll; ++u) {
       if (c + u * warp_stride >= n_chunks) break;  // warp-uniform
       const uint32_t b = chunk[u] * 32 + lane;
-      const uint32_t* w = v[u];
+      uint32_t w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = v[u][j];
+      if (b < n_real) xf(b, w);
       const uint32_t m2 = bmax2(bmax2(bmax2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
                                       bmax2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)),
                                 bmax2(bmax2(w[4] & 0x7FFF7FFFu, w[5] & 0x7FFF7FFFu),
@@ -525,6 +536,230 @@ cudaError_t launch_amax_quantize(const uint16_t* x, int64_t rows, int64_t k, flo
   return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(amax_quantize_kernel),
                                      dim3(static_cast<unsigned>(blocks)), dim3(kThreads), args, 0,
                                      st);
+}
+
+namespace {
+
+// ---------------------------------------------------------------- LayerNorm + modulation fused in
+// The DiT block's FFN input u = bf16(bf16(LN(x) * bf16(1 + scale)) + shift) (LN without
+// affine), quantized without writing u: pass 1 takes each row's mean and rstd exactly as
+// ln_modulate_kernel does (one warp per row, same lane layout and summation order), keeps
+// them in `stats` and takes max |u|; pass 2 recomputes u block by block from x and quantizes.
+__device__ __forceinline__ uint32_t ln_pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t ln_add_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t ln_mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// u of one bf16x2 word of x, given the row's mean and rstd and the column pair's
+// bf16x2 words of (1 + scale) and shift.
+__device__ __forceinline__ uint32_t ln_modulate_word(uint32_t xw, float mean, float rstd,
+                                                     uint32_t one_scale, uint32_t shift) {
+  const float lo = (__uint_as_float(xw << 16) - mean) * rstd;
+  const float hi = (__uint_as_float(xw & 0xFFFF0000u) - mean) * rstd;
+  return ln_add_bf16x2(ln_mul_bf16x2(ln_pack_bf16x2(lo, hi), one_scale), shift);
+}
+
+struct LnModXform {
+  const float2* stats;      // [rows] (mean, rstd)
+  const uint4* shift;       // [d / 8]
+  const uint4* scale;
+  uint32_t bpr;             // 16-value blocks per row
+  Div31 div;
+  __device__ __forceinline__ void operator()(uint32_t b, uint32_t (&w)[8]) const {
+    const uint32_t row = __umulhi(b, div.magic) >> div.shift;
+    const uint32_t blk = b - row * bpr;
+    const float2 st = __ldcg(stats + row);
+    const uint4 s0 = __ldg(shift + 2 * blk), s1 = __ldg(shift + 2 * blk + 1);
+    const uint4 c0 = __ldg(scale + 2 * blk), c1 = __ldg(scale + 2 * blk + 1);
+    const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      w[j] = ln_modulate_word(w[j], st.x, st.y, ln_add_bf16x2(0x3F803F80u, cw[j]), sw[j]);
+  }
+};
+
+template <int kVec>
+__global__ void __launch_bounds__(kThreads, kVec >= 8 ? 2 : 3) amax_quantize_ln_kernel(
+    const uint16_t* __restrict__ x, int64_t rows, int64_t k, const uint16_t* __restrict__ shift,
+    const uint16_t* __restrict__ scale, float eps, float2* __restrict__ stats, float* g_out,
+    uint8_t* __restrict__ codes, uint8_t* __restrict__ sf, uint32_t* ws, float* zero_word,
+    const uint4* __restrict__ rep_src, int64_t rep_k64, int64_t rep_total16,
+    uint4* __restrict__ rep_dst, uint64_t wait_limit, uint32_t* err_word, Div31 div) {
+  __shared__ uint32_t warp_max[kThreads / 32];
+  __shared__ int go;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kThreads;
+  const int lane = threadIdx.x & 31;
+  uint32_t gen = 0;
+  if (threadIdx.x == 0) gen = ld_acquire_gpu(&ws[kWsGeneration]);
+
+  // pass 1: per-row statistics and max |u| (one warp per row)
+  const int d = static_cast<int>(k), nvec = d / 8;
+  const uint4* sh4 = reinterpret_cast<const uint4*>(shift);
+  const uint4* sc4 = reinterpret_cast<const uint4*>(scale);
+  uint32_t m2 = 0;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+       row < rows; row += warps) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * d);
+    uint4 v[kVec];
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      const int j = lane + i * 32;
+      v[i] = j < nvec ? __ldg(xr + j) : make_uint4(0, 0, 0, 0);
+      const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        sum += __uint_as_float(w[q] << 16) + __uint_as_float(w[q] & 0xFFFF0000u);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+    const float mean = sum / static_cast<float>(d);
+    float sq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      const int j = lane + i * 32;
+      if (j >= nvec) continue;
+      const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float a = __uint_as_float(w[q] << 16) - mean, b = __uint_as_float(w[q] & 0xFFFF0000u) - mean;
+        sq += a * a + b * b;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xFFFFFFFFu, sq, o);
+    const float rstd = rsqrtf(sq / static_cast<float>(d) + eps);
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      const int j = lane + i * 32;
+      if (j >= nvec) continue;
+      const uint4 s = __ldg(sh4 + j), c = __ldg(sc4 + j);
+      const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      const uint32_t sw[4] = {s.x, s.y, s.z, s.w}, cw[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t u = ln_modulate_word(w[q], mean, rstd, ln_add_bf16x2(0x3F803F80u, cw[q]), sw[q]);
+        m2 = bmax2(m2, u & 0x7FFF7FFFu);
+      }
+    }
+    if (lane == 0) stats[row] = make_float2(mean, rstd);
+  }
+  uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
+  // W-scale replication share
+  for (int64_t o = tid; o < rep_total16; o += nthreads) {
+    const int64_t x16 = o & 31, h = (o >> 7) & 1, jb = o >> 8;
+    const int64_t nb = jb / rep_k64, j = jb - nb * rep_k64;
+    rep_dst[o] = __ldg(rep_src + ((2 * nb + h) * rep_k64 + j) * 32 + x16);
+  }
+  __threadfence();  // the row statistics are read by other CTAs after the grid barrier
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t bm = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) bm = max(bm, warp_max[w]);
+    ws[kWsPartial + blockIdx.x] = bm;
+    go = grid_barrier(ws, gen, wait_limit, err_word) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!go) return;
+
+  // pass 2: the same amax in every CTA, then quantize u recomputed from x
+  uint32_t bm = 0;
+  for (int b = threadIdx.x; b < static_cast<int>(gridDim.x); b += kThreads)
+    bm = max(bm, __ldcg(&ws[kWsPartial + b]));
+  bm = __reduce_max_sync(0xFFFFFFFFu, bm);
+  __syncthreads();                     // warp_max reuse
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = bm;
+  __syncthreads();
+  uint32_t r = 0;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) r = max(r, warp_max[w]);
+  const float amax = __uint_as_float(r << 16);
+  const float g = encode_scale(amax);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    ws[kWsAmax] = __float_as_uint(amax);
+    if (g_out != nullptr) *g_out = g;
+    if (zero_word != nullptr) *zero_word = 0.0f;
+  }
+  constexpr uint32_t kWarps = kThreads / 32;
+  const LnModXform xf{stats, sh4, sc4, static_cast<uint32_t>(k / 16), div};
+  quantize_blocks<false, false>(x, static_cast<uint32_t>(rows), static_cast<uint32_t>(k / 16), g,
+                                codes, sf, blockIdx.x * kWarps + (threadIdx.x >> 5),
+                                gridDim.x * kWarps, div, xf);
+}
+
+template <int kVec>
+cudaError_t launch_aq_ln_t(const uint16_t* x, int64_t rows, int64_t k, const uint16_t* shift,
+                           const uint16_t* scale, float eps, float2* stats, float* g_out,
+                           uint8_t* codes, uint8_t* sf, uint32_t* ws, float* zero_word,
+                           const uint8_t* rep_src, int64_t rep_n, int64_t rep_k, uint8_t* rep_dst,
+                           uint64_t wait_limit, uint32_t* err_word, cudaStream_t st) {
+  static int resident[64] = {0};   // CTAs of this kernel per SM, per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (resident[dev] == 0) {
+    int nb = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &nb, amax_quantize_ln_kernel<kVec>, kThreads, 0);
+    if (e != cudaSuccess) return e;
+    resident[dev] = nb > 0 ? nb : 1;
+  }
+  const int64_t n_all = pad_up(rows, 128) * (k / 16);
+  int64_t blocks = (n_all + kThreads * kQuantUnroll - 1) / (kThreads * kQuantUnroll);
+  blocks = blocks < 1 ? 1 : blocks;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * resident[dev];
+  if (blocks > cap) blocks = cap;
+  if (blocks > kAmaxMaxBlocks) blocks = kAmaxMaxBlocks;
+  const uint4* rsrc = reinterpret_cast<const uint4*>(rep_src);
+  uint4* rdst = reinterpret_cast<uint4*>(rep_dst);
+  int64_t rep_k64 = rep_k / 64 > 0 ? rep_k / 64 : 1;
+  int64_t rep_total16 = rep_dst != nullptr ? rep_n * (rep_k / 16) * 4 / 16 : 0;
+  Div31 div = make_div31(static_cast<uint32_t>(k / 16));
+  void* args[] = {&x, &rows, &k, &shift, &scale, &eps, &stats, &g_out, &codes, &sf, &ws,
+                  &zero_word, &rsrc, &rep_k64, &rep_total16, &rdst, &wait_limit, &err_word, &div};
+  return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(amax_quantize_ln_kernel<kVec>),
+                                     dim3(static_cast<unsigned>(blocks)), dim3(kThreads), args, 0,
+                                     st);
+}
+
+}  // namespace
+
+cudaError_t launch_amax_quantize_ln(const uint16_t* x, int64_t rows, int64_t k,
+                                    const uint16_t* shift, const uint16_t* scale, float eps,
+                                    float* stats, float* g_out, uint8_t* codes, uint8_t* sf,
+                                    uint32_t* ws, float* zero_word, const uint8_t* rep_src,
+                                    int64_t rep_n, int64_t rep_k, uint8_t* rep_dst,
+                                    uint64_t wait_limit, uint32_t* err_word, cudaStream_t st) {
+  float2* st2 = reinterpret_cast<float2*>(stats);
+  switch (static_cast<int>((k / 8 + 31) / 32)) {
+    case 0:
+    case 1: return launch_aq_ln_t<1>(x, rows, k, shift, scale, eps, st2, g_out, codes, sf, ws, zero_word, rep_src, rep_n, rep_k, rep_dst, wait_limit, err_word, st);
+    case 2: return launch_aq_ln_t<2>(x, rows, k, shift, scale, eps, st2, g_out, codes, sf, ws, zero_word, rep_src, rep_n, rep_k, rep_dst, wait_limit, err_word, st);
+    case 3:
+    case 4: return launch_aq_ln_t<4>(x, rows, k, shift, scale, eps, st2, g_out, codes, sf, ws, zero_word, rep_src, rep_n, rep_k, rep_dst, wait_limit, err_word, st);
+    case 5:
+    case 6: return launch_aq_ln_t<6>(x, rows, k, shift, scale, eps, st2, g_out, codes, sf, ws, zero_word, rep_src, rep_n, rep_k, rep_dst, wait_limit, err_word, st);
+    case 7:
+    case 8: return launch_aq_ln_t<8>(x, rows, k, shift, scale, eps, st2, g_out, codes, sf, ws, zero_word, rep_src, rep_n, rep_k, rep_dst, wait_limit, err_word, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_rcp_probe(const float* in, float* out, int64_t n, cudaStream_t st) {

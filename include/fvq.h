@@ -195,8 +195,10 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
  * LN without affine: bf16((x - mean) * rsqrtf(var + eps)), mean and biased
  * variance of the row in fp32; shift, scale, gate: bf16 [d_model]; every
  * elementwise step one bf16 rounding (torch's semantics on bf16 tensors).
- * FFN(u) is fvq_nvfp4_ffn's result; the gated residual is applied in the
- * second GEMM's epilogue.  d_model % 8 == 0 and <= 2048; pointers 16-byte
+ * FFN(u) is fvq_nvfp4_ffn's result; u is never stored (the first launch
+ * normalises, modulates and quantizes x in one pass) and the gated residual
+ * is applied in the second GEMM's epilogue.  d_model % 8 == 0 and <= 2048
+ * (and the FFN's d_model % 64 == 0); pointers 16-byte
  * aligned, the workspace (fvq_nvfp4_ffn_block_workspace_bytes, zeroed once)
  * 32-byte aligned.
  */
