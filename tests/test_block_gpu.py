@@ -163,3 +163,24 @@ def test_block_same_bits_on_one_sm_and_on_sm_pairs(ffn, m):
         _lib.call("fvq_set_gemm_pairing", 1)   # the library default
     torch.cuda.synchronize()
     assert torch.equal(paired, single)
+
+
+@pytest.mark.parametrize("d,f,m", [(256, 512, 300), (512, 768, 512), (1024, 512, 129), (2048, 512, 384)])
+def test_block_other_widths_bit_exact_given_u(d, f, m):
+    """The block's first launch normalises and modulates x inside the quantizer (one
+    instantiation per row width); at every width its result equals running the stand-alone
+    LayerNorm + modulation kernel first: out = x + gate * FFN(ln_modulate(x)), bit for bit."""
+    g = torch.Generator().manual_seed(d + f)
+    seq = torch.nn.Sequential(torch.nn.Linear(d, f), torch.nn.GELU(approximate="tanh"), torch.nn.Linear(f, d))
+    with torch.no_grad():
+        for lin in (seq[0], seq[2]):
+            lin.weight.copy_(torch.randn(lin.weight.shape, generator=g) * 0.02)
+            lin.bias.copy_(torch.randn(lin.bias.shape, generator=g) * 0.01)
+    seq = seq.to(device="cuda", dtype=torch.bfloat16)
+    blk = NVFP4FFN(QuantLinear(seq[0], "nvfp4"), seq[1], QuantLinear(seq[2], "nvfp4"))
+    x = (torch.randn(m, d, generator=g) * 0.7).to(torch.bfloat16).cuda()
+    shift, scale, gate = _modulation(d, seed=d)
+    out = blk.modulated(x, shift, scale, gate, EPS)
+    ref = x + gate * blk(ops.ln_modulate(x, shift, scale, EPS))
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref), f"{int((out != ref).sum())} of {out.numel()} differ"
