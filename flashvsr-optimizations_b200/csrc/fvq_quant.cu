@@ -176,8 +176,12 @@ __device__ __forceinline__ void discard_l2_line(const void* p) {
 
 // Element transform applied to each 16-value block of x before it is quantized
 // (block index b in row-major block order, the block's eight bf16x2 words).
+// load(b) fetches what the transform needs for block b; it is issued together
+// with the block's own loads, one batch ahead.
 struct NoXform {
-  __device__ __forceinline__ void operator()(uint32_t, uint32_t (&)[8]) const {}
+  struct Aux {};
+  __device__ __forceinline__ Aux load(uint32_t) const { return Aux{}; }
+  __device__ __forceinline__ void operator()(uint32_t, uint32_t (&)[8], const Aux&) const {}
 };
 
 // Quantize x with encode scale g.  The work is cut into chunks of 32 blocks
@@ -205,8 +209,10 @@ __device__ __forceinline__ void quantize_blocks(const uint16_t* __restrict__ x, 
 
   // software pipeline: the next batch's loads are issued before this batch is
   // processed, so each thread keeps 2 * kQuantUnroll blocks of loads in flight
+  using Aux = typename Xform::Aux;
   uint32_t vn[kQuantUnroll][8];
-  auto load_batch = [&](uint32_t c0, uint32_t (&dst)[kQuantUnroll][8]) {
+  Aux an[kQuantUnroll];
+  auto load_batch = [&](uint32_t c0, uint32_t (&dst)[kQuantUnroll][8], Aux (&adst)[kQuantUnroll]) {
 #pragma unroll
     for (int u = 0; u < kQuantUnroll; ++u) {
       const uint32_t cu = c0 + u * warp_stride;
@@ -214,24 +220,28 @@ __device__ __forceinline__ void quantize_blocks(const uint16_t* __restrict__ x, 
       const uint32_t b = ch * 32 + lane;
       if (cu < n_chunks && b < n_real) {
         ld_stream_v8(xw + static_cast<size_t>(b) * 8, dst[u]);
+        adst[u] = xf.load(b);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) dst[u][j] = 0;
+        adst[u] = Aux{};
       }
     }
   };
-  load_batch(warp_first, vn);
+  load_batch(warp_first, vn, an);
   for (uint32_t c = warp_first; c < n_chunks; c += warp_stride * kQuantUnroll) {
     uint32_t v[kQuantUnroll][8];
+    Aux a[kQuantUnroll];
     uint32_t chunk[kQuantUnroll];
 #pragma unroll
     for (int u = 0; u < kQuantUnroll; ++u) {
       const uint32_t cu = c + u * warp_stride;
       chunk[u] = kReverse ? n_chunks - 1 - cu : cu;
+      a[u] = an[u];
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[u][j] = vn[u][j];
     }
-    load_batch(c + warp_stride * kQuantUnroll, vn);
+    load_batch(c + warp_stride * kQuantUnroll, vn, an);
 #pragma unroll
     for (int u = 0; u < kQuantUnroll; ++u) {
       if (c + u * warp_stride >= n_chunks) break;  // warp-uniform
@@ -239,7 +249,7 @@ __device__ __forceinline__ void quantize_blocks(const uint16_t* __restrict__ x, 
       uint32_t w[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) w[j] = v[u][j];
-      if (b < n_real) xf(b, w);
+      if (b < n_real) xf(b, w, a[u]);
       const uint32_t m2 = bmax2(bmax2(bmax2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
                                       bmax2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)),
                                 bmax2(bmax2(w[4] & 0x7FFF7FFFu, w[5] & 0x7FFF7FFFu),
@@ -576,10 +586,13 @@ struct LnModXform {
   const uint4* scale;
   uint32_t bpr;             // 16-value blocks per row
   Div31 div;
-  __device__ __forceinline__ void operator()(uint32_t b, uint32_t (&w)[8]) const {
+  using Aux = float2;       // the block's row statistics, fetched with the block
+  __device__ __forceinline__ float2 load(uint32_t b) const {
+    return __ldcg(stats + (__umulhi(b, div.magic) >> div.shift));
+  }
+  __device__ __forceinline__ void operator()(uint32_t b, uint32_t (&w)[8], const float2& st) const {
     const uint32_t row = __umulhi(b, div.magic) >> div.shift;
     const uint32_t blk = b - row * bpr;
-    const float2 st = __ldcg(stats + row);
     const uint4 s0 = __ldg(shift + 2 * blk), s1 = __ldg(shift + 2 * blk + 1);
     const uint4 c0 = __ldg(scale + 2 * blk), c1 = __ldg(scale + 2 * blk + 1);
     const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
