@@ -1,36 +1,39 @@
 #!/usr/bin/env python
-"""Benchmark of the NVFP4 FFN path on B200: one FFN layer (d_model 1536, d_ff 8960,
-GELU-tanh, bias) over 7680 tokens per GPU, one process per GPU.
+"""Benchmark of the NVFP4 FFN path on B200: the 30-layer FFN stack of the Wan-1.3B DiT
+(d_model 1536, d_ff 8960, GELU-tanh, bias; 30 distinct layers) over 15360 tokens, the
+token rows split across the GPUs, one process per GPU.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+                    [--workload c4|c5]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1)
 
-A step is one pass of the FFN layer over a batch of 7680 synthetic tokens
-(two 48x80 latent frames, Student-t(4) x 0.5 activations, N(0, 0.02) weights,
-N(0, 0.01) biases; seeded).  Token rows are independent, so each rank runs
-its own batch with replicated weights and no collective in the step (weak
-scaling); the output all-gather the path uses after a stack is timed
-separately (`gather`).  Inputs rotate over 8 distinct (activation, weight)
-sets, 312 MB in all, so no step finds its operands in the 126 MB L2.
+A step is one pass of the stack over one batch: 15360 synthetic tokens (four 48x80
+latent frames, N(0,1), seed 3), split into N contiguous row blocks of 15360/N rows
+(strong scaling: the total work is fixed as N grows).  Each rank runs the 30 layers on
+its rows with replicated weights (layer l: W ~ N(0, 0.02), bias ~ N(0, 0.01), seeded,
+``workloads.stack_layer_params(l)``), then one NCCL all-gather over NVLink assembles the
+[15360, 1536] output on every rank; the all-gather is inside the step.  `--workload c5`
+runs the 4K-stream batch instead: 64800 tokens (two 135x240 frames, Student-t(4) x 0.5,
+seed 4).  The weights alone (464 MB) and each layer's intermediate are far larger than
+the 126 MB L2, so no step finds its operands in L2.
 
-Prints one JSON line (rank 0).  `value` is whole-job tokens/s with inputs
-resident in HBM; `e2e` is the same metric through the public module API with
-host buffers (pinned H2D of the input and D2H of the output inside the timed
-region); `roofline` describes the GEMM kernel; `cpu_baseline` times the
-reference arithmetic (the CPU oracle) on this host.  Two separate measurements
-follow the timed steps (skip them with --no-extras): `stack_30_layers`, the
-30-layer stack of distinct layers over 15360 tokens with rows sharded across the
-ranks and the outputs all-gathered, `quantize_sweep` (rank 0), the
-activation quantizer on K in {1536, 8960} x M in {1024, 4096, 16384, 65536}, and
-`fp8_mode` (rank 0), the same layer in the reference's other mode,
-QuantLinear('fp8') (E4M3 W8A8, per-row scales), `pil_resize` (rank 0), the
-input pipeline's Pillow-exact 4x bicubic resize of 32-frame chunks, and
-`dit_block` (rank 0), the DiT block's step around the layer (LayerNorm +
-modulation in, gated residual out) fused against torch's composition.
+Prints one JSON line (rank 0).  `value` is whole-job tokens/s (tokens through all 30
+layers, gathered) with inputs resident in HBM, timed on the device as the max over
+ranks; `e2e` is the same metric through the public module API (NVFP4FFN modules and
+sharding.gather_rows) with host buffers: every step uploads each rank's rows from pinned
+host memory and rank 0 reads the gathered output back, inside the timed region;
+`roofline` describes the layer's two GEMM launches (per-launch CUDA-event times from a
+second pass over the same steps); `cpu_baseline` times the reference arithmetic (the
+CPU oracle) on this host.  Extras after the timed steps (skip with --no-extras):
+`single_layer` (one layer over 7680 tokens per GPU), `c5_stack` (the 64800-token batch),
+`stack_check` (N > 1: shards with whole-tensor global scales gathered equal the
+unsharded stack bit for bit), `quantize_sweep`, `fp8_mode`, `pil_resize`, `dit_block`
+(rank 0), and at N = 1 `flashinfer` (the reference's own sm_100 kernels on the same
+box and shapes).  The all-gather's time and bus bandwidth come last.
 
-`--impl reference` times the reference's NVFP4 FFN arithmetic on the host CPU
-(the oracle restatement; the reference itself needs FlashInfer on a GPU) with
-all host threads, on bounded samples of the same workload.
+`--impl reference` times the reference's NVFP4 FFN arithmetic on the host CPU (the
+oracle restatement; the reference itself needs FlashInfer on a GPU) with all host
+threads, on bounded samples of the same workload.
 """
 from __future__ import annotations
 
@@ -52,30 +55,42 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 D_MODEL, D_FF = 1536, 8960
-TOKENS = 7680
+LAYERS = 30
+TOKENS = 7680                       # the single-layer extra: tokens per GPU
 FLOP_PER_TOKEN = 2 * D_MODEL * D_FF * 2
 ROTATE = 8
 METRIC = "nvfp4_ffn_tokens_per_s"
-WORKLOAD = "ffn_layer_d1536_ff8960_gelu_tanh_bias_7680tok_per_gpu"
-# fvq_nvfp4_ffn launches per layer: amax+quantize(x), GEMM1 (+bias, GELU, amax), quantize(h), GEMM2
+# launches per layer of fvq_nvfp4_ffn: amax+quantize(x), GEMM1 (+bias, GELU, amax), quantize(h), GEMM2
 LAUNCHES_PER_LAYER = 4
+STACK_WORKLOADS = {
+    "c4": {"total": 15360, "dist": "gaussian", "seed": 3,
+           "name": "ffn_stack30_d1536_ff8960_15360tok_rows_sharded_allgather",
+           "input": "N(0,1) bf16, seed 3 (four 48x80 latent frames)"},
+    "c5": {"total": 64800, "dist": "student_t", "seed": 4,
+           "name": "ffn_stack30_d1536_ff8960_64800tok_rows_sharded_allgather",
+           "input": "Student-t(4) x 0.5 bf16, seed 4 (two 135x240 latent frames, 4K output)"},
+}
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
-    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--workload", choices=tuple(STACK_WORKLOADS), default="c4")
+    ap.add_argument("--tokens", type=int, default=TOKENS,
+                    help="tokens per GPU of the single-layer extra and of --case layer")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip the quantize sweep and the 30-layer stack (separate measurements)")
+                    help="skip the separate measurements that follow the timed steps")
     ap.add_argument("--cpu-seconds", type=float, default=20.0,
                     help="wall-time budget of the CPU baseline sample")
-    ap.add_argument("--case", choices=("ffn", "fp8_ffn", "pil_resize", "dit_block"), default="ffn",
-                    help="ffn: the benchmark (default); fp8_ffn / pil_resize / dit_block: only that "
-                         "separate measurement, --steps calls, one JSON line (e.g. under a profiler)")
+    ap.add_argument("--case", choices=("stack", "layer", "fp8_ffn", "pil_resize", "dit_block"),
+                    default="stack",
+                    help="stack: the benchmark (default); layer: one fvq_nvfp4_ffn layer over "
+                         "--tokens rows, --steps calls (e.g. under a profiler); fp8_ffn / "
+                         "pil_resize / dit_block: only that separate measurement, one JSON line")
     return ap.parse_args()
 
 
@@ -200,42 +215,366 @@ class ClockSampler:
                 "samples": len(sm), "power_w_max": max(power)}
 
 
+# ---------------------------------------------------------------- the stack workload
+def to_dev(torch, bits: np.ndarray, dev):
+    return torch.from_numpy(np.ascontiguousarray(bits).astype(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def stack_input_rows(wl: dict, r0: int, r1: int) -> np.ndarray:
+    """bf16 bits of rows [r0, r1) of the workload's input.  The whole input is generated
+    from its seed, so every rank cuts its block out of the same tensor."""
+    from flashvsr_optimizations_b200 import workloads as W
+    gen = W.gaussian if wl["dist"] == "gaussian" else W.student_t
+    return np.ascontiguousarray(gen(wl["total"], D_MODEL, seed=wl["seed"])[r0:r1])
+
+
+class StackWeights:
+    """The 30 layers' NVFP4 weights on one GPU, quantized by the library exactly as
+    QuantLinear(linear, 'nvfp4') quantizes them (global scale, then the 128x4-swizzled
+    codes and scales), with their C-ABI descriptors.  keep_bf16 also keeps the bf16
+    weights (for building the reference's own modules on the same weights)."""
+
+    def __init__(self, torch, ops, dev, layers=LAYERS, keep_bf16=False):
+        from flashvsr_optimizations_b200 import _lib, workloads as W
+        self.tensors, self.structs, self.bf16 = [], [], []
+        for layer in range(layers):
+            w1, b1, w2, b2 = W.stack_layer_params(layer)
+            pair = []
+            for wb, bb, in_f, out_f in ((w1, b1, D_MODEL, D_FF), (w2, b2, D_FF, D_MODEL)):
+                w, b = to_dev(torch, wb, dev), to_dev(torch, bb, dev)
+                g = ops.global_scale(w)
+                q, s = ops.nvfp4_quantize(w, g)
+                self.tensors.append((q, s, g, b))
+                pair.append(_lib.FvqLinear(q.data_ptr(), s.data_ptr(), g.data_ptr(), b.data_ptr(),
+                                           in_f, out_f))
+                if keep_bf16:
+                    self.bf16.append((w, b))
+                del w
+            self.structs.append(tuple(pair))
+
+    def modules(self, torch):
+        """The public modules: one NVFP4FFN (QuantLinear, GELU(tanh), QuantLinear) per layer."""
+        from flashvsr_optimizations_b200.ffn_quantization import NVFP4FFN, QuantLinear
+        mods = []
+        for i in range(0, len(self.tensors), 2):
+            (q1, s1, g1, b1), (q2, s2, g2, b2) = self.tensors[i], self.tensors[i + 1]
+            mods.append(NVFP4FFN(QuantLinear.from_quantized(q1, s1, g1, b1, D_MODEL),
+                                 torch.nn.GELU(approximate="tanh"),
+                                 QuantLinear.from_quantized(q2, s2, g2, b2, D_FF)))
+        return mods
+
+
+class StackRun:
+    """The stack on this rank's row block: one fvq_nvfp4_ffn call per layer (four launches,
+    ping-pong activation buffers, one workspace), then (N > 1) the NCCL all-gather of the
+    last layer's rows into the full output."""
+
+    def __init__(self, torch, lib, dev, stream, weights, wl, world, rank):
+        from flashvsr_optimizations_b200.sharding import row_range
+        self.total = wl["total"]
+        r0, r1 = row_range(self.total, world, rank)
+        self.rows = r1 - r0
+        self.x = to_dev(torch, stack_input_rows(wl, r0, r1), dev)
+        self.ws_bytes = lib.fvq_nvfp4_ffn_workspace_bytes(self.rows, D_MODEL, D_FF)
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=dev)
+        self.bufs = [torch.empty(self.rows, D_MODEL, dtype=torch.bfloat16, device=dev)
+                     for _ in range(2)]
+        self.out = (torch.empty(self.total, D_MODEL, dtype=torch.bfloat16, device=dev)
+                    if world > 1 else None)
+        self.lib, self.sptr, self.structs, self.world = lib, stream.cuda_stream, weights.structs, world
+
+    def layers(self, profile: list | None = None):
+        """The 30 layers on this rank's rows; with `profile`, each layer runs through
+        fvq_nvfp4_ffn_profile (events around its four launches, one host wait per layer)
+        and appends the four device times (ms)."""
+        cur = self.x
+        for i, (l1, l2) in enumerate(self.structs):
+            out = self.bufs[i % 2]
+            args = (cur.data_ptr(), self.rows, ctypes.byref(l1), ctypes.byref(l2), out.data_ptr(),
+                    self.ws.data_ptr(), self.ws_bytes, self.sptr)
+            if profile is None:
+                rc = self.lib.fvq_nvfp4_ffn(*args)
+            else:
+                ms = (ctypes.c_float * 4)()
+                rc = self.lib.fvq_nvfp4_ffn_profile(*args, ms)
+                profile.append(list(ms))
+            if rc != 0:
+                raise RuntimeError(self.lib.fvq_last_error().decode())
+            cur = out
+        return cur
+
+    def step(self):
+        y = self.layers()
+        if self.world > 1:
+            from flashvsr_optimizations_b200.sharding import gather_rows
+            return gather_rows(y, self.total, out=self.out)
+        return y
+
+
+def barrier_sync(torch, dist, dev, world):
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+
+
+def max_over_ranks(torch, dist, dev, world, values: list[float]) -> list[float]:
+    if world == 1:
+        return values
+    t = torch.tensor(values, device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
+def timed_steps(torch, dist, dev, stream, world, fn, steps, warmup, sampler=None) -> float:
+    """max over ranks of the device time (ms) of `steps` calls of fn, after `warmup` calls,
+    bracketed by a barrier and a device synchronisation on both sides."""
+    for i in range(max(3, warmup)):
+        fn(i)
+    barrier_sync(torch, dist, dev, world)
+    if sampler is not None:
+        sampler.start()
+        if isinstance(sampler, ClockSampler):
+            time.sleep(0.15)  # nvidia-smi's start-up
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier_sync(torch, dist, dev, world)
+    start.record(stream)
+    for i in range(steps):
+        fn(i)
+    end.record(stream)
+    barrier_sync(torch, dist, dev, world)
+    return max_over_ranks(torch, dist, dev, world, [start.elapsed_time(end)])[0]
+
+
+def stack_kernel_timing(torch, dist, dev, world, run, passes) -> dict:
+    """Per-launch device times of the layer's four launches over `passes` passes of the
+    stack (fvq_nvfp4_ffn_profile: the library's CUDA events around its launches on the
+    launching stream), max over ranks of the per-launch means."""
+    prof: list = []
+    run.layers(prof)                      # one untimed pass
+    prof.clear()
+    for _ in range(passes):
+        run.layers(prof)
+    qx, g1, qh, g2 = (statistics.fmean(p[j] for p in prof) for j in range(4))
+    qx, g1, qh, g2 = max_over_ranks(torch, dist, dev, world, [qx, g1, qh, g2])
+    rows = run.rows
+    qh_bytes = rows * D_FF * 2 + rows * D_FF // 2 + (rows + 127) // 128 * 128 * D_FF // 16
+    gemm_flop = rows * D_MODEL * D_FF * 2
+    return {"rows_per_launch": rows, "launches_timed_per_kernel": len(prof),
+            "quant_x_ms": qx, "gemm1_ms": g1, "quant_h_ms": qh, "gemm2_ms": g2, "gemm_ms": g1 + g2,
+            "gemm1_tflops": gemm_flop / (g1 * 1e-3) / 1e12, "gemm2_tflops": gemm_flop / (g2 * 1e-3) / 1e12,
+            "quant_h_GBps": qh_bytes / (qh * 1e-3) / 1e9, "quant_h_bytes": qh_bytes,
+            "note": "each layer's four launches queued back to back; one host wait per layer"}
+
+
+def stack_e2e(torch, dist, weights, run, dev, world, rank, steps, warmup) -> dict:
+    """The stack through the public API with host buffers: per step every rank uploads its
+    rows from pinned host memory, runs the 30 NVFP4FFN modules (torch custom op
+    fvq::nvfp4_ffn), all-gathers with sharding.gather_rows, and rank 0 copies the gathered
+    [total, 1536] output to pinned host memory.  Uploads, compute and the download run on
+    three streams, double-buffered, so one step's copies overlap its neighbours' compute."""
+    from flashvsr_optimizations_b200.sharding import gather_rows
+    mods = weights.modules(torch)
+    xh = run.x.cpu().pin_memory()
+    xd = [torch.empty_like(run.x) for _ in range(2)]
+    out_rows = run.total if world > 1 else run.rows
+    outs = ([torch.empty(run.total, D_MODEL, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+            if world > 1 else None)
+    yh = ([torch.empty(out_rows, D_MODEL, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+          if rank == 0 else None)
+    s_up, s_cmp, s_down = (torch.cuda.Stream(dev) for _ in range(3))
+    done_cmp = [torch.cuda.Event() for _ in range(2)]    # compute that read xd[b] finished
+    done_down = [torch.cuda.Event() for _ in range(2)]   # download that read outs[b] finished
+    for ev in done_cmp:
+        ev.record(s_cmp)
+    for ev in done_down:
+        ev.record(s_down)
+
+    def step(i):
+        b = i % 2
+        up = torch.cuda.Event()
+        with torch.cuda.stream(s_up):
+            s_up.wait_event(done_cmp[b])
+            xd[b].copy_(xh, non_blocking=True)
+            up.record(s_up)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(up)
+            y = xd[b]
+            for m in mods:
+                y = m(y)
+            if world > 1:
+                s_cmp.wait_event(done_down[b])
+                y = gather_rows(y, run.total, out=outs[b])
+            done_cmp[b].record(s_cmp)
+        with torch.cuda.stream(s_down):
+            s_down.wait_event(done_cmp[b])
+            if rank == 0:
+                yh[b].copy_(y, non_blocking=True)
+            if world == 1:
+                y.record_stream(s_down)
+            done_down[b].record(s_down)
+
+    with torch.no_grad():
+        for i in range(max(3, warmup)):
+            step(i)
+        barrier_sync(torch, dist, dev, world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(s_up)
+        for st in (s_cmp, s_down):
+            st.wait_event(s)
+        for i in range(steps):
+            step(i)
+        for st in (s_up, s_cmp):
+            ev = torch.cuda.Event()
+            ev.record(st)
+            s_down.wait_event(ev)
+        e.record(s_down)
+        torch.cuda.synchronize(dev)
+    ms = max_over_ranks(torch, dist, dev, world, [s.elapsed_time(e)])[0]
+    nbytes = run.total * D_MODEL * 2
+    return {"value": run.total * steps / (ms * 1e-3), "unit": "tokens/s",
+            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+            "steps": steps, "ms_per_step": ms / steps,
+            "api": "30 NVFP4FFN modules (torch custom op fvq::nvfp4_ffn) + sharding.gather_rows; "
+                   "each rank uploads its rows, rank 0 downloads the gathered output; "
+                   "three streams, double-buffered"}
+
+
+def stack_check(torch, dist, dev, weights, run, wl, world, rank) -> dict:
+    """N > 1: the stack run on the shards with whole-tensor global scales
+    (sharding.nvfp4_ffn_global_scales: an all-reduce MAX of amax(x) and of amax(h) per
+    layer), gathered, against the unsharded stack on rank 0 (fvq_nvfp4_ffn per layer over
+    all rows): the two must agree bit for bit."""
+    from flashvsr_optimizations_b200.sharding import gather_rows, nvfp4_ffn_global_scales
+    mods = weights.modules(torch)
+    with torch.no_grad():
+        y = run.x
+        for m in mods:
+            y = nvfp4_ffn_global_scales(y, m)
+        full = gather_rows(y, run.total)
+        res = {"check": "30-layer stack, shards with whole-tensor global scales, gathered, vs "
+                        "the unsharded stack on rank 0"}
+        if rank == 0:
+            ref = to_dev(torch, stack_input_rows(wl, 0, run.total), dev)
+            for m in mods:
+                ref = m(ref)
+            res["bit_identical"] = bool(torch.equal(full, ref))
+            res["differing_values"] = int((full != ref).sum().item())
+            del ref
+        del full, y
+    barrier_sync(torch, dist, dev, world)
+    return res
+
+
+def fused_requant_timing(torch, dist, dev, stream, world, weights, run, wl, rank) -> dict:
+    """The stack with the intermediate quantized inside GEMM1's epilogue (NVFP4FFN with
+    delayed h scaling: three launches per layer, no bf16 intermediate), through the public
+    modules, on this rank's rows.  Two batches of the stack workload alternate (this
+    rank's rows of the workload input and of a second batch with the next seed), so every
+    call's estimate of max |h| comes from the other batch, as in a video stream; the
+    output is compared with the exact stack on the same batch."""
+    from flashvsr_optimizations_b200.sharding import row_range
+    mods = weights.modules(torch)
+    for m in mods:
+        m.set_h_scaling("delayed")
+    r0, r1 = row_range(wl["total"], world, rank)
+    other = to_dev(torch, stack_input_rows(dict(wl, seed=wl["seed"] + 100), r0, r1), dev)
+    batches = [run.x, other]
+
+    def fused(i):
+        y = batches[i % 2]
+        for m in mods:
+            y = m(y)
+        return y
+
+    with torch.no_grad():
+        fused(1)                                       # exact; seeds the estimates
+        ms = timed_steps(torch, dist, dev, stream, world, fused, 4, 2) / 4
+        fused(1)
+        y_f = fused(0).float()                        # estimates from the other batch
+        y_e = run.layers().float()
+        rel = float(((y_f - y_e).norm() / y_e.norm()).item())
+        flags = max(m.h_flags() for m in mods)
+        prof = (ctypes.c_float * 3)()
+        hint = torch.full((1,), 4.0, dtype=torch.float32, device=dev)
+        seen = torch.zeros(1, dtype=torch.float32, device=dev)
+        fl = torch.zeros(1, dtype=torch.int32, device=dev)
+        fws_bytes = run.lib.fvq_nvfp4_ffn_fused_workspace_bytes(run.rows, D_MODEL, D_FF)
+        fws = torch.zeros(fws_bytes, dtype=torch.uint8, device=dev)
+        acc = [[] for _ in range(3)]
+        cur = run.x
+        for i, (l1, l2) in enumerate(run.structs):
+            out = run.bufs[i % 2]
+            rc = run.lib.fvq_nvfp4_ffn_fused_profile(
+                cur.data_ptr(), run.rows, ctypes.byref(l1), ctypes.byref(l2), out.data_ptr(),
+                hint.data_ptr(), 1, seen.data_ptr(), fl.data_ptr(), fws.data_ptr(), fws_bytes,
+                run.sptr, prof)
+            if rc != 0:
+                raise RuntimeError(run.lib.fvq_last_error().decode())
+            for j in range(3):
+                acc[j].append(prof[j])
+            cur = out
+    ms, = max_over_ranks(torch, dist, dev, world, [ms])
+    kq = [statistics.fmean(a) for a in acc]
+    return {"mode": "NVFP4FFN.set_h_scaling('delayed'): GELU + NVFP4 quantization of h in GEMM1's "
+                    "epilogue with the previous call's max |h| x 2 (fvq_nvfp4_ffn_fused)",
+            "ms_per_stack": ms, "tokens_per_s": wl["total"] / (ms * 1e-3),
+            "rel_vs_exact_stack": rel, "flags": flags,
+            "kernels_ms": {"quant_x": kq[0], "gemm1_bias_gelu_quantize": kq[1], "gemm2_bias": kq[2]},
+            "gemm1_tflops": run.rows * D_MODEL * D_FF * 2 / (kq[1] * 1e-3) / 1e12}
+
+
+def gather_timing(torch, dist, dev, stream, world, run, reps=20) -> dict:
+    """The output all-gather alone (sharding.gather_rows, NCCL all_gather_into_tensor into
+    the preallocated output): device time, max over ranks, and NCCL's bus bandwidth."""
+    from flashvsr_optimizations_b200.sharding import gather_rows
+    local = run.bufs[1]
+    ms = timed_steps(torch, dist, dev, stream, world,
+                     lambda i: gather_rows(local, run.total, out=run.out), reps, 3) / reps
+    nbytes = run.total * D_MODEL * 2
+    busbw = (world - 1) / world * nbytes / (ms * 1e-3) / 1e9
+    return {"ms": ms, "bytes": nbytes, "busbw_GBps": busbw,
+            "frac_of_nvlink_peer_copy": busbw / 770.0,
+            "api": "sharding.gather_rows (NCCL all_gather_into_tensor, no padding or concatenation)"}
+
+
 # ---------------------------------------------------------------- CPU legs
-def cpu_ffn_tokens_per_s(steps: int, warmup: int, seconds: float, log=print) -> dict:
-    """Reference NVFP4 FFN arithmetic (the oracle, fp32 matmul) on host threads."""
+def cpu_stack_tokens_per_s(steps: int, warmup: int, seconds: float, wl: dict) -> dict:
+    """The reference NVFP4 FFN arithmetic (the oracle, fp32 BLAS matmul) on host threads, on a
+    bounded sample of the stack workload: `rows` tokens of its input through layer 0 of the
+    stack per step (every layer has the same shapes and cost), scaled to tokens through all
+    30 layers."""
     from oracle import nvfp4_oracle as O
     from flashvsr_optimizations_b200 import workloads as W
     threads = os.cpu_count() or 1
-    w1, b1 = W.linear_params(D_FF, D_MODEL, seed=20, b_std=0.01)
-    w2, b2 = W.linear_params(D_MODEL, D_FF, seed=21, b_std=0.01)
+    w1, b1, w2, b2 = W.stack_layer_params(0)
     l1, l2 = O.OracleQuantLinear(w1, b1), O.OracleQuantLinear(w2, b2)
-    # calibrate the per-step sample so the whole run fits the time budget
-    probe = W.student_t(64, D_MODEL, seed=1)
-    t0 = time.perf_counter()
+    x_all = stack_input_rows(wl, 0, 4096)
+    probe = x_all[:64]
     O.ffn_forward(probe, l1, l2, fp32_matmul=True)
     t0 = time.perf_counter()
     O.ffn_forward(probe, l1, l2, fp32_matmul=True)
     per_tok = (time.perf_counter() - t0) / 64
     rows = int(seconds / max(1, steps + warmup) / max(per_tok, 1e-6))
     rows = max(16, min(1024, rows // 16 * 16))
-    x_all = W.student_t(TOKENS, D_MODEL, seed=1)
     for i in range(warmup):
-        O.ffn_forward(x_all[(i * rows) % (TOKENS - rows):][:rows], l1, l2, fp32_matmul=True)
+        O.ffn_forward(x_all[(i * rows) % (4096 - rows):][:rows], l1, l2, fp32_matmul=True)
     times = []
     for i in range(steps):
-        xs = x_all[(i * rows) % (TOKENS - rows):][:rows]
+        xs = x_all[(i * rows) % (4096 - rows):][:rows]
         t = time.perf_counter()
         O.ffn_forward(xs, l1, l2, fp32_matmul=True)
         times.append(time.perf_counter() - t)
-    total = sum(times)
-    return {"value": rows * steps / total, "unit": "tokens/s", "cores": threads,
-            "kind": "port", "rows_per_step": rows, "seconds": total,
-            "sample": (f"{steps} steps of {rows} tokens from the 7680-token layer workload; numpy oracle "
-                       f"(quantize, dequantize, fp32 BLAS matmul, bias, GELU-tanh, requantize); "
+    per_layer = sum(times)
+    return {"value": rows * steps / (per_layer * LAYERS), "unit": "tokens/s", "cores": threads,
+            "kind": "port", "rows_per_step": rows, "seconds": per_layer,
+            "sample": (f"{steps} steps of {rows} tokens of the {wl['total']}-token stack input through "
+                       f"layer 0 (numpy oracle: quantize, dequantize, fp32 BLAS matmul, bias, "
+                       f"GELU-tanh, requantize, second GEMM), the per-layer time x {LAYERS} layers; "
                        f"weights quantized once outside the timing; {threads} host threads")}
 
 
-# ---------------------------------------------------------------- GPU setup
+# ---------------------------------------------------------------- the single-layer extra
 def make_sets(torch, ops, dev, tokens, rank):
     """ROTATE distinct (x, layer-1, layer-2) sets on the device, seeded per rank / set."""
     sets = []
@@ -256,6 +595,53 @@ def make_sets(torch, ops, dev, tokens, rank):
     return sets
 
 
+def single_layer_timing(torch, dist, ops, lib, dev, stream, world, rank, tokens, steps) -> dict:
+    """One FFN layer over `tokens` tokens per GPU (two 48x80 latent frames, Student-t(4) x 0.5)
+    with no collective (weak scaling), rotating over ROTATE distinct activation/weight sets
+    (312 MB > L2): whole-job tokens/s and the four launches' device times."""
+    from flashvsr_optimizations_b200 import _lib
+    sets = make_sets(torch, ops, dev, tokens, rank)
+    ws_bytes = lib.fvq_nvfp4_ffn_workspace_bytes(tokens, D_MODEL, D_FF)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    ys = [torch.empty(tokens, D_MODEL, dtype=torch.bfloat16, device=dev) for _ in range(ROTATE)]
+    sptr = stream.cuda_stream
+    structs = []
+    for x, ((q1, s1, g1, b1), (q2, s2, g2, b2)) in sets:
+        l1 = _lib.FvqLinear(q1.data_ptr(), s1.data_ptr(), g1.data_ptr(), b1.data_ptr(), D_MODEL, D_FF)
+        l2 = _lib.FvqLinear(q2.data_ptr(), s2.data_ptr(), g2.data_ptr(), b2.data_ptr(), D_FF, D_MODEL)
+        structs.append((x, l1, l2))
+
+    def step(i):
+        x, l1, l2 = structs[i % ROTATE]
+        rc = lib.fvq_nvfp4_ffn(x.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2),
+                               ys[i % ROTATE].data_ptr(), ws.data_ptr(), ws_bytes, sptr)
+        if rc != 0:
+            raise RuntimeError(lib.fvq_last_error().decode())
+
+    ms = timed_steps(torch, dist, dev, stream, world, step, steps, 5)
+    kms = (ctypes.c_float * 4)()
+    acc = [[] for _ in range(4)]
+    for i in range(min(steps, 200) + 5):
+        x, l1, l2 = structs[i % ROTATE]
+        rc = lib.fvq_nvfp4_ffn_profile(x.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2),
+                                       ys[i % ROTATE].data_ptr(), ws.data_ptr(), ws_bytes, sptr, kms)
+        if rc != 0:
+            raise RuntimeError(lib.fvq_last_error().decode())
+        if i >= 5:
+            for j in range(4):
+                acc[j].append(kms[j])
+    qx, g1, qh, g2 = max_over_ranks(torch, dist, dev, world, [statistics.fmean(a) for a in acc])
+    value = tokens * world * steps / (ms * 1e-3)
+    gemm_flop = tokens * FLOP_PER_TOKEN
+    return {"workload": "ffn_layer_d1536_ff8960_gelu_tanh_bias_7680tok_per_gpu (weak scaling)",
+            "tokens_per_s": value, "ms_per_layer": ms / steps, "steps": steps,
+            "tflops": value * FLOP_PER_TOKEN / 1e12,
+            "kernels_ms": {"quant_x": qx, "gemm1_bias_gelu_amax": g1, "quant_h": qh, "gemm2_bias": g2},
+            "gemm_tflops": gemm_flop / ((g1 + g2) * 1e-3) / 1e12,
+            "l2": f"inputs rotate over {ROTATE} distinct activation/weight sets (312 MB > 126 MB L2)"}
+
+
+# ---------------------------------------------------------------- other separate measurements
 def quantize_sweep(torch, lib, dev, stream, hbm_peak) -> list:
     """The standalone activation-quantize sweep: K in {1536, 8960} x M in {1024, 4096, 16384,
     65536}, N(0,1) with 0.1% of elements x50 (seed 2).  Per shape: the quantizer with a
@@ -305,76 +691,6 @@ def quantize_sweep(torch, lib, dev, stream, hbm_peak) -> list:
             del x, codes, sf
     torch.cuda.empty_cache()
     return out
-
-
-def stack_timing(torch, dist, ops, lib, dev, stream, world, rank, steps=10) -> dict:
-    """The 30-layer FFN stack: M = 15360 N(0,1) tokens (seed 3), 30 layers with distinct
-    N(0,0.02) weights (and N(0,0.01) biases), token rows sharded over the ranks, outputs
-    all-gathered.  Time = max over ranks of (30 layers + gather)."""
-    from flashvsr_optimizations_b200.sharding import gather_rows, row_range
-    total, layers = 15360, 30
-    r0, r1 = row_range(total, world, rank)
-    rows = r1 - r0
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(3)
-    x_all = torch.randn(total, D_MODEL, device=dev, generator=gen).to(torch.bfloat16)
-    x = x_all[r0:r1].contiguous()
-    del x_all
-    structs, keep = [], []
-    for layer in range(layers):
-        gl = torch.Generator(device=dev)
-        gl.manual_seed(100 + layer)
-        pair = []
-        for (n, k) in ((D_FF, D_MODEL), (D_MODEL, D_FF)):
-            w = (torch.randn(n, k, device=dev, generator=gl) * 0.02).to(torch.bfloat16)
-            b = (torch.randn(n, device=dev, generator=gl) * 0.01).to(torch.bfloat16)
-            gsc = ops.global_scale(w)
-            q, sc = ops.nvfp4_quantize(w, gsc)
-            keep.append((q, sc, gsc, b))
-            pair.append(_lib_linear(q, sc, gsc, b, k, n))
-        structs.append(pair)
-    ws_bytes = lib.fvq_nvfp4_ffn_workspace_bytes(rows, D_MODEL, D_FF)
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
-    bufs = [torch.empty(rows, D_MODEL, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    st = stream.cuda_stream
-
-    def run_stack():
-        cur = x
-        for i, (l1, l2) in enumerate(structs):
-            out = bufs[i % 2]
-            rc = lib.fvq_nvfp4_ffn(cur.data_ptr(), rows, ctypes.byref(l1), ctypes.byref(l2),
-                                   out.data_ptr(), ws.data_ptr(), ws_bytes, st)
-            if rc != 0:
-                raise RuntimeError(lib.fvq_last_error().decode())
-            cur = out
-        return gather_rows(cur, total) if world > 1 else cur
-
-    for _ in range(2):
-        run_stack()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for _ in range(steps):
-        y = run_stack()
-    e.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = s.elapsed_time(e) / steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    tflops = total * layers * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12
-    finite = bool(torch.isfinite(y.float()).all().item())
-    return {"tokens": total, "layers": layers, "ms_per_stack": ms,
-            "tokens_per_s": total / (ms * 1e-3), "tflops": tflops, "finite_output": finite,
-            "rows_per_rank": rows, "includes": "30 fvq_nvfp4_ffn calls per rank + all-gather of the outputs"}
-
-
-def _lib_linear(q, s, g, b, in_f, out_f):
-    from flashvsr_optimizations_b200 import _lib
-    return _lib.FvqLinear(q.data_ptr(), s.data_ptr(), g.data_ptr(), b.data_ptr(), in_f, out_f)
 
 
 def fp4_library_sustained(torch, dev, seconds=2.0) -> dict | None:
@@ -647,6 +963,176 @@ def fp4_library_peak(torch, dev) -> float | None:
         return None
 
 
+# ---------------------------------------------------------------- the reference's sm_100 kernels
+def _event_ms(torch, stream, fn, reps: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(reps):
+        fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def flashinfer_comparison(torch, ops, lib, dev, stream, weights, run) -> dict:
+    """The reference's own path on this GPU and shapes: FlashInfer's sm_100a
+    nvfp4_quantize, its CUTLASS mm_fp4 (ffn_quantization.py:64-67) and the reference's
+    QuantLinear modules (its global_scale Triton kernel, FlashInfer, torch bias and GELU),
+    from the reference module installed unmodified in baseline/_ref and FlashInfer's JIT
+    modules prebuilt in baseline/fi_jit, against this library on the same inputs.
+    speedup = reference time / this library's time."""
+    ref_dir, jit_dir = ROOT / "baseline" / "_ref", ROOT / "baseline" / "fi_jit"
+    if not (ref_dir / "ffn_quantization.py").exists():
+        return {"unavailable": "the reference module is not installed in baseline/_ref "
+                               "(__graft_entry__.build() installs it where the reference tree exists)"}
+    os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", str(jit_dir))
+    os.environ.setdefault("FLASHINFER_CUDA_ARCH_LIST", "10.0a")
+    try:
+        import flashinfer
+        if str(ref_dir) not in sys.path:
+            sys.path.insert(0, str(ref_dir))
+        import ffn_quantization as ref
+    except Exception as exc:  # noqa: BLE001
+        return {"unavailable": f"FlashInfer or the reference module did not load: {type(exc).__name__}: {exc}"}
+    from flashvsr_optimizations_b200 import workloads as W
+    st = stream.cuda_stream
+    res = {"flashinfer": flashinfer.__version__}
+    try:
+        with torch.no_grad():
+            # --- the activation quantizer on the sweep's shapes (N(0,1), 0.1% x50, seed 2)
+            quant = {}
+            for k in W.QUANT_SWEEP_K:
+                for m in W.QUANT_SWEEP_M:
+                    gen = torch.Generator(device=dev)
+                    gen.manual_seed(2)
+                    x = torch.randn(m, k, device=dev, generator=gen)
+                    idx = torch.randint(0, m * k, (max(1, m * k // 1000),), device=dev, generator=gen)
+                    x.view(-1)[idx] *= 50.0
+                    x = x.to(torch.bfloat16)
+                    del idx
+                    g = ref.global_scale(x)
+                    codes = torch.empty(m, k // 2, dtype=torch.uint8, device=dev)
+                    sf = torch.empty((m + 127) // 128 * 128, k // 16, dtype=torch.uint8, device=dev)
+                    ws = torch.zeros(lib.fvq_amax_workspace_bytes(), dtype=torch.uint8, device=dev)
+                    gout = torch.empty(1, dtype=torch.float32, device=dev)
+                    reps = max(5, min(200, int(2e9 // (2 * m * k))))
+                    t_ref = _event_ms(torch, stream, lambda: flashinfer.nvfp4_quantize(x, g), reps)
+                    t_our = _event_ms(torch, stream, lambda: lib.fvq_nvfp4_quantize(
+                        x.data_ptr(), m, k, g.data_ptr(), codes.data_ptr(), sf.data_ptr(), st), reps)
+                    t_ref_d = _event_ms(torch, stream,
+                                        lambda: flashinfer.nvfp4_quantize(x, ref.global_scale(x)), reps)
+                    t_our_d = _event_ms(torch, stream, lambda: lib.fvq_nvfp4_quantize_dynamic(
+                        x.data_ptr(), m, k, None, gout.data_ptr(), codes.data_ptr(), sf.data_ptr(),
+                        ws.data_ptr(), ws.numel(), st), reps)
+                    q_ref, s_ref = flashinfer.nvfp4_quantize(x, g)
+                    lib.fvq_nvfp4_quantize(x.data_ptr(), m, k, g.data_ptr(), codes.data_ptr(),
+                                           sf.data_ptr(), st)
+                    same = bool(torch.equal(q_ref.view(torch.uint8), codes) and
+                                torch.equal(s_ref.view(torch.uint8).reshape(-1), sf.reshape(-1)))
+                    quant[f"{m}x{k}"] = {"ref_us": round(t_ref * 1e3, 2), "ours_us": round(t_our * 1e3, 2),
+                                         "speedup": t_ref / t_our,
+                                         "with_global_scale_ref_us": round(t_ref_d * 1e3, 2),
+                                         "with_global_scale_ours_us": round(t_our_d * 1e3, 2),
+                                         "with_global_scale_speedup": t_ref_d / t_our_d,
+                                         "same_bits": same}
+                    del x, codes, sf, q_ref, s_ref
+            res["quantize"] = quant
+            torch.cuda.empty_cache()
+
+            # --- the reference's modules on the stack's weights
+            def ref_linear(w, b):
+                lin = torch.nn.Linear(w.shape[1], w.shape[0], bias=True, device=dev, dtype=torch.bfloat16)
+                lin.weight.copy_(w)
+                lin.bias.copy_(b)
+                return ref.QuantLinear(lin, "nvfp4")
+
+            ref_layers = []
+            for i in range(0, len(weights.bf16), 2):
+                (w1, b1), (w2, b2) = weights.bf16[i], weights.bf16[i + 1]
+                ref_layers.append(torch.nn.Sequential(ref_linear(w1, b1), torch.nn.GELU(approximate="tanh"),
+                                                      ref_linear(w2, b2)))
+            rows = run.rows
+            x = run.x
+            # --- the two GEMM shapes of a layer at this batch (mm_fp4 with the bias add as the
+            # reference runs it; this library's GEMM1 also applies GELU and takes the amax)
+            l1, l2 = ref_layers[0][0], ref_layers[0][2]
+            g_x = ref.global_scale(x)
+            qx, sx = flashinfer.nvfp4_quantize(x, g_x)
+            (mq1, ms1, mg1, mb1), (mq2, ms2, mg2, mb2) = weights.tensors[0], weights.tensors[1]
+            h = torch.nn.functional.gelu(l1(x), approximate="tanh")
+            g_h = ref.global_scale(h)
+            qh, sh = flashinfer.nvfp4_quantize(h, g_h)
+            gemms = {}
+            for name, (qa, sa, ga, lin, mq, ms, mg, mb, n, k, epi) in (
+                    (f"gemm1_{rows}x{D_FF}x{D_MODEL}", (qx, sx, g_x, l1, mq1, ms1, mg1, mb1, D_FF, D_MODEL, 1)),
+                    (f"gemm2_{rows}x{D_MODEL}x{D_FF}", (qh, sh, g_h, l2, mq2, ms2, mg2, mb2, D_MODEL, D_FF, 0))):
+                alpha = 1. / (ga * lin.global_sf)
+                out = torch.empty(rows, n, dtype=torch.bfloat16, device=dev)
+                amax = torch.zeros(1, dtype=torch.float32, device=dev)
+                t_ref = _event_ms(torch, stream, lambda: flashinfer.mm_fp4(
+                    qa, lin.qweight.t(), sa, lin.scale.t(), alpha=alpha, out_dtype=torch.bfloat16,
+                    backend="cutlass") + lin.bias, 20)
+                t_our = _event_ms(torch, stream, lambda: lib.fvq_nvfp4_gemm(
+                    qa.view(torch.uint8).data_ptr(), sa.view(torch.uint8).data_ptr(), ga.data_ptr(),
+                    mq.data_ptr(), ms.data_ptr(), mg.data_ptr(), mb.data_ptr(), out.data_ptr(),
+                    rows, n, k, epi, amax.data_ptr() if epi == 1 else None, st), 20)
+                flop = 2 * rows * n * k
+                gemms[name] = {"ref_mm_fp4_plus_bias_us": round(t_ref * 1e3, 2),
+                               "ours_us": round(t_our * 1e3, 2), "speedup": t_ref / t_our,
+                               "ours_tflops": flop / (t_our * 1e-3) / 1e12,
+                               "ours_epilogue": "bias + GELU + amax" if epi == 1 else "bias"}
+            res["gemm"] = gemms
+            del h, qh, sh
+            torch.cuda.empty_cache()
+            # --- one layer and the whole stack, reference modules against fvq_nvfp4_ffn
+            l0 = run.structs[0]
+            y0 = run.bufs[0]
+            def ours_layer():
+                rc = lib.fvq_nvfp4_ffn(x.data_ptr(), rows, ctypes.byref(l0[0]), ctypes.byref(l0[1]),
+                                       y0.data_ptr(), run.ws.data_ptr(), run.ws_bytes, st)
+                if rc != 0:
+                    raise RuntimeError(lib.fvq_last_error().decode())
+
+            t_ref = _event_ms(torch, stream, lambda: ref_layers[0](x), 10)
+            t_our = _event_ms(torch, stream, ours_layer, 10)
+            y_ref0 = ref_layers[0](x)
+            ours_layer()
+            same_layer = bool(torch.equal(y_ref0, y0))
+            del y_ref0
+            res["layer"] = {"rows": rows, "ref_ms": t_ref, "ours_ms": t_our, "speedup": t_ref / t_our,
+                            "same_bits": same_layer}
+
+            def ref_stack():
+                y = x
+                for m in ref_layers:
+                    y = m(y)
+                return y
+
+            t_ref = _event_ms(torch, stream, ref_stack, 3, warmup=1)
+            t_our = _event_ms(torch, stream, run.layers, 3, warmup=1)
+            same_stack = bool(torch.equal(ref_stack(), run.layers()))
+            res["stack30"] = {"rows": rows, "ref_ms": t_ref, "ours_ms": t_our, "speedup": t_ref / t_our,
+                              "ref_tokens_per_s": rows / (t_ref * 1e-3), "same_bits": same_stack}
+    except Exception as exc:  # noqa: BLE001
+        res["error"] = f"{type(exc).__name__}: {exc}"
+    return res
+
+
+def layer_case(torch, ops, lib, dev, stream, tokens, steps) -> dict:
+    """One fvq_nvfp4_ffn call (layer 0 of the stack) over the first `tokens` rows of the
+    stack input, `steps` times: the launch sequence a profiler capture looks at."""
+    weights = StackWeights(torch, ops, dev, layers=1)
+    wl = STACK_WORKLOADS["c4" if tokens <= STACK_WORKLOADS["c4"]["total"] else "c5"]
+    run = StackRun(torch, lib, dev, stream, weights, dict(wl, total=tokens), 1, 0)
+    for _ in range(steps):
+        run.layers()
+    torch.cuda.synchronize(dev)
+    return {"tokens": tokens, "calls": steps}
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -667,175 +1153,142 @@ def main():
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    import flashvsr_optimizations_b200 as fvq
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     from flashvsr_optimizations_b200 import _lib, ops
-    from flashvsr_optimizations_b200.ffn_quantization import NVFP4FFN
     lib = _lib.load()
-    tokens = args.tokens
-    if args.case != "ffn":
-        stream = torch.cuda.current_stream(dev)
-        hbm = measured_peaks().get("hbm_gbs") or 6650.0
-        if args.case == "fp8_ffn":
-            peak8 = 2.0 * (measured_peaks().get("bf16_tflops_sustained") or 1400.0)
-            out = fp8_mode_timing(torch, ops, lib, dev, stream, tokens, peak8, steps=args.steps)
+    stream = torch.cuda.current_stream(dev)
+    peaks = measured_peaks()
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    if args.case != "stack":
+        if args.case == "layer":
+            out = layer_case(torch, ops, lib, dev, stream, args.tokens, args.steps)
+        elif args.case == "fp8_ffn":
+            peak8 = 2.0 * (peaks.get("bf16_tflops_sustained") or 1400.0)
+            out = fp8_mode_timing(torch, ops, lib, dev, stream, args.tokens, peak8, steps=args.steps)
         elif args.case == "dit_block":
-            out = dit_block_timing(torch, lib, dev, stream, make_sets(torch, ops, dev, tokens, rank)[:4],
-                                   tokens, hbm, steps=args.steps)
+            out = dit_block_timing(torch, lib, dev, stream, make_sets(torch, ops, dev, args.tokens, rank)[:4],
+                                   args.tokens, hbm, steps=args.steps)
         else:
             out = pil_resize_timing(torch, dev, stream, hbm, iters=args.steps)
         if rank == 0:
             print(json.dumps({"case": args.case, **out}), flush=True)
-        return
-    sets = make_sets(torch, ops, dev, tokens, rank)
-    ws_bytes = lib.fvq_nvfp4_ffn_workspace_bytes(tokens, D_MODEL, D_FF)
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
-    ys = [torch.empty(tokens, D_MODEL, dtype=torch.bfloat16, device=dev) for _ in range(ROTATE)]
-    stream = torch.cuda.current_stream(dev)
-    sptr = stream.cuda_stream
-    # pre-bound C-ABI calls (fvq_nvfp4_ffn), one per rotating set
-    structs = []
-    for x, ((q1, s1, g1, b1), (q2, s2, g2, b2)) in sets:
-        l1 = _lib.FvqLinear(q1.data_ptr(), s1.data_ptr(), g1.data_ptr(), b1.data_ptr(), D_MODEL, D_FF)
-        l2 = _lib.FvqLinear(q2.data_ptr(), s2.data_ptr(), g2.data_ptr(), b2.data_ptr(), D_FF, D_MODEL)
-        structs.append((x, l1, l2))
-    ffn_call = lib.fvq_nvfp4_ffn
-
-    def step(i):
-        x, l1, l2 = structs[i % ROTATE]
-        rc = ffn_call(x.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2), ys[i % ROTATE].data_ptr(),
-                      ws.data_ptr(), ws_bytes, sptr)
-        if rc != 0:
-            raise RuntimeError(lib.fvq_last_error().decode())
-
-    def barrier_sync():
-        torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
-        torch.cuda.synchronize(dev)
+            dist.destroy_process_group()
+        return
 
-    for i in range(max(3, args.warmup)):
-        step(i)
-    barrier_sync()
+    wl = STACK_WORKLOADS[args.workload]
+    extras_here = not args.no_extras
+    weights = StackWeights(torch, ops, dev, keep_bf16=extras_here and world == 1)
+    run = StackRun(torch, lib, dev, stream, weights, wl, world, rank)
+
+    # ---- the timed steps: 30 layers on this rank's rows + the all-gather
     gpu_uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     sampler = clock_sampler(gpu_uuid)
-    sampler.start()
-    if isinstance(sampler, ClockSampler):
-        time.sleep(0.15)  # nvidia-smi's start-up
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier_sync()
-    start.record(stream)
-    for i in range(args.steps):
-        step(i)
-    end.record(stream)
-    barrier_sync()
+    ms = timed_steps(torch, dist, dev, stream, world, lambda i: run.step(), args.steps, args.warmup,
+                     sampler=sampler)
     clocks = sampler.stop()
-    ms = start.elapsed_time(end)
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    total_tokens = tokens * args.steps * world
-    value = total_tokens / (ms * 1e-3)
-    tflops = value * FLOP_PER_TOKEN / 1e12
+    total = wl["total"]
+    value = total * args.steps / (ms * 1e-3)
+    flop_per_step = total * LAYERS * FLOP_PER_TOKEN
+    tflops = flop_per_step * args.steps / (ms * 1e-3) / 1e12
 
-    # ---- per-kernel timing (the library's events around fvq_nvfp4_ffn's launches)
-    kt = kernel_timing(lib, structs, ys, ws, ws_bytes, tokens, sptr, min(args.steps, 400))
-    if world > 1:
-        t = torch.tensor([kt["gemm_ms"], kt["quant_h_ms"]], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        kt["gemm_ms"], kt["quant_h_ms"] = (float(v) for v in t.tolist())
-
-    # ---- end to end through the public module API with host buffers
-    e2e = e2e_timing(torch, dist, fvq, NVFP4FFN, sets, tokens, dev, stream, world,
-                     min(args.steps, 500), args.warmup)
-
-    # ---- output gather (NCCL all-gather over NVLink) of one layer's output
-    gather = None
-    if world > 1:
-        from flashvsr_optimizations_b200.sharding import gather_rows
-        total = tokens * world
-        for _ in range(3):
-            gather_rows(ys[0], total)
-        barrier_sync()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        for _ in range(20):
-            gather_rows(ys[0], total)
-        e.record(stream)
-        barrier_sync()
-        gms = s.elapsed_time(e) / 20
-        t = torch.tensor([gms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        gms = float(t.item())
-        gather = {"ms": gms, "bytes": total * D_MODEL * 2,
-                  "busbw_GBps": (world - 1) * tokens * D_MODEL * 2 / (gms * 1e-3) / 1e9,
-                  "api": "sharding.gather_rows (NCCL all_gather_into_tensor)"}
-
-    peaks = measured_peaks()
-    fp4_cublas = fp4_library_peak(torch, dev) if rank == 0 else None
-    # the GEMMs are timed inside long runs of layers, where the 1000 W cap holds the SM
-    # clock well below its maximum: the sustained bf16 figure is the matching denominator
-    bf16_sustained = peaks.get("bf16_tflops_sustained")
-    if bf16_sustained:
-        peak = 4.0 * bf16_sustained
-        peak_src = ("4 x measured cuBLAS bf16 sustained (MEASURED_PEAKS.json, power-capped); "
-                    "dense FP4 runs at 4x bf16 on B200")
+    # ---- per-launch device times (a second pass over the same steps' layers)
+    kt = stack_kernel_timing(torch, dist, dev, world, run, passes=max(1, min(args.steps, 5)))
+    burst = peaks.get("bf16_tflops")
+    sustained = peaks.get("bf16_tflops_sustained")
+    if burst:
+        peak, peak_src = 4.0 * burst, ("4 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json); dense "
+                                       "FP4 runs at 4x bf16 on B200; the GEMMs are timed per launch")
     else:
-        peak, peak_src = 4.0 * 1400.0, "4 x fallback sustained bf16 1.4 PFLOP/s"
-    hbm = peaks.get("hbm_gbs") or 6650.0
-    gemm_flop = tokens * FLOP_PER_TOKEN
+        peak, peak_src = 4.0 * 1590.0, "4 x fallback bf16 burst 1.59 PFLOP/s"
+    peak_sus = 4.0 * (sustained or 1400.0)
+    gemm_flop = run.rows * FLOP_PER_TOKEN
     achieved = gemm_flop / (kt["gemm_ms"] * 1e-3) / 1e12
     traffic = None
-    tp = ROOT / "profiles" / "nvfp4_gemm_ffn_layer_7680tok_traffic.json"
+    tp = ROOT / "profiles" / f"nvfp4_gemm_pair_{run.rows}tok_traffic.json"
     if tp.exists():
         try:
             traffic = json.loads(tp.read_text()).get("dram_bytes_per_gemm_pair")
         except ValueError:
             traffic = None
-    extras = {}
-    if not args.no_extras:
-        stack = stack_timing(torch, dist, ops, lib, dev, stream, world, rank)
-        stack["tflops_frac_of_fp4_peak"] = stack["tflops"] / (peak * world)  # whole job / N GPUs
-        extras["stack_30_layers"] = stack
-        if rank == 0:
-            extras["quantize_sweep"] = quantize_sweep(torch, lib, dev, stream, hbm)
-            fp8_peak = 2.0 * (bf16_sustained or 1400.0)
-            extras["fp8_mode"] = fp8_mode_timing(torch, ops, lib, dev, stream, tokens, fp8_peak)
-            extras["pil_resize"] = pil_resize_timing(torch, dev, stream, hbm)
-            extras["dit_block"] = dit_block_timing(torch, lib, dev, stream, sets, tokens, hbm)
+
+    # ---- end to end through the public module API with host buffers
+    e2e = stack_e2e(torch, dist, weights, run, dev, world, rank, args.steps, args.warmup)
+
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4(e2m1+e4m3 scales), fp32 accumulate, bf16 io",
-        "data": "synthetic (seeded Student-t(4)x0.5 activations, N(0,0.02) weights, N(0,0.01) bias)",
-        "config": {"workload": WORKLOAD, "tokens_per_gpu": tokens, "d_model": D_MODEL, "d_ff": D_FF,
-                   "layers": 1, "parallelism": f"token-row shards x{world}, replicated weights",
-                   "l2": f"inputs rotate over {ROTATE} distinct activation/weight sets (312 MB > 126 MB L2)"},
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "nvfp4 (e2m1 codes, e4m3 1x16 scales, fp32 global scales), fp32 accumulate, bf16 io",
+        "data": f"synthetic: {wl['input']}; layer weights N(0,0.02), biases N(0,0.01), seeded",
+        "config": {"workload": wl["name"], "tokens": total, "layers": LAYERS, "d_model": D_MODEL,
+                   "d_ff": D_FF, "rows_per_gpu": run.rows,
+                   "parallelism": f"token-row shards x{world}, replicated weights, NCCL all-gather "
+                                  f"of the output inside the step",
+                   "l2": "inputs larger than L2: 464 MB of weights per step, each layer's "
+                         f"{run.rows * D_FF * 2 / 1e6:.0f} MB intermediate"},
         "tflops": tflops, "tflops_frac_of_fp4_peak": tflops / (peak * world),
-        "gpu_launches": LAUNCHES_PER_LAYER * args.steps,
-        "roofline": {"bound": "tensor", "kernel": "nvfp4_gemm_kernel (GEMM1 + GEMM2 of the layer)",
-                     "achieved": achieved, "peak": peak, "peak_source": peak_src, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": traffic,
+        "gpu_launches": LAUNCHES_PER_LAYER * LAYERS * args.steps,
+        "roofline": {"bound": "tensor",
+                     "kernel": "the layer's two NVFP4 GEMM launches (tcgen05 mxf4nvf4)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_source": peak_src,
+                     "frac_of_sustained": achieved / peak_sus,
                      "algorithmic_flop_per_launch_pair": gemm_flop},
-        "quantize": {"kernel": "quantize_kernel on the 7680x8960 intermediate",
-                     "GBps": kt["quant_h_gbs"], "peak_GBps": hbm, "frac": kt["quant_h_gbs"] / hbm,
+        "quantize": {"kernel": f"quantize_kernel on the {run.rows}x{D_FF} intermediate",
+                     "GBps": kt["quant_h_GBps"], "peak_GBps": hbm, "frac": kt["quant_h_GBps"] / hbm,
                      "ms": kt["quant_h_ms"]},
         "kernels_ms": kt,
         "e2e": e2e,
         "clocks": clocks,
     }
-    if gather:
-        result["gather"] = gather
-    result.update(extras)
-    if fp4_cublas:
-        result["fp4_cublas_8192_tflops"] = fp4_cublas
-    if rank == 0 and not args.no_extras:
-        lib_sustained = fp4_library_sustained(torch, dev)
-        if lib_sustained:
-            result["fp4_cublas_sustained_layer_shapes"] = lib_sustained
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_ffn_tokens_per_s(5, 1, args.cpu_seconds)
+        result["cpu_baseline"] = cpu_stack_tokens_per_s(3, 1, args.cpu_seconds, wl)
+
+    tail = {}
+    if extras_here:
+        result["single_layer"] = single_layer_timing(torch, dist, ops, lib, dev, stream, world, rank,
+                                                     args.tokens, 200)
+        if args.workload == "c4":
+            wl5 = STACK_WORKLOADS["c5"]
+            run5 = StackRun(torch, lib, dev, stream, weights, wl5, world, rank)
+            ms5 = timed_steps(torch, dist, dev, stream, world, lambda i: run5.step(), 3, 1)
+            v5 = wl5["total"] * 3 / (ms5 * 1e-3)
+            tail["c5_stack"] = {"workload": wl5["name"], "tokens": wl5["total"], "rows_per_gpu": run5.rows,
+                                "ms_per_stack": ms5 / 3, "tokens_per_s": v5,
+                                "tflops": v5 * LAYERS * FLOP_PER_TOKEN / 1e12,
+                                "tflops_frac_of_fp4_peak": v5 * LAYERS * FLOP_PER_TOKEN / 1e12 / (peak * world)}
+            del run5
+            torch.cuda.empty_cache()
+        fr = fused_requant_timing(torch, dist, dev, stream, world, weights, run, wl, rank)
+        fr["speedup_vs_exact"] = (ms / args.steps) / fr["ms_per_stack"]
+        tail["fused_requant"] = fr
+        if world > 1 and args.workload == "c4":
+            tail["stack_check"] = stack_check(torch, dist, dev, weights, run, wl, world, rank)
+        if world == 1:
+            result["quantize_sweep"] = quantize_sweep(torch, lib, dev, stream, hbm)
+            fp8_peak = 2.0 * (sustained or 1400.0)
+            result["fp8_mode"] = fp8_mode_timing(torch, ops, lib, dev, stream, args.tokens, fp8_peak)
+            result["pil_resize"] = pil_resize_timing(torch, dev, stream, hbm)
+            result["dit_block"] = dit_block_timing(torch, lib, dev, stream,
+                                                   make_sets(torch, ops, dev, args.tokens, rank)[:4],
+                                                   args.tokens, hbm)
+            lib_sus = fp4_library_sustained(torch, dev)
+            if lib_sus:
+                result["fp4_cublas_sustained_layer_shapes"] = lib_sus
+            fp4_cublas = fp4_library_peak(torch, dev)
+            if fp4_cublas:
+                result["fp4_cublas_8192_tflops"] = fp4_cublas
+            tail["flashinfer"] = flashinfer_comparison(torch, ops, lib, dev, stream, weights, run)
+    if world > 1:
+        tail["gather"] = gather_timing(torch, dist, dev, stream, world, run)
+    result.update(tail)
+    # the figures that matter most for scaling last, where a truncated log keeps them
+    result["summary"] = {"n_gpus": world, "ms_per_step": ms / args.steps, "tokens_per_s": value,
+                         "e2e_tokens_per_s": e2e["value"], "gemm_frac_of_burst": achieved / peak,
+                         **({"gather_ms": tail["gather"]["ms"],
+                             "gather_busbw_GBps": tail["gather"]["busbw_GBps"]} if "gather" in tail else {})}
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
@@ -843,115 +1296,20 @@ def main():
         dist.destroy_process_group()
 
 
-def kernel_timing(lib, structs, ys, ws, ws_bytes, tokens, sptr, steps) -> dict:
-    """Device time of each of fvq_nvfp4_ffn's four launches, from the library's own
-    CUDA events (fvq_nvfp4_ffn_profile runs the same launch sequence and synchronises
-    after each layer, so every launch here starts on an idle GPU)."""
-    ms = (ctypes.c_float * 4)()
-    acc = [[] for _ in range(4)]
-
-    def one(i):
-        x, l1, l2 = structs[i % ROTATE]
-        rc = lib.fvq_nvfp4_ffn_profile(x.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2),
-                                       ys[i % ROTATE].data_ptr(), ws.data_ptr(), ws_bytes, sptr, ms)
-        if rc != 0:
-            raise RuntimeError(lib.fvq_last_error().decode())
-
-    for i in range(5):
-        one(i)
-    for i in range(steps):
-        one(i)
-        for j in range(4):
-            acc[j].append(ms[j])
-    qx, g1t, qh, g2t = (sum(v) / len(v) for v in acc)
-    d, f = D_MODEL, D_FF
-    qh_bytes = tokens * f * 2 + tokens * f // 2 + (tokens + 127) // 128 * 128 * f // 16
-    return {"quant_x_ms": qx, "gemm1_ms": g1t, "quant_h_ms": qh, "gemm2_ms": g2t,
-            "gemm_ms": g1t + g2t, "quant_h_gbs": qh_bytes / (qh * 1e-3) / 1e9,
-            "gemm1_tflops": tokens * 2 * d * f / (g1t * 1e-3) / 1e12,
-            "gemm2_tflops": tokens * 2 * d * f / (g2t * 1e-3) / 1e12, "steps": steps,
-            "note": "quant_x also writes the replicated W2 scales when GEMM2 runs on one SM per tile (not with the default SM pairs); launches timed one layer at a time"}
-
-
-def e2e_timing(torch, dist, fvq, NVFP4FFN, sets, tokens, dev, stream, world, steps, warmup) -> dict:
-    """Same metric through the public module (NVFP4FFN) with pinned host input/output.
-
-    Every step copies its input host->device, runs the module and copies the result
-    device->host, all inside the timed region.  The copies run on their own streams,
-    so step i+1's upload and step i-1's download overlap step i's compute (PCIe is
-    full duplex); device inputs are double-buffered and ordered with events.
-    """
-    from flashvsr_optimizations_b200.ffn_quantization import QuantLinear
-    mods = []
-    for x, ((q1, s1, g1, b1), (q2, s2, g2, b2)) in sets:
-        l1 = QuantLinear.from_quantized(q1, s1, g1, b1, D_MODEL)
-        l2 = QuantLinear.from_quantized(q2, s2, g2, b2, D_FF)
-        mods.append(NVFP4FFN(l1, torch.nn.GELU(approximate="tanh"), l2))
-    xh = [x.cpu().pin_memory() for x, _ in sets]
-    yh = [torch.empty(tokens, D_MODEL, dtype=torch.bfloat16).pin_memory() for _ in range(ROTATE)]
-    xd = [torch.empty(tokens, D_MODEL, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    s_up, s_cmp, s_down = (torch.cuda.Stream(dev) for _ in range(3))
-    done_cmp = [torch.cuda.Event() for _ in range(2)]   # compute that read xd[b] finished
-    for ev in done_cmp:
-        ev.record(s_cmp)
-
-    def step(i):
-        j, b = i % ROTATE, i % 2
-        up = torch.cuda.Event()
-        with torch.cuda.stream(s_up):
-            s_up.wait_event(done_cmp[b])
-            xd[b].copy_(xh[j], non_blocking=True)
-            up.record(s_up)
-        with torch.cuda.stream(s_cmp):
-            s_cmp.wait_event(up)
-            y = mods[j](xd[b])
-            done_cmp[b].record(s_cmp)
-        with torch.cuda.stream(s_down):
-            s_down.wait_event(done_cmp[b])
-            yh[j].copy_(y, non_blocking=True)
-            y.record_stream(s_down)
-
-    with torch.no_grad():
-        for i in range(max(3, warmup)):
-            step(i)
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(s_up)
-        for st in (s_cmp, s_down):
-            st.wait_event(s)
-        for i in range(steps):
-            step(i)
-        for st in (s_up, s_cmp):
-            ev = torch.cuda.Event()
-            ev.record(st)
-            s_down.wait_event(ev)
-        e.record(s_down)
-        torch.cuda.synchronize(dev)
-    ms = s.elapsed_time(e)
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    return {"value": tokens * steps * world / (ms * 1e-3), "unit": "tokens/s",
-            "h2d_bytes_per_step": tokens * D_MODEL * 2, "d2h_bytes_per_step": tokens * D_MODEL * 2,
-            "steps": steps, "ms_per_step": ms / steps,
-            "api": "NVFP4FFN.forward (install_ffn's fused module) via torch custom op fvq::nvfp4_ffn; "
-                   "uploads, layers and downloads on three streams, overlapped across steps"}
-
-
 def run_reference(args, rank, world):
+    """The reference arm: the reference's NVFP4 FFN arithmetic restated on the host CPU (the
+    reference's own path runs only on a GPU), rank 0 only, on bounded samples."""
     if rank != 0:
         return
-    res = cpu_ffn_tokens_per_s(args.steps, args.warmup, seconds=60.0)
-    ms_per_step = res["seconds"] / args.steps * 1e3
+    wl = STACK_WORKLOADS[args.workload]
+    res = cpu_stack_tokens_per_s(args.steps, args.warmup, seconds=60.0, wl=wl)
+    ms_per_step = res["seconds"] / args.steps * LAYERS * 1e3
     line = {"metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "nvfp4 emulated (fp32 dequantized matmul)", "data": "synthetic (seeded)",
-            "config": {"workload": WORKLOAD, "tokens_per_step": res["rows_per_step"],
-                       "d_model": D_MODEL, "d_ff": D_FF, "layers": 1, "parallelism": "host CPU"},
+            "config": {"workload": wl["name"], "tokens_per_step": res["rows_per_step"],
+                       "layers": LAYERS, "d_model": D_MODEL, "d_ff": D_FF, "parallelism": "host CPU"},
             "impl": "reference",
             "cpu_baseline": {"value": res["value"], "unit": "tokens/s", "cores": res["cores"],
                              "kind": res["kind"], "sample": res["sample"]},

@@ -86,6 +86,12 @@ SIGNATURES = {
     "fvq_nvfp4_ffn_profile": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear),
                                          _c.POINTER(FvqLinear), _vp, _vp, _sz, _vp,
                                          _c.POINTER(_c.c_float)]),
+    "fvq_nvfp4_ffn_fused_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "fvq_nvfp4_ffn_fused": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _c.POINTER(FvqLinear),
+                                       _vp, _vp, _c.c_int, _vp, _vp, _vp, _sz, _vp]),
+    "fvq_nvfp4_ffn_fused_profile": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear),
+                                               _c.POINTER(FvqLinear), _vp, _vp, _c.c_int, _vp,
+                                               _vp, _vp, _sz, _vp, _c.POINTER(_c.c_float)]),
     "fvq_fp8_row_quantize": (_c.c_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "fvq_fp8_tensor_quantize_workspace_bytes": (_sz, []),
     "fvq_fp8_tensor_quantize": (_c.c_int, [_vp, _i64, _vp, _vp, _vp, _sz, _vp]),

@@ -3,6 +3,7 @@
 // sequences of QuantLinear.forward and the FFN.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -14,7 +15,10 @@
 namespace {
 
 thread_local std::string g_last_error;
-uint64_t g_wait_limit = fvq::kDefaultWaitLimit;
+// Process-wide bound on device waits (fvq_set_wait_limit); read by every launch path from
+// any host thread, hence atomic.
+std::atomic<uint64_t> g_wait_limit_ns{fvq::kDefaultWaitLimit};
+uint64_t wait_limit() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -102,7 +106,7 @@ int gemm_impl(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
               const uint16_t* residual = nullptr, const uint16_t* gate = nullptr) {
   const char* why = nullptr;
   cudaError_t e = fvq::launch_gemm(a_codes, a_sf, g_a, w_codes, w_sf, g_w, alpha, bias, out, m, n, k,
-                                   epilogue, amax_out, g_wait_limit, st, &why, w_sf_rep, residual,
+                                   epilogue, amax_out, wait_limit(), st, &why, w_sf_rep, residual,
                                    gate);
   if (e != cudaSuccess) {
     if (why) return fail(FVQ_ECUDA, "fvq_nvfp4_gemm: %s", why);
@@ -183,7 +187,7 @@ int fvq_nvfp4_quantize_dynamic(const uint16_t* x, int64_t rows, int64_t k, const
     // amax, global scale and quantization in one launch
     uint32_t* ws = static_cast<uint32_t*>(workspace);
     cudaError_t e = fvq::launch_amax_quantize(x, rows, k, g_out, codes, sf, ws, nullptr, nullptr, 0,
-                                              0, nullptr, g_wait_limit, fvq::error_word_ptr(), st);
+                                              0, nullptr, wait_limit(), fvq::error_word_ptr(), st);
     if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_quantize_dynamic launch");
     return FVQ_OK;
   }
@@ -304,7 +308,7 @@ int fvq_nvfp4_linear(const uint16_t* x, int64_t rows, const fvq_linear* lin, uin
   uint8_t* codes = c.take(static_cast<size_t>(rows * k / 2));
   uint8_t* sf = c.take(fvq::sf_bytes(rows, k));
   cudaError_t e = fvq::launch_amax_quantize(x, rows, k, &scalars[0], codes, sf, amax_ws, nullptr,
-                                            nullptr, 0, 0, nullptr, g_wait_limit,
+                                            nullptr, 0, 0, nullptr, wait_limit(),
                                             fvq::error_word_ptr(), st);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_linear quantize launch");
   return gemm_impl(codes, sf, &scalars[0], lin->qweight, lin->scale, lin->global_sf, nullptr,
@@ -384,10 +388,10 @@ int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_
   cudaError_t e =
       ln == nullptr
           ? fvq::launch_amax_quantize(x, rows, d, g_x, codes_x, sf_x, amax_ws, amax_h, lin2->scale,
-                                      d, f, sf_w2_rep, g_wait_limit, fvq::error_word_ptr(), st)
+                                      d, f, sf_w2_rep, wait_limit(), fvq::error_word_ptr(), st)
           : fvq::launch_amax_quantize_ln(x, rows, d, ln->shift, ln->scale, ln->eps, ln->stats, g_x,
                                          codes_x, sf_x, amax_ws, amax_h, lin2->scale, d, f,
-                                         sf_w2_rep, g_wait_limit, fvq::error_word_ptr(), st);
+                                         sf_w2_rep, wait_limit(), fvq::error_word_ptr(), st);
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(x) launch");
   mark(1);
   // 2. h = bf16(gelu(bf16(bf16(alpha1 * acc) + b1))), amax_h = max |h|
@@ -416,6 +420,134 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
                   uint16_t* y, void* workspace, size_t workspace_bytes, void* stream) {
   return ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes,
                   static_cast<cudaStream_t>(stream), nullptr);
+}
+
+size_t fvq_nvfp4_ffn_fused_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff) {
+  if (rows <= 0 || d_model <= 0 || d_ff <= 0) return 0;
+  Carve c(nullptr);
+  c.take(fvq::kAmaxWorkspaceBytes);
+  c.take(kScalarBytes);
+  c.take(static_cast<size_t>(rows * d_model / 2));
+  c.take(fvq::sf_bytes(rows, d_model));
+  c.take(static_cast<size_t>(rows * d_ff / 2));
+  c.take(fvq::sf_bytes(rows, d_ff));
+  c.take(static_cast<size_t>(4 * d_model * (d_ff / 16)));  // W2 scales, replicated
+  return c.off;
+}
+
+namespace {
+
+// The FFN with the intermediate quantized inside GEMM1's epilogue (three launches):
+// amax + quantize of x (which also zeroes the amax word GEMM1 maxes into) -> GEMM1 with
+// bias, GELU, amax and NVFP4 quantization of h with g = 2688 / max(*amax_hint, 1e-12)
+// -> GEMM2 with alpha = 1 / (g * g_w2).  ev: NULL or 4 events (profile).
+int ffn_fused_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
+                   uint16_t* y, const float* amax_hint, int headroom_log2, float* amax_seen,
+                   uint32_t* flags, void* workspace, size_t workspace_bytes, cudaStream_t st,
+                   cudaEvent_t* ev) {
+  if (int rc = check_linear(lin1, "fvq_nvfp4_ffn_fused (linear 1)")) return rc;
+  if (int rc = check_linear(lin2, "fvq_nvfp4_ffn_fused (linear 2)")) return rc;
+  if (lin1->out_features != lin2->in_features || lin2->out_features != lin1->in_features)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_fused: linear shapes do not chain");
+  if (int rc = check_quant_shape(rows, lin1->in_features, "fvq_nvfp4_ffn_fused")) return rc;
+  if (!x || !y || !workspace || !amax_hint)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_fused: NULL pointer");
+  if (headroom_log2 < 0 || headroom_log2 > 30)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_fused: headroom_log2 must be in [0, 30] (got %d)",
+                headroom_log2);
+  if (amax_seen != nullptr && amax_seen == amax_hint)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_fused: amax_seen must not alias amax_hint "
+                "(the call zeroes amax_seen before it reads the hint)");
+  const int64_t d = lin1->in_features, f = lin1->out_features;
+  const size_t need = fvq_nvfp4_ffn_fused_workspace_bytes(rows, d, f);
+  if (workspace_bytes < need)
+    return fail(FVQ_EWORKSPACE, "fvq_nvfp4_ffn_fused: workspace needs %zu bytes, got %zu", need,
+                workspace_bytes);
+  if (!aligned32(x) || !aligned16(y) || !aligned16(workspace))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_ffn_fused: x must be 32-byte aligned, y and workspace 16-byte");
+  if (int rc = check_device()) return rc;
+  Carve c(workspace);
+  uint32_t* amax_ws = reinterpret_cast<uint32_t*>(c.take(fvq::kAmaxWorkspaceBytes));
+  float* scalars = reinterpret_cast<float*>(c.take(kScalarBytes));
+  uint8_t* codes_x = c.take(static_cast<size_t>(rows * d / 2));
+  uint8_t* sf_x = c.take(fvq::sf_bytes(rows, d));
+  uint8_t* codes_h = c.take(static_cast<size_t>(rows * f / 2));
+  uint8_t* sf_h = c.take(fvq::sf_bytes(rows, f));
+  uint8_t* sf_w2_rep = c.take(static_cast<size_t>(4 * d * (f / 16)));
+  if (fvq::gemm_pairs_raw_scales(rows)) sf_w2_rep = nullptr;
+  float* g_x = &scalars[0];
+  float* g_h = &scalars[1];
+  float* amax_h = amax_seen != nullptr ? amax_seen : &scalars[2];
+  auto mark = [&](int i) {
+    if (ev != nullptr) cudaEventRecord(ev[i], st);
+  };
+  mark(0);
+  cudaError_t e = fvq::launch_amax_quantize(x, rows, d, g_x, codes_x, sf_x, amax_ws, amax_h,
+                                            lin2->scale, d, f, sf_w2_rep, wait_limit(),
+                                            fvq::error_word_ptr(), st);
+  if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn_fused quantize(x) launch");
+  mark(1);
+  fvq::QuantOut qo;
+  qo.codes = codes_h;
+  qo.sf = sf_h;
+  qo.amax_hint = amax_hint;
+  qo.headroom_log2 = headroom_log2;
+  qo.g_used = g_h;
+  qo.flags = flags;
+  const char* why = nullptr;
+  e = fvq::launch_gemm(codes_x, sf_x, g_x, lin1->qweight, lin1->scale, lin1->global_sf, nullptr,
+                       lin1->bias, nullptr, rows, f, d, 3, amax_h, wait_limit(), st, &why, nullptr,
+                       nullptr, nullptr, &qo);
+  if (e != cudaSuccess) {
+    if (why) return fail(FVQ_ECUDA, "fvq_nvfp4_ffn_fused GEMM1: %s", why);
+    return cuda_fail(e, "fvq_nvfp4_ffn_fused GEMM1 launch");
+  }
+  mark(2);
+  if (int rc = gemm_impl(codes_h, sf_h, g_h, lin2->qweight, lin2->scale, lin2->global_sf, nullptr,
+                         lin2->bias, y, rows, d, f, FVQ_EPI_BF16, nullptr, st, sf_w2_rep))
+    return rc;
+  mark(3);
+  return FVQ_OK;
+}
+
+}  // namespace
+
+int fvq_nvfp4_ffn_fused(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                        const fvq_linear* lin2, uint16_t* y, const float* amax_hint,
+                        int headroom_log2, float* amax_seen, uint32_t* flags, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  return ffn_fused_impl(x, rows, lin1, lin2, y, amax_hint, headroom_log2, amax_seen, flags,
+                        workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int fvq_nvfp4_ffn_fused_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                                const fvq_linear* lin2, uint16_t* y, const float* amax_hint,
+                                int headroom_log2, float* amax_seen, uint32_t* flags, void* workspace,
+                                size_t workspace_bytes, void* stream, float* kernel_ms) {
+  if (kernel_ms == nullptr)
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_fused_profile: kernel_ms is NULL");
+  if (int rc = check_device()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaEvent_t ev[4];
+  int made = 0;
+  for (; made < 4; ++made) {
+    if (cudaEventCreate(&ev[made]) != cudaSuccess) break;
+  }
+  int rc = FVQ_OK;
+  if (made < 4) {
+    rc = fail(FVQ_ECUDA, "fvq_nvfp4_ffn_fused_profile: cudaEventCreate failed");
+  } else {
+    rc = ffn_fused_impl(x, rows, lin1, lin2, y, amax_hint, headroom_log2, amax_seen, flags,
+                        workspace, workspace_bytes, st, ev);
+    if (rc == FVQ_OK) {
+      cudaError_t e = cudaEventSynchronize(ev[3]);
+      for (int i = 0; e == cudaSuccess && i < 3; ++i)
+        e = cudaEventElapsedTime(&kernel_ms[i], ev[i], ev[i + 1]);
+      if (e != cudaSuccess) rc = cuda_fail(e, "fvq_nvfp4_ffn_fused_profile timing");
+    }
+  }
+  for (int i = 0; i < made; ++i) cudaEventDestroy(ev[i]);
+  return rc;
 }
 
 int fvq_ln_modulate(const uint16_t* x, int64_t rows, int64_t d, const uint16_t* shift,
@@ -578,7 +710,7 @@ int fp8_gemm_impl(const uint8_t* a, const float* sa, const uint8_t* w, const flo
                   int epilogue, uint32_t* row_amax, cudaStream_t st) {
   const char* why = nullptr;
   cudaError_t e = fvq::launch_fp8_gemm(a, sa, w, sw, bias, out, m, n, k, epilogue, row_amax,
-                                       g_wait_limit, st, &why);
+                                       wait_limit(), st, &why);
   if (e != cudaSuccess) {
     if (why) return fail(FVQ_ECUDA, "fp8 GEMM: %s", why);
     return cuda_fail(e, "fp8 GEMM launch");
@@ -845,7 +977,8 @@ int fvq_set_fp8_gemm_pairing(int mode) {
 }
 
 int fvq_set_wait_limit(uint64_t nanoseconds) {
-  g_wait_limit = nanoseconds == 0 ? fvq::kDefaultWaitLimit : nanoseconds;
+  g_wait_limit_ns.store(nanoseconds == 0 ? fvq::kDefaultWaitLimit : nanoseconds,
+                        std::memory_order_relaxed);
   return FVQ_OK;
 }
 

@@ -72,19 +72,30 @@ constexpr int kWarpStagingBytes = 32 * kStageRowBytes;
 // kRepSfb: stages carry the W scales already replicated four times (16 KB per
 // K tile), moved to TMEM with four 128x256b copies instead of eight
 // 32x128b.warpx4 copies.
+// kEpi 3 (GEMM1 quantizing its own output) writes NVFP4 codes and scales straight
+// from registers: it needs no staging buffer, so four stages fit, and in resident mode
+// the W scales are preloaded through the last stage's buffer (kPreloadInStage: the
+// producer fills that stage only after the MMA warp's copies out of it completed).
 template <int kEpi, bool kResident, bool kRepSfb = false>
 struct Plan {
   static constexpr int kStageBytes =
       kABytes + kBBytes + kSfaBytes + (kResident ? 0 : (kRepSfb ? kSfbRepBytes : kSfbBytes));
-  static constexpr int kStages = kEpi != 1 ? (kRepSfb ? 3 : 4) : (kResident ? 3 : 2);
+  static constexpr int kStages =
+      kEpi == 3 ? 4 : (kEpi != 1 ? (kRepSfb ? 3 : 4) : (kResident ? 3 : 2));
   static constexpr bool kStaged = kEpi == 1;
+  static constexpr bool kGelu = kEpi == 1 || kEpi == 3;
+  static constexpr bool kPreloadInStage = kResident && !kStaged;
   static constexpr int kStagingOff = kStages * kStageBytes;
   static constexpr int kTableOff = kStagingOff + (kStaged ? kStagingBytes : 0);
-  static constexpr int kBarrierOff = kTableOff + (kEpi == 1 ? kGeluTabBytes : 0);
+  static constexpr int kBarrierOff = kTableOff + (kGelu ? kGeluTabBytes : 0);
   static constexpr int kSmemBytes = kBarrierOff + kBarrierBytes;
 };
 static_assert(Plan<1, true>::kSmemBytes <= 232448, "GEMM1 resident plan exceeds shared memory");
 static_assert(Plan<1, false>::kSmemBytes <= 232448, "GEMM1 streaming plan exceeds shared memory");
+static_assert(Plan<3, true>::kSmemBytes <= 232448, "quantizing GEMM1 plan exceeds shared memory");
+static_assert(Plan<3, false>::kSmemBytes <= 232448, "quantizing GEMM1 plan exceeds shared memory");
+static_assert(2 * (kMaxResidentKSteps * 512) <= Plan<3, true>::kStageBytes,
+              "resident W scales must fit one stage buffer");
 static_assert(Plan<0, false>::kSmemBytes <= 232448, "GEMM2 plan exceeds shared memory");
 static_assert(Plan<0, false, true>::kSmemBytes <= 232448, "GEMM2 replicated plan exceeds shared memory");
 
@@ -104,6 +115,7 @@ struct Barriers {
   uint64_t acc_empty;
   uint64_t teardown;
   uint64_t sfb_full;
+  uint64_t sfb_free;   // the resident W scales' copies to TMEM completed (kPreloadInStage)
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -162,14 +174,26 @@ __device__ __forceinline__ void gelu_table_init(uint16_t* tab, int tid, int nthr
   }
 }
 
+// bf16(gelu(x)) for |x| < 2^-12 (zeros and subnormals included).  There the fp32
+// formula is 0.5x * (1 + t) with |t| = |tanh(sqrt(2/pi)(x + 0.044715x^3))| < 2^-12: for
+// a normal x, 0.5x is a bf16 value and the factor (1 + t) moves it by far less than
+// half a bf16 ulp, so the result rounds back to 0.5x; for a subnormal x, t is so small
+// that 1 + t == 1 in fp32.  Either way the result is bf16_rn(0.5x) (0.5x exact in
+// fp32, then one rounding).  The GPU test compares every bf16 input with torch.
+__device__ __forceinline__ uint32_t gelu_bf16_tiny(uint32_t x_bits) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn(__uint_as_float(x_bits << 16), 0.5f)));
+}
+
 // bf16(gelu(x)) for a bf16 input, bit-identical to the exact formula.  For
 // 8 <= |x| (finite, and +inf) the fp32 tanh saturates to +-1, so the formula
-// gives x itself for positive x and -0 for negative x.
+// gives x itself for positive x and -0 for negative x; below 2^-12 see
+// gelu_bf16_tiny; only -inf and NaN evaluate the formula.
 __device__ __forceinline__ uint32_t gelu_bf16(uint32_t x_bits, const uint16_t* tab) {
   const uint32_t mag = x_bits & 0x7FFFu;
   const uint32_t off = mag - kGeluTabLo;
   if (off < kGeluTabSpan) return tab[off | ((x_bits & 0x8000u) >> 4)];
-  if (mag >= 0x4100u && mag < 0x7F80u) return (x_bits & 0x8000u) ? 0x8000u : x_bits;
+  if (mag < kGeluTabLo) return gelu_bf16_tiny(x_bits);
+  if (mag < 0x7F80u) return (x_bits & 0x8000u) ? 0x8000u : x_bits;
   if (x_bits == 0x7F80u) return x_bits;
   return gelu_bf16_exact(x_bits);
 }
@@ -312,7 +336,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                       const float* __restrict__ g_w, const float* __restrict__ alpha_in,
                       const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m, int n,
                       int k, float* amax_out, uint64_t wait_limit,
-                      const uint16_t* __restrict__ residual, const uint16_t* __restrict__ gate) {
+                      const uint16_t* __restrict__ residual, const uint16_t* __restrict__ gate,
+                      QuantOut qo) {
   using P = Plan<kEpi, kResident, kRepSfb>;
   constexpr int kStages = P::kStages;
   constexpr int kStageBytes = P::kStageBytes;
@@ -333,7 +358,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int num_k_tiles = k / BK;
   const int64_t sf_tile_stride = static_cast<int64_t>(k / 64) * 512;  // bytes per 128-row block
   const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
-  const TileSeq<kResident, kEpi != 1> seq(num_m_blocks, num_n_blocks);
+  const TileSeq<kResident, kEpi != 1 && kEpi != 3> seq(num_m_blocks, num_n_blocks);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -344,6 +369,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     mbar_init(&bars->acc_empty, kEpiWarps);
     mbar_init(&bars->teardown, 1);
     mbar_init(&bars->sfb_full, 1);
+    mbar_init(&bars->sfb_free, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -364,13 +390,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // (the whole warp runs the loop; one elected lane issues the copies)
     if (seq.count > 0) {
       bool sfb_armed = false;
+      uint8_t* preload = P::kPreloadInStage ? smem + (kStages - 1) * kStageBytes : staging;
       if (kResident) {
         // the W scales of this CTA's N block, all K: two contiguous 128-row runs
         if (elect_one()) {
           mbar_arrive_expect_tx(&bars->sfb_full, static_cast<uint32_t>(2 * sf_tile_stride));
-          bulk_load(staging, w_sf + (2 * seq.nb_fixed) * sf_tile_stride,
+          bulk_load(preload, w_sf + (2 * seq.nb_fixed) * sf_tile_stride,
                     static_cast<uint32_t>(sf_tile_stride), &bars->sfb_full);
-          bulk_load(staging + sf_tile_stride, w_sf + (2 * seq.nb_fixed + 1) * sf_tile_stride,
+          bulk_load(preload + sf_tile_stride, w_sf + (2 * seq.nb_fixed + 1) * sf_tile_stride,
                     static_cast<uint32_t>(sf_tile_stride), &bars->sfb_full);
         }
         __syncwarp();
@@ -381,10 +408,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (int s = 0; s < kStages; ++s) armed[s] = 0;
       int stage = 0;
       uint32_t phase = 0;
-      for (int i = 0; i < seq.count && !warp_aborted(bars); ++i) {
+      int issued = 0;  // K tiles loaded so far
+      bool failed = false;
+      for (int i = 0; i < seq.count && !failed && !warp_aborted(bars); ++i) {
         int mb, nb, half;
         seq.at(i, mb, nb, half);  // a half tile loads the whole W tile
-        for (int kt = 0; kt < num_k_tiles; ++kt) {
+        for (int kt = 0; kt < num_k_tiles; ++kt, ++issued) {
+          if (P::kPreloadInStage && issued == kStages - 1 &&
+              !warp_wait_bounded(&bars->sfb_free, 0, wait_limit)) {
+            // the resident W scales still occupy the last stage's buffer
+            warp_flag_error(bars, kErrWaitProducer);
+            failed = true;
+            break;
+          }
           if (!warp_wait_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
             warp_flag_error(bars, kErrWaitProducer);
             break;
@@ -444,14 +480,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           ok = false;
         } else {
           tc_fence_after();
+          const uint8_t* preload = P::kPreloadInStage ? smem + (kStages - 1) * kStageBytes : staging;
           if (elect_one()) {
             for (int s = 0; s < k / 64; ++s) {
               tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * s,
-                                 make_smem_desc(smem_u32(staging + 512 * s), 16, 128, 0));
+                                 make_smem_desc(smem_u32(preload + 512 * s), 16, 128, 0));
               tmem_cp_32x128b_x4(tmem + kSfbCol + 8 * s + 4,
-                                 make_smem_desc(smem_u32(staging + sf_tile_stride + 512 * s), 16,
+                                 make_smem_desc(smem_u32(preload + sf_tile_stride + 512 * s), 16,
                                                 128, 0));
             }
+            if (P::kPreloadInStage) tc_commit(&bars->sfb_free);  // the buffer may be refilled
           }
           __syncwarp();
           issued_any = true;
@@ -539,9 +577,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int quarter = (warp - 2) >> 2;
     const int col_base = quarter * 64;
     const int trow = quad * 32 + lane;
-    if constexpr (kEpi == 1) {
+    if constexpr (P::kGelu) {
       gelu_table_init(gelu_tab, threadIdx.x - 64, kEpiThreads);
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+    }
+    // kEpi 3: the intermediate's provisional encode scale and its loop invariants
+    float gq = 0.0f, r6 = 0.0f, rgq = 0.0f;
+    uint32_t qflags = 0;
+    if constexpr (kEpi == 3) {
+      // 2^-headroom_log2 as an exact power of two (headroom_log2 in [0, 30])
+      gq = __fmul_rn(encode_scale(*qo.amax_hint), __int_as_float((127 - qo.headroom_log2) << 23));
+      r6 = rcp_approx_ftz(6.0f);
+      rgq = rcp_approx_ftz(gq);
+      if (blockIdx.x == 0 && threadIdx.x == 64 && qo.g_used != nullptr) *qo.g_used = gq;
     }
     const uint32_t tab_base = smem_u32(gelu_tab);
     uint8_t* warp_staging = staging + (warp - 2) * kWarpStagingBytes;
@@ -577,7 +625,59 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
       for (int j = 0; j < 32; ++j) y[j] = scale_pack_bf16x2(r[2 * j], r[2 * j + 1], alpha2);
       const int col0 = nb * BN + (half > 0 ? BN / 2 : 0) + col_base;
-      if constexpr (P::kStaged) {
+      if constexpr (kEpi == 3) {
+        // GEMM1 quantizing its output: bias and GELU as kEpi 1, then each of the row's
+        // four 16-column blocks is quantized with the provisional encode scale exactly as
+        // the activation quantizer does it (quantize_block16); the 32 code bytes and the
+        // four scale bytes (one 32-bit word of the 128x4 layout) are stored directly.
+        const int row = mb * BM + trow;
+        const bool real = row < m;
+        const uint4* bias4 = reinterpret_cast<const uint4*>(bias + col0);
+        uint32_t tile_max = 0, s8w = 0;
+        uint32_t cw[8];
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+          uint32_t hw[8];
+#pragma unroll
+          for (int hq = 0; hq < 2; ++hq) {
+            const int q = 2 * blk + hq;
+            uint4 bv = make_uint4(0, 0, 0, 0);
+            if (bias != nullptr) bv = __ldg(bias4 + q);
+            const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              o[j] = y[4 * q + j];
+              if (bias != nullptr) o[j] = add_bf16x2(o[j], bw[j]);
+            }
+            gelu_bf16x2_x4(o, tab_base, gelu_tab);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              tile_max = max_u16x2(tile_max, o[j] & 0x7FFF7FFFu);
+              hw[4 * hq + j] = o[j];
+            }
+          }
+          float sfval;
+          uint32_t vbits;
+          const uint32_t s8 = quantize_block16(hw, gq, r6, rgq, cw[2 * blk], cw[2 * blk + 1], &sfval,
+                                               &vbits);
+          s8w |= s8 << (8 * blk);
+          if (real) {
+            if (sfval > 448.0f) qflags |= kQuantSaturated;
+            if (vbits >= 0x0080u && s8 == 0) qflags |= kQuantUnderflow;
+          }
+        }
+        if (real) {
+          amax2 = max_u16x2(amax2, tile_max);
+          uint4* dst = reinterpret_cast<uint4*>(qo.codes + static_cast<int64_t>(row) * (n / 2) + col0 / 2);
+          dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+          dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+        }
+        // rows past m inside the last 128-row block get zero scales, as the quantizer's do
+        const int64_t off = static_cast<int64_t>(row >> 7) * ((n / 64) * 512) + (col0 >> 6) * 512 +
+                            (row & 31) * 16 + ((row & 127) >> 5) * 4;
+        *reinterpret_cast<uint32_t*>(qo.sf + off) = real ? s8w : 0u;
+      } else if constexpr (P::kStaged) {
         // GEMM1: bias, GELU and the amax on this thread's row, then the warp's
         // 32 x 64 block goes out in one tensor store from 128B-swizzled staging
         // (chunk c of row r at r*128 + ((c ^ (r & 7)) * 16), the tensor map's
@@ -640,12 +740,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
       }
     }
-    if (kEpi == 1) {
+    if (kEpi == 1 || kEpi == 3) {
       // the tensor stores must be complete before the CTA exits
-      if (lane == 0) bulk_wait_group0();
+      if (kEpi == 1 && lane == 0) bulk_wait_group0();
       const uint32_t mag = max(amax2 & 0xFFFFu, amax2 >> 16);
       const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, mag << 16);
       if (lane == 0 && bits != 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), bits);
+      if (kEpi == 3) {
+        const uint32_t f = __reduce_or_sync(0xFFFFFFFFu, qflags);
+        if (lane == 0 && f != 0 && qo.flags != nullptr) atomicOr(qo.flags, f);
+      }
     }
   }
 
@@ -1625,23 +1729,20 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CU
                           const uint8_t* w_sf, const float* g_a, const float* g_w,
                           const float* alpha, const uint16_t* bias, uint16_t* out, int m, int n,
                           int k, float* amax_out, uint64_t wait_limit, cudaStream_t st,
-                          const uint16_t* residual = nullptr, const uint16_t* gate = nullptr) {
-  static bool attr_set[64] = {false};
+                          const uint16_t* residual = nullptr, const uint16_t* gate = nullptr,
+                          const QuantOut& qo = QuantOut()) {
+  static ContextCache attr_done;
   constexpr int kSmemBytes = Plan<kEpi, kResident, kRepSfb>::kSmemBytes;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_kernel<kEpi, kResident, kRepSfb>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  if (cudaError_t e = ensure_max_dynamic_smem(
+          attr_done, reinterpret_cast<const void*>(nvfp4_gemm_kernel<kEpi, kResident, kRepSfb>),
+          kSmemBytes))
+    return e;
   const int tiles = ((m + BM - 1) / BM) * (n / BN);
   int grid = sm_count();
   if (grid > tiles) grid = tiles;
   nvfp4_gemm_kernel<kEpi, kResident, kRepSfb><<<grid, kNumThreads, kSmemBytes, st>>>(
       ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit, residual,
-      gate);
+      gate, qo);
   return cudaGetLastError();
 }
 
@@ -1691,16 +1792,11 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
                              const uint16_t* bias, uint16_t* out, int m, int n, int k,
                              uint64_t wait_limit, cudaStream_t st,
                              const uint16_t* residual = nullptr, const uint16_t* gate = nullptr) {
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(nvfp4_gemm_pair_kernel<kEpi, kRawSfb>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         PairPlan<kRawSfb>::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  static ContextCache attr_done;
+  if (cudaError_t e = ensure_max_dynamic_smem(
+          attr_done, reinterpret_cast<const void*>(nvfp4_gemm_pair_kernel<kEpi, kRawSfb>),
+          PairPlan<kRawSfb>::kSmemBytes))
+    return e;
   const int tiles = (m / (2 * BM)) * (n / BN);
   int pairs = sm_count() / 2;
   if (pairs > tiles) pairs = tiles;
@@ -1725,16 +1821,11 @@ cudaError_t launch_fp8_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, cons
                               const float* sa, const float* sw, const uint16_t* bias, uint16_t* out,
                               int m, int n, int k, uint32_t* row_amax, uint64_t wait_limit,
                               cudaStream_t st) {
-  static bool attr_set[64] = {false};
+  static ContextCache attr_done;
   constexpr int kSmemBytes = F8Plan<kEpi>::kSmemBytes;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<kEpi>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  if (cudaError_t e = ensure_max_dynamic_smem(
+          attr_done, reinterpret_cast<const void*>(fp8_gemm_kernel<kEpi>), kSmemBytes))
+    return e;
   const int tiles = ((m + BM - 1) / BM) * (n / BN);
   int grid = sm_count();
   if (grid > tiles) grid = tiles;
@@ -1748,16 +1839,11 @@ cudaError_t launch_fp8_gemm_pair_t(const CUtensorMap& ma, const CUtensorMap& mb_
                                    const CUtensorMap& mo, const float* sa, const float* sw,
                                    const uint16_t* bias, uint16_t* out, int m, int n, int k,
                                    uint32_t* row_amax, uint64_t wait_limit, cudaStream_t st) {
-  static bool attr_set[64] = {false};
+  static ContextCache attr_done;
   constexpr int kSmemBytes = F8PairPlan<kEpi>::kSmemBytes;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_pair_kernel<kEpi>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  if (cudaError_t e = ensure_max_dynamic_smem(
+          attr_done, reinterpret_cast<const void*>(fp8_gemm_pair_kernel<kEpi>), kSmemBytes))
+    return e;
   const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * (n / BN);
   int pairs = sm_count() / 2;
   if (pairs > tiles) pairs = tiles;
@@ -1833,7 +1919,7 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                         const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
                         int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
                         const char** why, const uint8_t* w_sf_rep, const uint16_t* residual,
-                        const uint16_t* gate) {
+                        const uint16_t* gate, const QuantOut* qo) {
   alignas(64) CUtensorMap ma;
   alignas(64) CUtensorMap mb;
   if (!make_code_map(&ma, a_codes, m, k, BM) || !make_code_map(&mb, w_codes, n, k, BN)) {
@@ -1847,6 +1933,19 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
     return cudaErrorInvalidValue;
   }
   const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
+  if (epilogue == 3) {
+    if (qo == nullptr || qo->codes == nullptr || qo->sf == nullptr || qo->amax_hint == nullptr ||
+        amax_out == nullptr) {
+      if (why) *why = "the quantizing epilogue needs codes, scales, an amax hint and amax_out";
+      return cudaErrorInvalidValue;
+    }
+    const bool resident = (k / 64) <= kMaxResidentKSteps && (n / BN) <= sm_count();
+    if (resident)
+      return launch_gemm_t<3, true>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
+                                    amax_out, wait_limit, st, nullptr, nullptr, *qo);
+    return launch_gemm_t<3, false>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
+                                   amax_out, wait_limit, st, nullptr, nullptr, *qo);
+  }
   if (epilogue == 1) {
     // W scales stay in TMEM when they fit and every N block gets a CTA
     const bool resident = (k / 64) <= kMaxResidentKSteps && (n / BN) <= sm_count();
@@ -1915,19 +2014,74 @@ cudaError_t launch_gelu_probe(const uint16_t* in, uint16_t* out, int64_t count, 
   return cudaGetLastError();
 }
 
-uint32_t* error_word_ptr() {
-  static uint32_t* cached[64] = {nullptr};
-  static std::mutex mu;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  std::lock_guard<std::mutex> lock(mu);
-  if (cached[dev] == nullptr) {
+namespace {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+struct CtxQuery {
+  CtxGetCurrentFn get_current = nullptr;
+  CtxGetIdFn get_id = nullptr;
+};
+
+const CtxQuery& ctx_query() {
+  static CtxQuery q;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess)
-      cached[dev] = static_cast<uint32_t*>(p);
-  }
-  return cached[dev];
+    cudaDriverEntryPointQueryResult r;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &r) == cudaSuccess &&
+        r == cudaDriverEntryPointSuccess)
+      q.get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &r) == cudaSuccess &&
+        r == cudaDriverEntryPointSuccess)
+      q.get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  return q;
+}
+}  // namespace
+
+uint64_t current_context_id() {
+  const CtxQuery& q = ctx_query();
+  if (q.get_current == nullptr || q.get_id == nullptr) return 0;
+  CUcontext c = nullptr;
+  if (q.get_current(&c) != CUDA_SUCCESS || c == nullptr) return 0;
+  unsigned long long id = 0;
+  if (q.get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return static_cast<uint64_t>(id);
+}
+
+cudaError_t context_symbol_address(ContextCache& cache, const void* symbol, void** out) {
+  uint64_t id = current_context_id();
+  if (id != 0 && cache.get(id, out)) return cudaSuccess;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, symbol);
+  if (e != cudaSuccess) return e;
+  if (p == nullptr) return cudaErrorInvalidSymbol;
+  if (id == 0) id = current_context_id();  // the lookup itself made the primary context current
+  if (id != 0) cache.put(id, p);
+  *out = p;
+  return cudaSuccess;
+}
+
+cudaError_t ensure_max_dynamic_smem(ContextCache& cache, const void* fn, int bytes) {
+  void* done = nullptr;
+  const uint64_t id = current_context_id();
+  if (id != 0 && cache.get(id, &done)) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  const uint64_t id2 = id != 0 ? id : current_context_id();
+  if (id2 != 0) cache.put(id2, reinterpret_cast<void*>(1));
+  return cudaSuccess;
+}
+
+uint32_t* error_word_ptr() {
+  static ContextCache cache;
+  void* p = nullptr;
+  if (context_symbol_address(cache, reinterpret_cast<const void*>(&g_device_error), &p) !=
+      cudaSuccess)
+    return nullptr;
+  return static_cast<uint32_t*>(p);
 }
 
 cudaError_t set_error_word(uint32_t v, cudaStream_t st) {

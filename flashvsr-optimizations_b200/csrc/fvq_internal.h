@@ -3,6 +3,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
 
 namespace fvq {
@@ -25,7 +26,7 @@ constexpr int kAmaxMaxBlocks = 2048;
 constexpr int kWsCounter = 0;
 constexpr int kWsGeneration = 1;
 constexpr int kWsAmax = 2;
-constexpr int kWsGroups = 32;          // 64 group counters
+constexpr int kWsGroups = 32;          // up to 32 group counters (words 32..127)
 constexpr int kBarrierGroup = 64;      // CTAs per group counter
 constexpr int kWsPartial = 128;
 constexpr size_t kAmaxWorkspaceBytes = (kWsPartial + kAmaxMaxBlocks) * 4;
@@ -37,6 +38,50 @@ inline size_t sf_bytes(int64_t rows, int64_t k) {
 }
 
 int sm_count();
+
+// Per-context caches.  The device address of a __device__ symbol of this library and a
+// kernel's function attributes belong to a CUDA context, not to a device ordinal: after
+// cudaDeviceReset, or under a caller's own driver-API context, the module is loaded
+// again, possibly at another address.  Values are therefore cached under the unique id
+// of the calling thread's current context (cuCtxGetId; ids are never reused).
+uint64_t current_context_id();  // 0 when no context is current or the query failed
+
+class ContextCache {
+ public:
+  bool get(uint64_t ctx, void** value) {
+    std::lock_guard<std::mutex> lock(mu_);
+    for (int i = 0; i < n_; ++i)
+      if (ids_[i] == ctx) {
+        *value = vals_[i];
+        return true;
+      }
+    return false;
+  }
+  void put(uint64_t ctx, void* value) {
+    std::lock_guard<std::mutex> lock(mu_);
+    for (int i = 0; i < n_; ++i)
+      if (ids_[i] == ctx) {
+        vals_[i] = value;
+        return;
+      }
+    const int slot = n_ < kSlots ? n_++ : static_cast<int>(next_++ % kSlots);  // oldest goes
+    ids_[slot] = ctx;
+    vals_[slot] = value;
+  }
+
+ private:
+  static constexpr int kSlots = 64;
+  std::mutex mu_;
+  uint64_t ids_[kSlots] = {};
+  void* vals_[kSlots] = {};
+  int n_ = 0;
+  uint64_t next_ = 0;
+};
+
+// cudaGetSymbolAddress of `symbol` in the current context, cached per context.
+cudaError_t context_symbol_address(ContextCache& cache, const void* symbol, void** out);
+// cudaFuncSetAttribute(fn, MaxDynamicSharedMemorySize, bytes) once per context.
+cudaError_t ensure_max_dynamic_smem(ContextCache& cache, const void* fn, int bytes);
 
 // Record a message for fvq_last_error() and return `code` (fvq_api.cu).
 int report_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
@@ -74,12 +119,29 @@ cudaError_t launch_replicate_w_scales(const uint8_t* sf, int64_t n, int64_t k, u
                                       cudaStream_t st);
 
 // GEMM (fvq_gemm.cu)
+// Epilogue 3 (GEMM1 quantizing its own output): bias, GELU and the amax as epilogue 1,
+// then NVFP4 codes [m, n/2] and 128x4-swizzled E4M3 scales of the result with the
+// provisional encode scale g = 2^-headroom_log2 * 2688 / max(*amax_hint, 1e-12), written
+// to `codes` / `sf` (no bf16 output).  g_used (optional) receives g; flags (optional) collects
+// kQuantSaturated (a block's scale value g * vmax / 6 exceeded 448 and was clipped)
+// and kQuantUnderflow (a nonzero block's scale rounded to zero).
+constexpr uint32_t kQuantSaturated = 1u << 0;
+constexpr uint32_t kQuantUnderflow = 1u << 1;
+struct QuantOut {
+  uint8_t* codes = nullptr;
+  uint8_t* sf = nullptr;
+  const float* amax_hint = nullptr;
+  int headroom_log2 = 0;
+  float* g_used = nullptr;
+  uint32_t* flags = nullptr;
+};
 cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
                         const float* alpha, const uint16_t* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
                         int epilogue, float* amax_out, uint64_t wait_limit, cudaStream_t st,
                         const char** why, const uint8_t* w_sf_rep = nullptr,
-                        const uint16_t* residual = nullptr, const uint16_t* gate = nullptr);
+                        const uint16_t* residual = nullptr, const uint16_t* gate = nullptr,
+                        const QuantOut* qo = nullptr);
 // epilogue 2 (replicated W scales only): out = bf16(residual + bf16(gate[n] * y)), y the
 // epilogue-0 result -- the gated residual of a DiT block around its FFN.
 // FVQ_EPI_BF16 GEMMs with replicated W scales, alpha from the global scales and

@@ -15,16 +15,16 @@
 //     GPU that loads the library until the process exits;
 //   * rows x in_features must fit it (fvq_nvfp4_linear_workspace_bytes);
 //     larger calls are rejected with FVQ_EWORKSPACE and a message;
-//   * the first call on a device resolves the array's device address with
-//     cudaGetSymbolAddress (with that device current); make that first call
-//     before any stream capture;
+//   * the first call in each CUDA context (the device's primary context, or a
+//     caller's own driver-API context) resolves the array's device address with
+//     cudaGetSymbolAddress, with that context current, and caches it under the
+//     context's unique id, so a device reset or another context is looked up
+//     again; make that first call before any stream capture;
 //   * every call shares the one array: calls that overlap on the GPU (other
 //     streams, other host threads) race.  The amax arrival counter inside it
 //     starts at zero (static device memory is zero-initialised) and every
 //     call re-arms it; everything else is written before it is read.
 #include <cuda_runtime.h>
-
-#include <mutex>
 
 #include "../../include/fvq.h"
 #include "fvq_internal.h"
@@ -35,22 +35,22 @@ constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[64] = {nullptr};
+fvq::ContextCache g_noalloc_addr;
 
-// Device address of the scratch array for the current device (set-up on first use).
+// Device address of the scratch array in the calling thread's current CUDA context.
+// The address belongs to the context (a device reset or a caller's own driver-API
+// context loads the library's device image again, possibly elsewhere), so it is
+// looked up with cudaGetSymbolAddress once per context and cached under the
+// context's unique id.
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) return FVQ_ECUDA;
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) return FVQ_ECUDA;
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+  uint64_t ctx = fvq::current_context_id();
+  if (ctx != 0 && g_noalloc_addr.get(ctx, out)) return FVQ_OK;
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess || ptr == nullptr) return FVQ_ECUDA;
+  if (ctx == 0) ctx = fvq::current_context_id();  // the lookup made the primary context current
+  if (ctx != 0) g_noalloc_addr.put(ctx, ptr);
+  *out = ptr;
   return FVQ_OK;
 }
 

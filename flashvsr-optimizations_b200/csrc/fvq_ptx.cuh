@@ -481,4 +481,75 @@ __device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
   return out;
 }
 
+// Packed bf16 maximum (max.bf16x2); on non-negative non-NaN values it orders
+// exactly like the bit patterns.
+__device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// four bytes (low 8 bits of each argument) -> one word, b0 lowest
+__device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
+  uint32_t lo, hi, r;
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(lo) : "r"(b0), "r"(b1));
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(hi) : "r"(b2), "r"(b3));
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+
+// bf16x2 word times the block's scale (both halves, one mul.rn.ftz.f32x2),
+// converted to two E2M1 codes.
+__device__ __forceinline__ uint32_t scaled_e2m1x2(uint32_t w, uint64_t os2) {
+  uint64_t xv, pv;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(xv) : "r"(w << 16), "r"(w & 0xFFFF0000u));
+  asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(pv) : "l"(xv), "l"(os2));
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(pv));
+  return f32x2_to_e2m1x2(lo, hi);
+}
+
+// g = reciprocal(max(amax, 1e-12)) * 2688 with IEEE rounding at each step,
+// as torch evaluates 2688. / t on a device tensor.
+__device__ __forceinline__ float encode_scale(float amax) {
+  float m = fmaxf(amax, 1e-12f);
+  return __fmul_rn(__frcp_rn(m), 2688.0f);
+}
+
+
+// One 16-value block of NVFP4 quantization (the per-block recipe of FlashInfer's
+// cvt_warp_fp16_to_fp4, non-TE branch) on its eight bf16x2 words w:
+//   vmax = max |x| (exact, bf16);  s8 = e4m3_rn_satfinite(g * (vmax * rcp(6)));
+//   os = vmax != 0 ? rcp(float(s8) * rcp(g)) : 0;  code = e2m1_rn_satfinite(x * os)
+// with rcp = rcp.approx.ftz.f32 and flush-to-zero products.  r6 = rcp(6), rg = rcp(g)
+// are passed in (loop invariants).  Returns s8; c0, c1 get the 16 codes (element 2j in
+// the low nibble of byte j).  *sf_value (if given) receives g * (vmax * rcp(6)) before
+// the E4M3 conversion and *vmax_bits the block maximum (for saturation checks).
+__device__ __forceinline__ uint32_t quantize_block16(const uint32_t (&w)[8], float g, float r6,
+                                                     float rg, uint32_t& c0, uint32_t& c1,
+                                                     float* sf_value = nullptr,
+                                                     uint32_t* vmax_bits = nullptr) {
+  const uint32_t m2 = bmax2(bmax2(bmax2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                                  bmax2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)),
+                            bmax2(bmax2(w[4] & 0x7FFF7FFFu, w[5] & 0x7FFF7FFFu),
+                                  bmax2(w[6] & 0x7FFF7FFFu, w[7] & 0x7FFF7FFFu)));
+  const uint32_t bm = max(m2 & 0xFFFFu, m2 >> 16);   // block max |x|, bf16 bits (exact)
+  const float vmax = __uint_as_float(bm << 16);
+  const float sfval = mul_ftz(g, mul_ftz(vmax, r6));
+  const uint32_t s8 = f32_to_e4m3(sfval);
+  const float sfv = e4m3_to_f32(s8);
+  // vmax != 0 under flush-to-zero: a subnormal maximum counts as zero
+  const float os = (bm >= 0x0080u) ? rcp_approx_ftz(mul_ftz(sfv, rg)) : 0.0f;
+  uint64_t os2;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(os2) : "f"(os));
+  uint32_t byte[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) byte[j] = scaled_e2m1x2(w[j], os2);
+  c0 = pack4(byte[0], byte[1], byte[2], byte[3]);
+  c1 = pack4(byte[4], byte[5], byte[6], byte[7]);
+  if (sf_value != nullptr) *sf_value = sfval;
+  if (vmax_bits != nullptr) *vmax_bits = bm;
+  return s8;
+}
+
 }  // namespace fvq

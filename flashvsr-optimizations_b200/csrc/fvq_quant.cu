@@ -29,14 +29,6 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
   return v;
 }
 
-// Packed bf16 maximum (max.bf16x2); on non-negative non-NaN values it orders
-// exactly like the bit patterns.
-__device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
 // max of |bf16| over the 8 values of a uint4, as a bf16 bit pattern in the low 16 bits.
 __device__ __forceinline__ uint32_t absmax8(uint4 v) {
   const uint32_t m = bmax2(bmax2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
@@ -61,22 +53,6 @@ __device__ __forceinline__ uint32_t absmax_words(const uint4* __restrict__ xv, i
     for (int u = 0; u < kUnroll; ++u) m = max(m, absmax8(v[u]));
   }
   return m;
-}
-
-// four bytes (low 8 bits of each argument) -> one word, b0 lowest
-__device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
-  uint32_t lo, hi, r;
-  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(lo) : "r"(b0), "r"(b1));
-  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(hi) : "r"(b2), "r"(b3));
-  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(r) : "r"(lo), "r"(hi));
-  return r;
-}
-
-// g = reciprocal(max(amax, 1e-12)) * 2688 with IEEE rounding at each step,
-// as torch evaluates 2688. / t on a device tensor.
-__device__ __forceinline__ float encode_scale(float amax) {
-  float m = fmaxf(amax, 1e-12f);
-  return __fmul_rn(__frcp_rn(m), 2688.0f);
 }
 
 // ---------------------------------------------------------------- amax
@@ -159,16 +135,6 @@ Div31 make_div31(uint32_t d) {  // d >= 2
   return Div31{static_cast<uint32_t>((num + d - 1) / d), l - 1};
 }
 
-// bf16x2 word times the block's scale (both halves, one mul.rn.ftz.f32x2),
-// converted to two E2M1 codes.
-__device__ __forceinline__ uint32_t scaled_e2m1x2(uint32_t w, uint64_t os2) {
-  uint64_t xv, pv;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(xv) : "r"(w << 16), "r"(w & 0xFFFF0000u));
-  asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(pv) : "l"(xv), "l"(os2));
-  float lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(pv));
-  return f32x2_to_e2m1x2(lo, hi);
-}
 
 __device__ __forceinline__ void discard_l2_line(const void* p) {
   asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
@@ -250,23 +216,8 @@ __device__ __forceinline__ void quantize_blocks(const uint16_t* __restrict__ x, 
 #pragma unroll
       for (int j = 0; j < 8; ++j) w[j] = v[u][j];
       if (b < n_real) xf(b, w, a[u]);
-      const uint32_t m2 = bmax2(bmax2(bmax2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
-                                      bmax2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)),
-                                bmax2(bmax2(w[4] & 0x7FFF7FFFu, w[5] & 0x7FFF7FFFu),
-                                      bmax2(w[6] & 0x7FFF7FFFu, w[7] & 0x7FFF7FFFu)));
-      const uint32_t bm = max(m2 & 0xFFFFu, m2 >> 16);   // block max |x|, bf16 bits (exact)
-      const float vmax = __uint_as_float(bm << 16);
-      const uint32_t s8 = f32_to_e4m3(mul_ftz(g, mul_ftz(vmax, r6)));
-      const float sfv = e4m3_to_f32(s8);
-      // vmax != 0 under flush-to-zero: a subnormal maximum counts as zero
-      const float os = (bm >= 0x0080u) ? rcp_approx_ftz(mul_ftz(sfv, rg)) : 0.0f;
-      uint64_t os2;
-      asm("mov.b64 %0, {%1, %1};" : "=l"(os2) : "f"(os));
-      uint32_t byte[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) byte[j] = scaled_e2m1x2(w[j], os2);
-      const uint32_t c0 = pack4(byte[0], byte[1], byte[2], byte[3]);
-      const uint32_t c1 = pack4(byte[4], byte[5], byte[6], byte[7]);
+      uint32_t c0, c1;
+      const uint32_t s8 = quantize_block16(w, g, r6, rg, c0, c1);
       // gather the group's 4 scale bytes into its first lane (b % 4 == lane % 4)
       const uint32_t lead = lane & ~3u;
       const uint32_t s1 = __shfl_sync(0xFFFFFFFFu, s8, lead + 1);

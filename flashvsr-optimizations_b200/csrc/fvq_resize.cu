@@ -316,15 +316,10 @@ __global__ void __launch_bounds__(kResizeThreads) pil_normalize_kernel(
 template <bool kU8, bool kBf16>
 cudaError_t launch_resize_t(const uint8_t* src, int64_t frames, const ResizeGeom& g, uint8_t* u8,
                             uint16_t* bf16, size_t smem, cudaStream_t st) {
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(pil_resize_kernel<kU8, kBf16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  static ContextCache attr_done;
+  if (cudaError_t e = ensure_max_dynamic_smem(
+          attr_done, reinterpret_cast<const void*>(pil_resize_kernel<kU8, kBf16>), 227 * 1024))
+    return e;
   const dim3 grid((g.crop_h + kTileRows - 1) / kTileRows, (g.crop_w + g.tile_w - 1) / g.tile_w,
                   static_cast<unsigned>(frames));
   pil_resize_kernel<kU8, kBf16><<<grid, kResizeThreads, smem, st>>>(src, g, u8, bf16);

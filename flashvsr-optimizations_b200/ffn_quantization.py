@@ -109,20 +109,109 @@ class NVFP4FFN(torch.nn.Sequential):
 
     Indexing, iteration and state-dict keys are those of the Sequential it
     replaces; ``forward`` computes exactly what the Sequential of QuantLinear
-    modules would, in five kernel launches.
+    modules would, in four kernel launches (amax + quantize of x, GEMM1 with bias,
+    GELU and the amax of the intermediate, quantize of the intermediate, GEMM2 with
+    bias).
     """
+
+    H_SCALINGS = ("exact", "static", "delayed")
 
     def __init__(self, lin1: QuantLinear, act: torch.nn.Module, lin2: QuantLinear):
         super().__init__(lin1, act, lin2)
         if lin1.out_features != lin2.in_features or lin2.out_features != lin1.in_features:
             raise ValueError("NVFP4FFN: linear shapes do not chain")
+        self.h_scaling = "exact"
+        self.headroom_log2 = 0
+        self.rerun_on_saturation = False
+        self._h_state = None      # fp32 [2]: the hint and the amax seen (swapped per call)
+        self._h_flags = None      # int32 [1]
+        self._h_turn = 0
+        self._h_seeded = False
+
+    def set_h_scaling(self, mode: str = "exact", amax=None, headroom_log2: int | None = None,
+                      rerun_on_saturation: bool = False) -> "NVFP4FFN":
+        """How the intermediate h = GELU(linear1(x)) is scaled for its NVFP4 quantization.
+
+        * ``"exact"`` (default): the reference's scale 2688 / amax(h) of the whole tensor
+          (ffn_quantization.py:63-64).  amax(h) is known only after GEMM1 has finished, so h
+          makes one bf16 round trip through HBM (four launches); the output equals the
+          reference's bit for bit.
+        * ``"static"``: GEMM1's epilogue quantizes h itself with a provisional scale from
+          `amax`, a calibrated estimate of max |h|: no bf16 intermediate, three launches.
+        * ``"delayed"``: the same, with the max |h| the previous call saw as the estimate
+          (its first call runs the exact path to seed it); default headroom 2x.
+
+        The provisional scale differs from the exact one by other than a power of two, so
+        the intermediate is quantized differently from the reference (the same number
+        format and recipe, another scale grid): as close to the unquantized FFN as the
+        reference is, not bit-identical to it.  A block whose scale saturates (h above
+        hint x 2^headroom_log2) sets bit 0 of the device flags (``h_flags()``); with
+        `rerun_on_saturation` the call then reads the flag (a host synchronisation) and
+        reruns the exact path.
+        """
+        if mode not in self.H_SCALINGS:
+            raise ValueError(mode)
+        self.h_scaling = mode
+        self.headroom_log2 = (1 if mode == "delayed" else 0) if headroom_log2 is None else int(headroom_log2)
+        self.rerun_on_saturation = bool(rerun_on_saturation)
+        dev = self[0].qweight.device
+        self._h_state = torch.zeros(2, dtype=torch.float32, device=dev)
+        self._h_flags = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._h_turn = 0
+        self._h_seeded = False
+        if mode == "static":
+            if amax is None:
+                raise ValueError("static h scaling needs amax (an estimate of max |h|)")
+            self._h_state[0] = torch.as_tensor(amax, dtype=torch.float32).reshape(())
+            self._h_seeded = True
+        return self
+
+    def h_flags(self, clear: bool = True) -> int:
+        """The provisional-scale flags of the calls so far (1 saturated, 2 underflowed);
+        reads the device (a host synchronisation)."""
+        if self._h_flags is None:
+            return 0
+        v = int(self._h_flags.item())
+        if clear:
+            self._h_flags.zero_()
+        return v
+
+    def _exact_with_amax(self, x2: torch.Tensor):
+        """The exact path as separate launches, returning max |h| as well (the same bits as
+        fvq_nvfp4_ffn)."""
+        l1, l2 = self[0], self[2]
+        g = ops.global_scale(x2)
+        q, s = ops.nvfp4_quantize(x2, g)
+        h, amax_h = ops.nvfp4_gemm(q, s, g, l1.qweight, l1.scale, l1.global_sf, l1.bias, gelu=True)
+        qh, sh, gh = ops.nvfp4_quantize_from_amax(h, amax_h)
+        y, _ = ops.nvfp4_gemm(qh, sh, gh, l2.qweight, l2.scale, l2.global_sf, l2.bias, gelu=False)
+        return y, amax_h
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         l1, l2 = self[0], self[2]
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).contiguous()
-        y = ops.nvfp4_ffn(x2, l1.qweight, l1.scale, l1.global_sf, l1.bias,
-                          l2.qweight, l2.scale, l2.global_sf, l2.bias)
+        if self.h_scaling == "exact":
+            y = ops.nvfp4_ffn(x2, l1.qweight, l1.scale, l1.global_sf, l1.bias,
+                              l2.qweight, l2.scale, l2.global_sf, l2.bias)
+        elif not self._h_seeded:
+            y, amax_h = self._exact_with_amax(x2)
+            self._h_state[0:1].copy_(amax_h)
+            self._h_turn = 0
+            self._h_seeded = True
+        else:
+            t = self._h_turn
+            hint, seen = self._h_state[t:t + 1], self._h_state[1 - t:2 - t]
+            y = ops.nvfp4_ffn_fused(x2, l1.qweight, l1.scale, l1.global_sf, l1.bias,
+                                    l2.qweight, l2.scale, l2.global_sf, l2.bias,
+                                    hint, self.headroom_log2, seen, self._h_flags)
+            if self.h_scaling == "delayed":
+                self._h_turn = 1 - t
+            if self.rerun_on_saturation and self.h_flags(clear=False) & 1:
+                self._h_flags.zero_()
+                y, amax_h = self._exact_with_amax(x2)
+                if self.h_scaling == "delayed":
+                    self._h_state[self._h_turn:self._h_turn + 1].copy_(amax_h)
         return y.reshape(*shape[:-1], l2.out_features)
 
     def modulated(self, x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,

@@ -291,6 +291,42 @@ def _(x, q1, s1, g1, b1, q2, s2, g2, b2):
     return x.new_empty(x.shape, dtype=torch.bfloat16)
 
 
+@torch.library.custom_op("fvq::nvfp4_ffn_fused", mutates_args=("amax_seen", "flags"))
+def nvfp4_ffn_fused(x: torch.Tensor, q1: torch.Tensor, s1: torch.Tensor, g1: torch.Tensor,
+                    b1: torch.Tensor | None, q2: torch.Tensor, s2: torch.Tensor, g2: torch.Tensor,
+                    b2: torch.Tensor | None, amax_hint: torch.Tensor, headroom_log2: int,
+                    amax_seen: torch.Tensor, flags: torch.Tensor) -> torch.Tensor:
+    """The FFN with the intermediate quantized inside GEMM1's epilogue (fvq_nvfp4_ffn_fused):
+    h never reaches HBM in bf16; its encode scale is 2^-headroom_log2 * 2688 / amax_hint
+    instead of 2688 / amax(h).  amax_seen (fp32 [1]) receives max |h|; flags (int32 [1]) is
+    OR-ed with 1 when a block's scale saturated and 2 when a nonzero block's scale
+    underflowed to zero."""
+    _check_cuda("nvfp4_ffn_fused", x, q1, s1, g1, b1, q2, s2, g2, b2, amax_hint, amax_seen, flags)
+    _check_bf16("nvfp4_ffn_fused", x)
+    m, d = x.shape
+    f = q1.shape[0]
+    if m == 0:
+        raise RuntimeError("nvfp4_ffn_fused: empty input")
+    if amax_hint.dtype != torch.float32 or amax_seen.dtype != torch.float32 or \
+            flags.dtype != torch.int32:
+        raise ValueError("nvfp4_ffn_fused: amax_hint / amax_seen fp32, flags int32")
+    x = _aligned32(x)
+    y = torch.empty((m, d), dtype=torch.bfloat16, device=x.device)
+    lib = _lib.load()
+    ws = workspace(x.device, lib.fvq_nvfp4_ffn_fused_workspace_bytes(m, d, f))
+    l1 = _linear_struct(q1, s1, g1, b1, d, f)
+    l2 = _linear_struct(q2, s2, g2, b2, f, d)
+    _lib.call("fvq_nvfp4_ffn_fused", _ptr(x), m, ctypes.byref(l1), ctypes.byref(l2), _ptr(y),
+              _ptr(amax_hint), int(headroom_log2), _ptr(amax_seen), _ptr(flags), _ptr(ws),
+              ws.numel(), _stream(x))
+    return y
+
+
+@nvfp4_ffn_fused.register_fake
+def _(x, q1, s1, g1, b1, q2, s2, g2, b2, amax_hint, headroom_log2, amax_seen, flags):
+    return x.new_empty(x.shape, dtype=torch.bfloat16)
+
+
 # ---------------------------------------------------------------- the DiT block around the FFN
 def _vec(name: str, v: torch.Tensor, d: int) -> torch.Tensor:
     v = v.reshape(-1)

@@ -39,30 +39,52 @@ def shard_rows(x: torch.Tensor, world: int, rank: int) -> torch.Tensor:
     return x[start:stop]
 
 
-def gather_rows(local: torch.Tensor, total: int, group=None) -> torch.Tensor:
+def gather_rows(local: torch.Tensor, total: int, group=None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
     """All-gather row blocks made by `row_range` back into the full [total, ...] tensor.
 
-    Blocks may differ by one row; each is padded to the largest block for the
-    fixed-size collective and the padding is dropped afterwards.
+    When every rank holds the same number of rows (total % world == 0, as for the stack
+    workloads on 1/2/4/8 GPUs) the blocks are gathered straight into `out` with one
+    all_gather_into_tensor: no padding, no concatenation.  Uneven blocks (they differ by
+    one row) are padded to the largest block for the fixed-size collective, and the
+    ranks after the first total % world are moved down by their missing rows afterwards.
+    `out` (optional) receives the result and is returned.
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     start, stop = row_range(total, world, rank)
     if local.shape[0] != stop - start:
         raise ValueError(f"rank {rank}: expected {stop - start} rows, got {local.shape[0]}")
-    biggest = row_range(total, world, 0)[1]
-    padded = local.new_zeros((biggest, *local.shape[1:]))
+    shape = (total, *local.shape[1:])
+    if out is None:
+        out = local.new_empty(shape)
+    elif tuple(out.shape) != shape or out.dtype != local.dtype or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {local.dtype} tensor of shape {shape}")
+    nccl = dist.get_backend(group) == "nccl"
+    base, extra = divmod(total, world)
+    local = local.contiguous()
+    if extra == 0:
+        if nccl:
+            dist.all_gather_into_tensor(out, local, group=group)
+        else:
+            dist.all_gather(list(out.chunk(world)), local, group=group)
+        return out
+    biggest = base + 1
+    padded = local.new_empty((biggest, *local.shape[1:]))
     padded[: local.shape[0]] = local
-    out = local.new_empty((world * biggest, *local.shape[1:]))
-    if dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(out, padded.contiguous(), group=group)
+    if local.shape[0] < biggest:
+        padded[local.shape[0]:].zero_()
+    gathered = local.new_empty((world * biggest, *local.shape[1:]))
+    if nccl:
+        dist.all_gather_into_tensor(gathered, padded, group=group)
     else:
-        dist.all_gather(list(out.chunk(world)), padded.contiguous(), group=group)
-    parts = []
-    for r in range(world):
-        s, e = row_range(total, world, r)
-        parts.append(out[r * biggest: r * biggest + (e - s)])
-    return torch.cat(parts, dim=0)
+        dist.all_gather(list(gathered.chunk(world)), padded, group=group)
+    # ranks 0..extra-1 hold `biggest` rows and already sit at their final offsets
+    out[: extra * biggest] = gathered[: extra * biggest]
+    if world > extra:
+        tail = gathered[extra * biggest:].reshape(world - extra, biggest, *local.shape[1:])
+        out[extra * biggest:] = tail[:, :base].reshape(-1, *local.shape[1:])
+    return out
 
 
 def global_amax(amax: torch.Tensor, group=None) -> torch.Tensor:

@@ -87,3 +87,16 @@ def edge_case_tensor(m: int = 130, k: int = 256, seed: int = 5) -> np.ndarray:
     x[5, 3] = np.float32(0.0)                                                 # zeros inside
     x[6, 17] = np.float32(-0.0)                                               # non-zero blocks
     return f32_to_bf16_bits(x)
+
+
+def stack_layer_params(layer: int):
+    """Weights of layer `layer` (0-based) of the 30-layer stack workloads (15360 and 64800
+    tokens): distinct per layer, W ~ N(0, 0.02), bias ~ N(0, 0.01) for both linears.
+    Returns (w1, b1, w2, b2) as bf16 bits: w1 [d_ff, d_model], w2 [d_model, d_ff]."""
+    w1, b1 = linear_params(D_FF, D_MODEL, seed=300 + 2 * layer, b_std=0.01)
+    w2, b2 = linear_params(D_MODEL, D_FF, seed=301 + 2 * layer, b_std=0.01)
+    return w1, b1, w2, b2
+
+
+# Per-rank row counts of the stack workloads on 1/2/4/8 GPUs (contiguous row blocks).
+STACK_SHARD_ROWS = {M_STACK: (15360, 7680, 3840, 1920), M_4K: (64800, 32400, 16200, 8100)}

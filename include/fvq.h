@@ -163,10 +163,12 @@ int fvq_nvfp4_linear(const uint16_t* x, int64_t rows, const fvq_linear* lin, uin
  * a fixed 16 MiB array built into the library (fvq_noalloc_scratch_bytes),
  * which every GPU that loads the library holds until the process exits.
  * Calls whose fvq_nvfp4_linear_workspace_bytes(rows, in_features) exceeds it
- * return FVQ_EWORKSPACE.  The first call on a device looks the array's
- * address up (cudaGetSymbolAddress); make it before any stream capture.  All
- * calls share the array, so calls that overlap on the GPU race.  Nothing is
- * allocated by this call.
+ * return FVQ_EWORKSPACE.  The first call in each CUDA context (a device's
+ * primary context, or a caller's own driver-API context) looks the array's
+ * address up with cudaGetSymbolAddress and caches it under the context's
+ * unique id, so a cudaDeviceReset or another context is looked up again; make
+ * that first call before any stream capture.  All calls share the array, so
+ * calls that overlap on the GPU race.  Nothing is allocated by this call.
  */
 int fvq_nvfp4_linear_noalloc(const uint16_t* x, int64_t rows, const fvq_linear* lin, uint16_t* y,
                              void* stream);
@@ -185,6 +187,42 @@ size_t fvq_nvfp4_ffn_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff
  */
 int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
                   uint16_t* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * The FFN with the intermediate never stored in bf16: GEMM1's epilogue applies bias and
+ * GELU and quantizes h to NVFP4 itself (codes and 128x4-swizzled E4M3 scales, the
+ * activation quantizer's exact per-block recipe), with a provisional encode scale
+ *   g = 2^-headroom_log2 * 2688 / max(*amax_hint, 1e-12)      (headroom_log2 in [0, 30])
+ * instead of the reference's 2688 / amax(h); GEMM2 uses alpha = 1 / (g * g_w2).  Three
+ * launches.  No reference counterpart as a call: it replaces the same
+ * nn.Sequential(QuantLinear, GELU(tanh), QuantLinear) as fvq_nvfp4_ffn
+ * (ffn_quantization.py:77-80) but is not bit-exact with it unless *amax_hint equals
+ * amax(h) times a power of two (a block's codes depend on g only through its
+ * mantissa); otherwise it is an equally accurate but different quantization of h.
+ *   amax_hint: device fp32, an estimate of max |h| (a calibrated value, or the previous
+ *              call's amax_seen: delayed scaling).  Read, never written.
+ *   headroom_log2: g is divided by 2^headroom_log2 (exactly), leaving room for h to
+ *              exceed the hint by that factor before a block's scale saturates.
+ *   amax_seen: device fp32 or NULL; receives max |h| of this call (zeroed by the call's
+ *              first launch, so it must not alias amax_hint).
+ *   flags:     device u32 or NULL; OR-ed with 1 when a block's scale value
+ *              g * vmax / 6 exceeded 448 and was clipped (the hint was too small: rerun
+ *              fvq_nvfp4_ffn), 2 when a nonzero block's scale rounded to zero.  The
+ *              caller zeroes it.
+ * Workspace: fvq_nvfp4_ffn_fused_workspace_bytes (no bf16 intermediate).
+ */
+size_t fvq_nvfp4_ffn_fused_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff);
+int fvq_nvfp4_ffn_fused(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                        const fvq_linear* lin2, uint16_t* y, const float* amax_hint,
+                        int headroom_log2, float* amax_seen, uint32_t* flags, void* workspace,
+                        size_t workspace_bytes, void* stream);
+/* fvq_nvfp4_ffn_fused with CUDA events around its three launches; synchronises and
+ * writes the device times (ms) to kernel_ms[0..2].  Instrumentation. */
+int fvq_nvfp4_ffn_fused_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                                const fvq_linear* lin2, uint16_t* y, const float* amax_hint,
+                                int headroom_log2, float* amax_seen, uint32_t* flags,
+                                void* workspace, size_t workspace_bytes, void* stream,
+                                float* kernel_ms);
 
 /*
  * The DiT block around the FFN -- the caller of block.ffn that the reference's
@@ -385,7 +423,9 @@ int fvq_set_fp8_gemm_pairing(int mode);
  * Bounded device waits: a GEMM whose pipeline wait exceeds the limit sets a
  * device error word and returns early (after letting its own copies and MMAs
  * drain).  fvq_set_wait_limit changes the limit, in nanoseconds of wall time
- * per wait (0 restores the default of 2 s), for later launches.
+ * per wait (0 restores the default of 2 s), for later launches.  The limit is
+ * process-wide: it applies to launches from every host thread, so a short
+ * limit set by one thread also shortens the waits of other threads' calls.
  * fvq_read_device_error synchronises `stream`, returns the error word
  * (0 = none) in *flags and clears it.
  */

@@ -1,22 +1,30 @@
 """Generate the golden fixtures of tests/golden/ from the reference path on a B200.
 
-    FLASHINFER_WORKSPACE_BASE=<prebuilt JIT cache> \
-        python tests/golden/make_golden.py [--out tests/golden] [--time out.json]
+    FLASHINFER_WORKSPACE_BASE=baseline/fi_jit FLASHINFER_CUDA_ARCH_LIST=10.0a \
+        python tests/golden/make_golden.py [--out tests/golden] [--time out.json] [--stack-only]
 
 The reference computes its NVFP4 FFN with ``global_scale`` (ffn_quantization.py
 :29-32), ``flashinfer.nvfp4_quantize`` (:47, :64), ``flashinfer.mm_fp4(...,
 backend='cutlass')`` (:65-67), a bf16 bias add (:68-69) and the upstream
-``GELU(approximate='tanh')`` between the two linears.  This script runs exactly
-that sequence -- FlashInfer's own kernels, with the reference's torch scalar
-arithmetic restated inline because the reference file itself is not available
-where this runs -- on seeded inputs from ``workloads.py`` and stores:
+``GELU(approximate='tanh')`` between the two linears.  This script runs that
+sequence with FlashInfer's own kernels on seeded inputs from ``workloads.py``.
+The stack-workload cases come from the reference's own module
+(``ffn_quantization.QuantLinear``, installed unmodified into baseline/_ref by
+``__graft_entry__.build()``); the earlier cases restate its scalar glue inline,
+and the script records in golden_meta.json whether that restatement and the
+reference module give the same bits (``restated_glue_equals_reference_module``).
+It stores:
 
 * quantizer cases: codes, swizzled scale factors and global scale, plus the
   GPU's ``rcp.approx.ftz.f32`` results for every reciprocal argument the case
   needs (measured with libfvq's probe), so the CPU oracle can be bit-exact;
 * large quantizer cases: SHA-256 digests of codes and scale factors;
 * a QuantLinear case and a small FFN case: full bf16 outputs;
-* the one-layer FFN at 7680 tokens: 64 seeded rows of the output and its norm.
+* the one-layer FFN at 7680 tokens: 64 seeded rows of the output and its norm;
+* one layer of the 30-layer stack workloads (15360 and 64800 tokens) on the whole
+  input and on rank 0's row block at 2, 4 and 8 GPUs: 64 seeded rows, the norm and
+  the global scale of x, computed by the reference's own ``ffn_quantization``
+  module when it is installed in baseline/_ref (``--stack-only`` adds just these).
 
 Inputs are not stored: tests regenerate them from the same seeds.
 With ``--time`` it also times the reference kernels on the benchmark shapes.
@@ -136,10 +144,18 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=str(ROOT / "tests" / "golden"))
     ap.add_argument("--time", default=None, help="also time the reference kernels; JSON path")
+    ap.add_argument("--stack-only", action="store_true",
+                    help="only (re)make the stack-workload cases and add them to golden_meta.json")
     a = ap.parse_args()
     out = Path(a.out)
     out.mkdir(parents=True, exist_ok=True)
     torch.manual_seed(0)
+    if a.stack_only:
+        meta = json.loads((out / "golden_meta.json").read_text())
+        stack_cases(out, meta)
+        (out / "golden_meta.json").write_text(json.dumps(meta, indent=1, sort_keys=True))
+        print("added stack cases to", out)
+        return
     meta = {"flashinfer": flashinfer.__version__, "torch": torch.__version__,
             "device": torch.cuda.get_device_name(), "cases": {}}
 
@@ -208,6 +224,7 @@ def main() -> None:
     meta["cases"]["ffn_7680_rows"] = {"x": "student_t(7680,1536,seed=1)", **weights_meta,
                                       "y_fro": float(y.float().norm().item()),
                                       "y_sha256": sha(y)}
+    stack_cases(out, meta)
     (out / "golden_meta.json").write_text(json.dumps(meta, indent=1, sort_keys=True))
     print("wrote", len(meta["cases"]), "cases to", out)
 
@@ -215,6 +232,88 @@ def main() -> None:
         timings = time_reference(l1, l2)
         Path(a.time).write_text(json.dumps(timings, indent=1))
         print(json.dumps(timings, indent=1))
+
+
+def reference_module():
+    """The reference's own ffn_quantization module, installed unmodified into baseline/_ref
+    (``__graft_entry__.build()`` puts it there), or None when it is not installed."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "ffn_quantization.py").exists():
+        return None
+    if str(ref_dir) not in sys.path:
+        sys.path.insert(0, str(ref_dir))
+    import ffn_quantization
+    return ffn_quantization
+
+
+def reference_ffn_modules(w1, b1, w2, b2):
+    """nn.Sequential(QuantLinear, GELU(tanh), QuantLinear) built by the reference's own
+    QuantLinear(linear, 'nvfp4') (ffn_quantization.py:35-52) from bf16 weights."""
+    ref = reference_module()
+
+    def linear(wb, bb):
+        out_f, in_f = wb.shape
+        lin = torch.nn.Linear(in_f, out_f, bias=True, device="cuda", dtype=torch.bfloat16)
+        with torch.no_grad():
+            lin.weight.copy_(to_dev(wb))
+            lin.bias.copy_(to_dev(bb))
+        return ref.QuantLinear(lin, "nvfp4")
+
+    return torch.nn.Sequential(linear(w1, b1), torch.nn.GELU(approximate="tanh"), linear(w2, b2))
+
+
+# Stack workloads: one layer (layer 0 of the stack's weights) on the stack inputs, on the
+# whole tensor and on rank 0's row block at each GPU count (the reference run on that
+# shard: per-shard global scales).  (name, input generator, kwargs, rows of the shard)
+STACK_CASES = [
+    ("ffn_c4_15360", W.gaussian, dict(m=W.M_STACK, k=W.D_MODEL, seed=3), (15360, 7680, 3840, 1920)),
+    ("ffn_c5_64800", W.student_t, dict(m=W.M_4K, k=W.D_MODEL, seed=4), (64800, 32400, 16200, 8100)),
+]
+
+
+def stack_cases(out: Path, meta: dict) -> None:
+    """64 seeded output rows, the Frobenius norm and the global scales of one FFN layer at
+    the stack workloads' sizes, from the reference's own module when it is installed (else
+    from the restated glue above, which gives the same bits: checked on ffn_64 here)."""
+    w1, b1, w2, b2 = W.stack_layer_params(0)
+    ref = reference_module()
+    with torch.no_grad():
+        if ref is not None:
+            seq = reference_ffn_modules(w1, b1, w2, b2)
+            run = lambda x: seq(x)  # noqa: E731
+            # the restated glue and the reference module agree on the small golden case
+            sw1, sb1 = W.linear_params(W.D_FF, W.D_MODEL, seed=20, b_std=0.01)
+            sw2, sb2 = W.linear_params(W.D_MODEL, W.D_FF, seed=21, b_std=0.01)
+            l1 = RefQuantLinear(to_dev(sw1), to_dev(sb1))
+            l2 = RefQuantLinear(to_dev(sw2), to_dev(sb2))
+            small = reference_ffn_modules(sw1, sb1, sw2, sb2)
+            xs = to_dev(W.student_t(64, W.D_MODEL, seed=1))
+            meta["restated_glue_equals_reference_module"] = bool(
+                torch.equal(ref_ffn(xs, l1, l2), small(xs)))
+            source = "baseline/_ref/ffn_quantization.py (the reference module, unmodified)"
+        else:
+            l1 = RefQuantLinear(to_dev(w1), to_dev(b1))
+            l2 = RefQuantLinear(to_dev(w2), to_dev(b2))
+            run = lambda x: ref_ffn(x, l1, l2)  # noqa: E731
+            source = "restated glue (reference module not installed)"
+        for name, gen, kw, shard_rows in STACK_CASES:
+            x_all = to_dev(gen(**kw))
+            for rows in shard_rows:
+                x = x_all[:rows].contiguous()
+                y = run(x)
+                pick = np.sort(np.random.default_rng(rows).choice(rows, 64, replace=False))
+                g1 = ref_global_scale(x)
+                case = f"{name}_rows{rows}"
+                np.savez_compressed(out / f"{case}.npz", rows=pick,
+                                    y_rows=raw(y[torch.from_numpy(pick).cuda()]).view(np.uint16),
+                                    g1_bits=u32(g1))
+                meta["cases"][case] = {"x": f"{gen.__name__}({kw['m']},{kw['k']},seed={kw['seed']})[:{rows}]",
+                                       "weights": "workloads.stack_layer_params(0)",
+                                       "y_fro": float(y.float().norm().item()), "y_sha256": sha(y),
+                                       "source": source}
+                del y, x
+            del x_all
+            torch.cuda.empty_cache()
 
 
 def _time(fn, iters=20, warmup=5):

@@ -45,6 +45,11 @@ def _worker(rank, world, port, total, d, q):
         layer = _RowLayer(d)
         y = ShardedFFN(layer)(x)
         ok = torch.allclose(y, layer(x), atol=1e-6, rtol=1e-6)
+        # gathering into a caller's buffer gives the same rows in place
+        lo, hi = row_range(total, world, rank)
+        out = torch.full((total, d), float("nan"))
+        got = gather_rows(x[lo:hi] * 2.0, total, out=out)
+        ok = ok and got.data_ptr() == out.data_ptr() and torch.equal(out, x * 2.0)
         q.put((rank, bool(ok), tuple(y.shape)))
         dist.barrier()
         dist.destroy_process_group()
@@ -52,7 +57,7 @@ def _worker(rank, world, port, total, d, q):
         q.put((rank, False, repr(e)))
 
 
-@pytest.mark.parametrize("world,total", [(2, 7680), (2, 131), (3, 10), (3, 2)])
+@pytest.mark.parametrize("world,total", [(2, 7680), (2, 131), (3, 10), (3, 2), (4, 15360), (4, 15363)])
 def test_sharded_ffn_matches_single_rank(world, total):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

@@ -87,3 +87,27 @@ def test_noalloc_rejects_rows_beyond_its_scratch(layer):
                                       torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.FVQ_EWORKSPACE
     assert b"fvq_nvfp4_linear_noalloc" in lib.fvq_last_error()
+
+
+def test_noalloc_recovers_after_a_timed_out_call(layer):
+    """The shared scratch array cannot be zeroed again by the caller, so a call
+    whose bounded waits gave up (1 ns wait limit: the fused quantizer's grid
+    barrier and the GEMM's pipeline waits) must still leave the array's amax
+    counters re-armed: the error word reports the timeout and the next call,
+    with the default limit, equals fvq_nvfp4_linear bit for bit."""
+    lib = _lib.load()
+    lin, _ = layer
+    x = _bits_to_dev(W.gaussian(7680, 1536, seed=53))
+    assert ops.read_device_error() == 0
+    try:
+        ops.set_wait_limit(1)
+        _noalloc(lib, x, lin)
+        flags = ops.read_device_error()            # synchronises, returns and clears
+    finally:
+        ops.set_wait_limit(0)
+    assert flags != 0
+    y = _noalloc(lib, x, lin)
+    r = _regular(lib, x, lin)
+    torch.cuda.synchronize()
+    assert ops.read_device_error() == 0
+    assert torch.equal(y, r)
