@@ -86,10 +86,12 @@ def parse():
                     help="skip the separate measurements that follow the timed steps")
     ap.add_argument("--cpu-seconds", type=float, default=20.0,
                     help="wall-time budget of the CPU baseline sample")
-    ap.add_argument("--case", choices=("stack", "layer", "fp8_ffn", "pil_resize", "dit_block"),
+    ap.add_argument("--case", choices=("stack", "layer", "layer_fused", "fp8_ffn", "pil_resize",
+                                       "dit_block"),
                     default="stack",
-                    help="stack: the benchmark (default); layer: one fvq_nvfp4_ffn layer over "
-                         "--tokens rows, --steps calls (e.g. under a profiler); fp8_ffn / "
+                    help="stack: the benchmark (default); layer / layer_fused: one fvq_nvfp4_ffn / "
+                         "fvq_nvfp4_ffn_fused layer over --tokens rows, --steps calls (e.g. under "
+                         "a profiler); fp8_ffn / "
                          "pil_resize / dit_block: only that separate measurement, one JSON line")
     return ap.parse_args()
 
@@ -1121,16 +1123,32 @@ def flashinfer_comparison(torch, ops, lib, dev, stream, weights, run) -> dict:
     return res
 
 
-def layer_case(torch, ops, lib, dev, stream, tokens, steps) -> dict:
-    """One fvq_nvfp4_ffn call (layer 0 of the stack) over the first `tokens` rows of the
-    stack input, `steps` times: the launch sequence a profiler capture looks at."""
+def layer_case(torch, ops, lib, dev, stream, tokens, steps, fused=False) -> dict:
+    """One FFN call (layer 0 of the stack) over the first `tokens` rows of the stack input,
+    `steps` times: the launch sequence a profiler capture looks at.  fused: the call is
+    fvq_nvfp4_ffn_fused (GEMM1 quantizes h; estimate of max |h| 4.0, one bit of headroom)
+    instead of fvq_nvfp4_ffn."""
     weights = StackWeights(torch, ops, dev, layers=1)
     wl = STACK_WORKLOADS["c4" if tokens <= STACK_WORKLOADS["c4"]["total"] else "c5"]
     run = StackRun(torch, lib, dev, stream, weights, dict(wl, total=tokens), 1, 0)
-    for _ in range(steps):
-        run.layers()
+    if not fused:
+        for _ in range(steps):
+            run.layers()
+    else:
+        l1, l2 = run.structs[0]
+        hint = torch.full((1,), 4.0, dtype=torch.float32, device=dev)
+        seen = torch.zeros(1, dtype=torch.float32, device=dev)
+        flags = torch.zeros(1, dtype=torch.int32, device=dev)
+        nbytes = lib.fvq_nvfp4_ffn_fused_workspace_bytes(tokens, D_MODEL, D_FF)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        for _ in range(steps):
+            rc = lib.fvq_nvfp4_ffn_fused(run.x.data_ptr(), tokens, ctypes.byref(l1), ctypes.byref(l2),
+                                         run.bufs[0].data_ptr(), hint.data_ptr(), 1, seen.data_ptr(),
+                                         flags.data_ptr(), ws.data_ptr(), nbytes, run.sptr)
+            if rc != 0:
+                raise RuntimeError(lib.fvq_last_error().decode())
     torch.cuda.synchronize(dev)
-    return {"tokens": tokens, "calls": steps}
+    return {"tokens": tokens, "calls": steps, "fused": fused}
 
 
 def measured_peaks() -> dict:
@@ -1160,8 +1178,9 @@ def main():
     peaks = measured_peaks()
     hbm = peaks.get("hbm_gbs") or 6650.0
     if args.case != "stack":
-        if args.case == "layer":
-            out = layer_case(torch, ops, lib, dev, stream, args.tokens, args.steps)
+        if args.case in ("layer", "layer_fused"):
+            out = layer_case(torch, ops, lib, dev, stream, args.tokens, args.steps,
+                             fused=args.case == "layer_fused")
         elif args.case == "fp8_ffn":
             peak8 = 2.0 * (peaks.get("bf16_tflops_sustained") or 1400.0)
             out = fp8_mode_timing(torch, ops, lib, dev, stream, args.tokens, peak8, steps=args.steps)

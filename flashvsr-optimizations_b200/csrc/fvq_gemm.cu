@@ -55,15 +55,17 @@ constexpr int kBarrierBytes = 256;
 constexpr int kStagingBytes = BM * BN * 2;       // bf16 tile staged for coalesced stores
 
 // GELU of a bf16 input is a function of 16 bits.  Inputs with exponent field
-// in [115, 130) (|x| in [2^-12, 8)) are tabulated per CTA in shared memory
-// (computed with the exact fp32 formula at kernel start); all other inputs
-// take the exact formula directly.  Entry index: (sign << 11) | ((bits &
-// 0x7FFF) - 0x3980), so the sign is one shifted bit of the input (indices
-// 0x780..0x7FF of each half are unused).
-constexpr uint32_t kGeluTabLo = 115u << 7;       // 0x3980 = 2^-12
-constexpr uint32_t kGeluTabSpan = 15u << 7;      // 0x780: magnitudes below 8.0
-constexpr int kGeluTabEntries = 4096;
+// in [107, 130) (|x| in [2^-20, 8)) are tabulated per CTA in shared memory
+// (computed with the exact fp32 formula at kernel start); the rest take short
+// exact paths (gelu_bf16).  The range reaches down to 2^-20 because the
+// intermediate of a deep stack is small: its pre-activations shrink to a
+// standard deviation near 0.02, where 1% of them lie below 2^-12.  Entry
+// index: ((bits & 0x7FFF) - 0x3580) + sign * 2944, 2 x 2944 entries (11.5 KB).
+constexpr uint32_t kGeluTabLo = 107u << 7;       // 0x3580 = 2^-20
+constexpr uint32_t kGeluTabSpan = 23u << 7;      // 0xB80: magnitudes below 8.0
+constexpr int kGeluTabEntries = 2 * kGeluTabSpan;
 constexpr int kGeluTabBytes = kGeluTabEntries * 2;
+static_assert(kGeluTabBytes % 16 == 0, "table keeps what follows it 16-byte aligned");
 constexpr int kStageRowBytes = 128;              // one epilogue row: 64 bf16 columns
 constexpr int kWarpStagingBytes = 32 * kStageRowBytes;
 
@@ -73,7 +75,7 @@ constexpr int kWarpStagingBytes = 32 * kStageRowBytes;
 // K tile), moved to TMEM with four 128x256b copies instead of eight
 // 32x128b.warpx4 copies.
 // kEpi 3 (GEMM1 quantizing its own output) writes NVFP4 codes and scales straight
-// from registers: it needs no staging buffer, so four stages fit, and in resident mode
+// from registers: it needs no staging buffer, so four resident stages fit, and in resident mode
 // the W scales are preloaded through the last stage's buffer (kPreloadInStage: the
 // producer fills that stage only after the MMA warp's copies out of it completed).
 template <int kEpi, bool kResident, bool kRepSfb = false>
@@ -81,7 +83,7 @@ struct Plan {
   static constexpr int kStageBytes =
       kABytes + kBBytes + kSfaBytes + (kResident ? 0 : (kRepSfb ? kSfbRepBytes : kSfbBytes));
   static constexpr int kStages =
-      kEpi == 3 ? 4 : (kEpi != 1 ? (kRepSfb ? 3 : 4) : (kResident ? 3 : 2));
+      kEpi == 3 ? (kResident ? 4 : 3) : (kEpi != 1 ? (kRepSfb ? 3 : 4) : (kResident ? 3 : 2));
   static constexpr bool kStaged = kEpi == 1;
   static constexpr bool kGelu = kEpi == 1 || kEpi == 3;
   static constexpr bool kPreloadInStage = kResident && !kStaged;
@@ -167,10 +169,9 @@ __device__ __noinline__ uint32_t gelu_bf16_exact(uint32_t x_bits) {
 
 __device__ __forceinline__ void gelu_table_init(uint16_t* tab, int tid, int nthreads) {
   for (int i = tid; i < kGeluTabEntries; i += nthreads) {
-    const uint32_t off = static_cast<uint32_t>(i) & 0x7FFu;
-    const uint32_t sign = (static_cast<uint32_t>(i) & 0x800u) << 4;
-    tab[i] = off < kGeluTabSpan ? static_cast<uint16_t>(gelu_bf16_exact(sign | (kGeluTabLo + off)))
-                                : static_cast<uint16_t>(0);
+    const uint32_t neg = static_cast<uint32_t>(i) >= kGeluTabSpan ? 1u : 0u;
+    const uint32_t off = static_cast<uint32_t>(i) - neg * kGeluTabSpan;
+    tab[i] = static_cast<uint16_t>(gelu_bf16_exact((neg << 15) | (kGeluTabLo + off)));
   }
 }
 
@@ -191,7 +192,7 @@ __device__ __forceinline__ uint32_t gelu_bf16_tiny(uint32_t x_bits) {
 __device__ __forceinline__ uint32_t gelu_bf16(uint32_t x_bits, const uint16_t* tab) {
   const uint32_t mag = x_bits & 0x7FFFu;
   const uint32_t off = mag - kGeluTabLo;
-  if (off < kGeluTabSpan) return tab[off | ((x_bits & 0x8000u) >> 4)];
+  if (off < kGeluTabSpan) return tab[off + ((x_bits >> 15) & 1u) * kGeluTabSpan];
   if (mag < kGeluTabLo) return gelu_bf16_tiny(x_bits);
   if (mag < 0x7F80u) return (x_bits & 0x8000u) ? 0x8000u : x_bits;
   if (x_bits == 0x7F80u) return x_bits;
@@ -222,10 +223,10 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
 
 // GELU of four bf16x2 words.  Per word both magnitude offsets are formed in one
 // 32-bit subtraction and clamped to the last entry in one min.u16x2, so the two
-// lookups stay inside the table whatever the input; the sign is bit 11 of the
-// index.  There is no branch between the eight lookups, so all can be in flight
-// at once; a word with a half that was clamped (outside [2^-12, 8), or a borrow
-// from the low half) is redone on the exact path afterwards.  tab_base is the
+// lookups stay inside the table whatever the input; a negative half adds the
+// table's span to its index.  There is no branch between the eight lookups, so all
+// can be in flight at once; a word with a half that was clamped (outside
+// [2^-20, 8), or a borrow from the low half) is redone through gelu_bf16 afterwards.  tab_base is the
 // table's shared-memory address.
 __device__ __forceinline__ void gelu_bf16x2_x4(uint32_t (&w)[4], uint32_t tab_base,
                                                const uint16_t* tab) {
@@ -235,7 +236,7 @@ __device__ __forceinline__ void gelu_bf16x2_x4(uint32_t (&w)[4], uint32_t tab_ba
   for (int j = 0; j < 4; ++j) {
     const uint32_t d = (w[j] & 0x7FFF7FFFu) - ((kGeluTabLo << 16) | kGeluTabLo);
     const uint32_t c = min_u16x2(d, ((kGeluTabSpan - 1) << 16) | (kGeluTabSpan - 1));
-    const uint32_t off2 = (c << 1) | ((w[j] >> 3) & 0x10001000u);
+    const uint32_t off2 = (c + ((w[j] >> 15) & 0x00010001u) * kGeluTabSpan) << 1;
     res[j] = __byte_perm(lds_u16(tab_base + (off2 & 0xFFFFu)), lds_u16(tab_base + (off2 >> 16)),
                          0x5410);
     slow |= static_cast<uint32_t>(c != d) << j;
@@ -384,10 +385,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // programmatic dependent launch: the next kernel may start its prologue; the roles
+  // below wait for the previous kernel before they touch global memory
+  if (threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     // (the whole warp runs the loop; one elected lane issues the copies)
+    grid_dependency_wait();
     if (seq.count > 0) {
       bool sfb_armed = false;
       uint8_t* preload = P::kPreloadInStage ? smem + (kStages - 1) * kStageBytes : staging;
@@ -581,6 +586,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       gelu_table_init(gelu_tab, threadIdx.x - 64, kEpiThreads);
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
     }
+    grid_dependency_wait();
     // kEpi 3: the intermediate's provisional encode scale and its loop invariants
     float gq = 0.0f, r6 = 0.0f, rgq = 0.0f;
     uint32_t qflags = 0;
@@ -831,7 +837,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t rank = cluster_ctarank();
   const bool even = rank == 0;
   const int pairs = gridDim.x / 2, pair = blockIdx.x / 2;
-  const int num_m_pairs = m / (2 * BM);
+  // ragged m: the last pair tile may hold fewer than 256 rows; a CTA whose 128 rows lie
+  // wholly past m loads the last valid row block instead (so every TMA box starts inside
+  // A) and stores nothing
+  const int num_m_pairs = (m + 2 * BM - 1) / (2 * BM);
+  const int num_m_blocks = (m + BM - 1) / BM;
   const int num_n_blocks = n / BN;
   const int tiles = num_m_pairs * num_n_blocks;
   const int count = pair < tiles ? (tiles - 1 - pair) / pairs + 1 : 0;  // same in both CTAs
@@ -864,10 +874,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem = bars->tmem_base;
   const auto even_addr = [&](const void* p) { return mapa_shared(smem_u32(p), 0); };
   const auto odd_addr = [&](const void* p) { return mapa_shared(smem_u32(p), 1); };
+  if (threadIdx.x == 0) grid_launch_dependents();  // as in nvfp4_gemm_kernel
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
     // (the whole warp runs the loop; one elected lane issues the copies)
+    grid_dependency_wait();
     if (count > 0) {
       uint32_t armed[kPairStages];
 #pragma unroll
@@ -877,7 +889,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       for (int i = 0; i < count && !warp_aborted(bars); ++i) {
         const int t = pair + i * pairs;
         const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
-        const int a_block = 2 * mbp + static_cast<int>(rank);  // this CTA's 128 rows
+        const int a_block = min(2 * mbp + static_cast<int>(rank), num_m_blocks - 1);  // its rows
         for (int kt = 0; kt < num_k_tiles; ++kt) {
           if (!warp_wait_cluster_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
             warp_flag_error(bars, kErrWaitProducer);
@@ -1000,6 +1012,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const int quarter = (warp - 2) >> 2;
     const int col_base = quarter * 64;
     const int trow = quad * 32 + lane;
+    grid_dependency_wait();
     const float alpha = __frcp_rn(__fmul_rn(*g_a, *g_w));
     uint64_t alpha2;
     asm("mov.b64 %0, {%1, %1};" : "=l"(alpha2) : "f"(alpha));
@@ -1740,10 +1753,20 @@ cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CU
   const int tiles = ((m + BM - 1) / BM) * (n / BN);
   int grid = sm_count();
   if (grid > tiles) grid = tiles;
-  nvfp4_gemm_kernel<kEpi, kResident, kRepSfb><<<grid, kNumThreads, kSmemBytes, st>>>(
-      ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit, residual,
-      gate, qo);
-  return cudaGetLastError();
+  // programmatic dependent launch (the kernel waits for its predecessor itself)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kNumThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, nvfp4_gemm_kernel<kEpi, kResident, kRepSfb>, ma, mb, mo, a_sf,
+                            w_sf, g_a, g_w, alpha, bias, out, m, n, k, amax_out, wait_limit,
+                            residual, gate, qo);
 }
 
 // 3-D maps over 512-byte scale atoms (128 x u32): A scales [blocks][k/64 atoms][128],
@@ -1797,7 +1820,7 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
           attr_done, reinterpret_cast<const void*>(nvfp4_gemm_pair_kernel<kEpi, kRawSfb>),
           PairPlan<kRawSfb>::kSmemBytes))
     return e;
-  const int tiles = (m / (2 * BM)) * (n / BN);
+  const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * (n / BN);
   int pairs = sm_count() / 2;
   if (pairs > tiles) pairs = tiles;
   cudaLaunchConfig_t cfg = {};
@@ -1805,13 +1828,15 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
   cfg.blockDim = dim3(kNumThreads);
   cfg.dynamicSmemBytes = PairPlan<kRawSfb>::kSmemBytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, nvfp4_gemm_pair_kernel<kEpi, kRawSfb>, ma, mb_half, msfa, msfb,
                             g_a, g_w, bias, out, m, n, k, wait_limit, residual, gate);
 }
@@ -1911,8 +1936,9 @@ cudaError_t launch_fp8_gemm(const uint8_t* a, const float* sa, const uint8_t* w,
 // the power cap under sustained tensor load).
 static int g_pairing = 1;  // SM pairs with W scales in the library layout
 void set_gemm_pairing(int mode) { g_pairing = mode; }
-bool gemm_pairs(int64_t m, int epilogue) { return g_pairing != 0 && epilogue == 0 && m % (2 * BM) == 0; }
-bool gemm_pairs_raw_scales(int64_t m) { return g_pairing == 1 && m % (2 * BM) == 0; }
+// Any m: a ragged last pair tile is handled in the kernel (see nvfp4_gemm_pair_kernel).
+bool gemm_pairs(int64_t m, int epilogue) { return g_pairing != 0 && epilogue == 0 && m > 0; }
+bool gemm_pairs_raw_scales(int64_t m) { return g_pairing == 1 && m > 0; }
 
 cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
@@ -1965,7 +1991,7 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
       alignas(64) CUtensorMap msfa;
       alignas(64) CUtensorMap msfb;
       if (!make_code_map(&mb_half, w_codes, n, k, BN / 2) ||
-          !make_scale_maps(&msfa, &msfb, a_sf, m / BM, w_sf, false, n, k)) {
+          !make_scale_maps(&msfa, &msfb, a_sf, (m + BM - 1) / BM, w_sf, false, n, k)) {
         if (why) *why = "cuTensorMapEncodeTiled failed for the SM-pair GEMM";
         return cudaErrorInvalidValue;
       }
@@ -1989,7 +2015,8 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
     alignas(64) CUtensorMap msfa;
     alignas(64) CUtensorMap msfb;
     if (!make_code_map(&mb_half, w_codes, n, k, BN / 2) ||
-        !make_scale_maps(&msfa, &msfb, a_sf, m / BM, pair_rep ? w_sf_rep : w_sf, pair_rep, n, k)) {
+        !make_scale_maps(&msfa, &msfb, a_sf, (m + BM - 1) / BM, pair_rep ? w_sf_rep : w_sf, pair_rep,
+                         n, k)) {
       if (why) *why = "cuTensorMapEncodeTiled failed for the SM-pair GEMM";
       return cudaErrorInvalidValue;
     }

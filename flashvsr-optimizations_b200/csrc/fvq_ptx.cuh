@@ -442,6 +442,20 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo,
   return d;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with cudaLaunchAttributeProgrammaticStreamSerialization may start
+// while the kernel before it in the stream is still finishing; grid_dependency_wait()
+// returns once that kernel has completed and its memory operations are visible, so every
+// thread waits before it touches global memory the previous kernel may write or read.
+// grid_launch_dependents() lets the next such kernel start launching once every CTA of
+// this grid has called it (or exited).
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- numerics
 __device__ __forceinline__ float rcp_approx_ftz(float a) {
   float b;

@@ -249,6 +249,9 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(
     const uint16_t* __restrict__ x, uint32_t rows, uint32_t bpr, const float* __restrict__ g_ptr,
     const float* __restrict__ amax_ptr, float* g_out, uint8_t* __restrict__ codes,
     uint8_t* __restrict__ sf, float* zero_word, Div31 div) {
+  // launched as a programmatic dependent of the GEMM that wrote x
+  grid_launch_dependents();
+  grid_dependency_wait();
   const float g = amax_ptr != nullptr ? encode_scale(*amax_ptr) : *g_ptr;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     if (g_out != nullptr) *g_out = g;
@@ -346,6 +349,7 @@ __global__ void __launch_bounds__(kThreads) amax_quantize_kernel(
     uint4* __restrict__ rep_dst, uint64_t wait_limit, uint32_t* err_word, Div31 div) {
   __shared__ uint32_t warp_max[kThreads / 32];
   __shared__ int go;
+  grid_launch_dependents();  // the GEMM that follows may start its prologue
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kThreads;
   uint32_t gen = 0;
@@ -443,14 +447,20 @@ cudaError_t launch_quantize(const uint16_t* x, int64_t rows, int64_t k, const fl
   const Div31 div = make_div31(static_cast<uint32_t>(k / 16));
   const uint32_t r = static_cast<uint32_t>(rows), bpr = static_cast<uint32_t>(k / 16);
   // the discard works on whole 128-byte lines
-  if (scratch_input && (reinterpret_cast<uintptr_t>(x) & 127) == 0) {
-    quantize_kernel<true, true><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
-        x, r, bpr, g, amax, g_out, codes, sf, zero_word, div);
-  } else {
-    quantize_kernel<false, false><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
-        x, r, bpr, g, amax, g_out, codes, sf, zero_word, div);
-  }
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (scratch_input && (reinterpret_cast<uintptr_t>(x) & 127) == 0)
+    return cudaLaunchKernelEx(&cfg, quantize_kernel<true, true>, x, r, bpr, g, amax, g_out, codes,
+                              sf, zero_word, div);
+  return cudaLaunchKernelEx(&cfg, quantize_kernel<false, false>, x, r, bpr, g, amax, g_out, codes,
+                            sf, zero_word, div);
 }
 
 cudaError_t launch_replicate_w_scales(const uint8_t* sf, int64_t n, int64_t k, uint8_t* rep,
@@ -563,6 +573,7 @@ __global__ void __launch_bounds__(kThreads, kVec >= 8 ? 2 : 3) amax_quantize_ln_
     uint4* __restrict__ rep_dst, uint64_t wait_limit, uint32_t* err_word, Div31 div) {
   __shared__ uint32_t warp_max[kThreads / 32];
   __shared__ int go;
+  grid_launch_dependents();  // the GEMM that follows may start its prologue
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kThreads;
   const int lane = threadIdx.x & 31;
