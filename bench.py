@@ -86,13 +86,16 @@ def parse():
                     help="skip the separate measurements that follow the timed steps")
     ap.add_argument("--cpu-seconds", type=float, default=20.0,
                     help="wall-time budget of the CPU baseline sample")
-    ap.add_argument("--case", choices=("stack", "layer", "layer_fused", "fp8_ffn", "pil_resize",
-                                       "dit_block"),
+    ap.add_argument("--case", choices=("stack", "shard", "layer", "layer_fused", "fp8_ffn",
+                                       "pil_resize", "dit_block"),
                     default="stack",
-                    help="stack: the benchmark (default); layer / layer_fused: one fvq_nvfp4_ffn / "
-                         "fvq_nvfp4_ffn_fused layer over --tokens rows, --steps calls (e.g. under "
-                         "a profiler); fp8_ffn / "
+                    help="stack: the benchmark (default); shard: the stack on rank 0's row block "
+                         "of a --shard-of N split, on this GPU alone (no collective); layer / "
+                         "layer_fused: one fvq_nvfp4_ffn / fvq_nvfp4_ffn_fused layer over --tokens "
+                         "rows, --steps calls (e.g. under a profiler); fp8_ffn / "
                          "pil_resize / dit_block: only that separate measurement, one JSON line")
+    ap.add_argument("--shard-of", type=int, default=8,
+                    help="--case shard: the number of ranks whose first row block is run")
     return ap.parse_args()
 
 
@@ -267,9 +270,10 @@ class StackWeights:
 
 
 class StackRun:
-    """The stack on this rank's row block: one fvq_nvfp4_ffn call per layer (four launches,
-    ping-pong activation buffers, one workspace), then (N > 1) the NCCL all-gather of the
-    last layer's rows into the full output."""
+    """The stack on this rank's row block: one fvq_nvfp4_ffn_chain call per layer (four
+    launches, ping-pong activation buffers, one workspace; each layer hands the next the
+    max |y| of its output, so only layer 0 runs the amax pass over its input), then (N > 1)
+    the NCCL all-gather of the last layer's rows into the full output."""
 
     def __init__(self, torch, lib, dev, stream, weights, wl, world, rank):
         from flashvsr_optimizations_b200.sharding import row_range
@@ -281,24 +285,29 @@ class StackRun:
         self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=dev)
         self.bufs = [torch.empty(self.rows, D_MODEL, dtype=torch.bfloat16, device=dev)
                      for _ in range(2)]
+        self.amax = torch.zeros(2, dtype=torch.float32, device=dev)   # max |y|, ping-pong
         self.out = (torch.empty(self.total, D_MODEL, dtype=torch.bfloat16, device=dev)
                     if world > 1 else None)
         self.lib, self.sptr, self.structs, self.world = lib, stream.cuda_stream, weights.structs, world
 
     def layers(self, profile: list | None = None):
         """The 30 layers on this rank's rows; with `profile`, each layer runs through
-        fvq_nvfp4_ffn_profile (events around its four launches, one host wait per layer)
-        and appends the four device times (ms)."""
+        fvq_nvfp4_ffn_chain_profile (events around its four launches, one host wait per
+        layer) and appends the four device times (ms)."""
         cur = self.x
+        last = len(self.structs) - 1
+        a0, a1 = self.amax.data_ptr(), self.amax.data_ptr() + 4
         for i, (l1, l2) in enumerate(self.structs):
             out = self.bufs[i % 2]
+            x_amax = None if i == 0 else (a0, a1)[(i - 1) % 2]
+            y_amax = None if i == last else (a0, a1)[i % 2]
             args = (cur.data_ptr(), self.rows, ctypes.byref(l1), ctypes.byref(l2), out.data_ptr(),
-                    self.ws.data_ptr(), self.ws_bytes, self.sptr)
+                    x_amax, y_amax, self.ws.data_ptr(), self.ws_bytes, self.sptr)
             if profile is None:
-                rc = self.lib.fvq_nvfp4_ffn(*args)
+                rc = self.lib.fvq_nvfp4_ffn_chain(*args)
             else:
                 ms = (ctypes.c_float * 4)()
-                rc = self.lib.fvq_nvfp4_ffn_profile(*args, ms)
+                rc = self.lib.fvq_nvfp4_ffn_chain_profile(*args, ms)
                 profile.append(list(ms))
             if rc != 0:
                 raise RuntimeError(self.lib.fvq_last_error().decode())
@@ -371,12 +380,14 @@ def stack_kernel_timing(torch, dist, dev, world, run, passes) -> dict:
 
 def stack_e2e(torch, dist, weights, run, dev, world, rank, steps, warmup) -> dict:
     """The stack through the public API with host buffers: per step every rank uploads its
-    rows from pinned host memory, runs the 30 NVFP4FFN modules (torch custom op
-    fvq::nvfp4_ffn), all-gathers with sharding.gather_rows, and rank 0 copies the gathered
-    [total, 1536] output to pinned host memory.  Uploads, compute and the download run on
-    three streams, double-buffered, so one step's copies overlap its neighbours' compute."""
+    rows from pinned host memory, runs the 30 NVFP4FFN modules as an NVFP4FFNStack (torch
+    custom op fvq::nvfp4_ffn_chain), all-gathers with sharding.gather_rows, and rank 0 copies
+    the gathered [total, 1536] output to pinned host memory.  Uploads, compute and the
+    download run on three streams, double-buffered, so one step's copies overlap its
+    neighbours' compute."""
+    from flashvsr_optimizations_b200.ffn_quantization import NVFP4FFNStack
     from flashvsr_optimizations_b200.sharding import gather_rows
-    mods = weights.modules(torch)
+    stack = NVFP4FFNStack(weights.modules(torch))
     xh = run.x.cpu().pin_memory()
     xd = [torch.empty_like(run.x) for _ in range(2)]
     out_rows = run.total if world > 1 else run.rows
@@ -401,9 +412,7 @@ def stack_e2e(torch, dist, weights, run, dev, world, rank, steps, warmup) -> dic
             up.record(s_up)
         with torch.cuda.stream(s_cmp):
             s_cmp.wait_event(up)
-            y = xd[b]
-            for m in mods:
-                y = m(y)
+            y = stack(xd[b])
             if world > 1:
                 s_cmp.wait_event(done_down[b])
                 y = gather_rows(y, run.total, out=outs[b])
@@ -437,7 +446,8 @@ def stack_e2e(torch, dist, weights, run, dev, world, rank, steps, warmup) -> dic
     return {"value": run.total * steps / (ms * 1e-3), "unit": "tokens/s",
             "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
             "steps": steps, "ms_per_step": ms / steps,
-            "api": "30 NVFP4FFN modules (torch custom op fvq::nvfp4_ffn) + sharding.gather_rows; "
+            "api": "NVFP4FFNStack of 30 NVFP4FFN modules (torch custom op fvq::nvfp4_ffn_chain) + "
+                   "sharding.gather_rows; "
                    "each rank uploads its rows, rank 0 downloads the gathered output; "
                    "three streams, double-buffered"}
 
@@ -1151,6 +1161,24 @@ def layer_case(torch, ops, lib, dev, stream, tokens, steps, fused=False) -> dict
     return {"tokens": tokens, "calls": steps, "fused": fused}
 
 
+def shard_case(torch, dist, ops, lib, dev, stream, wl, shard_of, steps, warmup) -> dict:
+    """The 30-layer stack on rank 0's row block of a `shard_of`-way split, on this GPU alone
+    and without the all-gather: the per-rank compute of the N-GPU benchmark, measured on one
+    GPU (device time of `steps` stacks, and the per-launch times of one more pass)."""
+    from flashvsr_optimizations_b200.sharding import row_range
+    weights = StackWeights(torch, ops, dev)
+    run = StackRun(torch, lib, dev, stream, weights, wl, 1, 0)
+    r0, r1 = row_range(wl["total"], shard_of, 0)
+    run.rows = r1 - r0
+    run.x = run.x[:run.rows].contiguous()
+    run.bufs = [b[:run.rows] for b in run.bufs]
+    ms = timed_steps(torch, dist, dev, stream, 1, lambda i: run.layers(), steps, warmup) / steps
+    kt = stack_kernel_timing(torch, dist, dev, 1, run, passes=2)
+    return {"workload": wl["name"], "shard_of": shard_of, "rows": run.rows, "ms_per_stack": ms,
+            "tokens_per_s": run.rows / (ms * 1e-3),
+            "tflops": run.rows * LAYERS * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12, "kernels_ms": kt}
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -1178,7 +1206,10 @@ def main():
     peaks = measured_peaks()
     hbm = peaks.get("hbm_gbs") or 6650.0
     if args.case != "stack":
-        if args.case in ("layer", "layer_fused"):
+        if args.case == "shard":
+            out = shard_case(torch, dist, ops, lib, dev, stream, STACK_WORKLOADS[args.workload],
+                             args.shard_of, args.steps, args.warmup)
+        elif args.case in ("layer", "layer_fused"):
             out = layer_case(torch, ops, lib, dev, stream, args.tokens, args.steps,
                              fused=args.case == "layer_fused")
         elif args.case == "fp8_ffn":

@@ -79,6 +79,8 @@ SIGNATURES = {
     "fvq_nvfp4_ffn_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "fvq_nvfp4_ffn": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _c.POINTER(FvqLinear), _vp,
                                  _vp, _sz, _vp]),
+    "fvq_nvfp4_ffn_chain": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _c.POINTER(FvqLinear),
+                                       _vp, _vp, _vp, _vp, _sz, _vp]),
     "fvq_nvfp4_ffn_block_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "fvq_ln_modulate": (_c.c_int, [_vp, _i64, _i64, _vp, _vp, _c.c_float, _vp, _vp]),
     "fvq_nvfp4_ffn_block": (_c.c_int, [_vp, _i64, _vp, _vp, _vp, _c.c_float, _c.POINTER(FvqLinear),
@@ -86,6 +88,9 @@ SIGNATURES = {
     "fvq_nvfp4_ffn_profile": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear),
                                          _c.POINTER(FvqLinear), _vp, _vp, _sz, _vp,
                                          _c.POINTER(_c.c_float)]),
+    "fvq_nvfp4_ffn_chain_profile": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear),
+                                               _c.POINTER(FvqLinear), _vp, _vp, _vp, _vp, _sz, _vp,
+                                               _c.POINTER(_c.c_float)]),
     "fvq_nvfp4_ffn_fused_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "fvq_nvfp4_ffn_fused": (_c.c_int, [_vp, _i64, _c.POINTER(FvqLinear), _c.POINTER(FvqLinear),
                                        _vp, _vp, _c.c_int, _vp, _vp, _vp, _sz, _vp]),

@@ -35,6 +35,7 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(FVQ_ECUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 // the quantizer reads bf16 inputs in 32-byte vectors
 bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
@@ -212,7 +213,8 @@ int fvq_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a
     return fail(FVQ_EALIGN, "fvq_nvfp4_gemm: operands, scales, bias and out must be 16-byte aligned");
   if (int rc = check_device()) return rc;
   return gemm_impl(a_codes, a_sf, g_a, w_codes, w_sf, g_w, nullptr, bias, out, m, n, k, epilogue,
-                   amax_out, static_cast<cudaStream_t>(stream));
+                   epilogue == FVQ_EPI_GELU_AMAX ? amax_out : nullptr,
+                   static_cast<cudaStream_t>(stream));
 }
 
 size_t fvq_w_scales_replicated_bytes(int64_t n, int64_t k) {
@@ -335,7 +337,9 @@ namespace {
 // The FFN launch sequence.  ev: NULL, or 5 events recorded before the first
 // launch and after each of the four (for fvq_nvfp4_ffn_profile).  residual and
 // gate (both or neither): GEMM2 writes the gated residual residual + gate * FFN(x).
-// The DiT block's input step, applied to x inside the first launch.
+// x_amax (optional): max |x| given, so the first launch only quantizes x; y_amax
+// (optional): receives max |y| from GEMM2's epilogue (fvq_nvfp4_ffn_chain).
+// LnModulate: the DiT block's input step, applied to x inside the first launch.
 struct LnModulate {
   const uint16_t* shift;
   const uint16_t* scale;
@@ -346,7 +350,8 @@ struct LnModulate {
 int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_linear* lin2,
              uint16_t* y, void* workspace, size_t workspace_bytes, cudaStream_t st,
              cudaEvent_t* ev, const uint16_t* residual = nullptr, const uint16_t* gate = nullptr,
-             const LnModulate* ln = nullptr) {
+             const LnModulate* ln = nullptr, const float* x_amax = nullptr,
+             float* y_amax = nullptr) {
   if (int rc = check_linear(lin1, "fvq_nvfp4_ffn (linear 1)")) return rc;
   if (int rc = check_linear(lin2, "fvq_nvfp4_ffn (linear 2)")) return rc;
   if (lin1->out_features != lin2->in_features || lin2->out_features != lin1->in_features)
@@ -385,19 +390,37 @@ int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_
   //    accumulates into it and, when GEMM2 runs on one SM per tile, writes the W2
   //    scales in the layout of its 128x256b scale copies
   //    (for the DiT block: of u = LN(x) * (1 + scale) + shift, computed on the fly)
-  cudaError_t e =
-      ln == nullptr
-          ? fvq::launch_amax_quantize(x, rows, d, g_x, codes_x, sf_x, amax_ws, amax_h, lin2->scale,
-                                      d, f, sf_w2_rep, wait_limit(), fvq::error_word_ptr(), st)
-          : fvq::launch_amax_quantize_ln(x, rows, d, ln->shift, ln->scale, ln->eps, ln->stats, g_x,
-                                         codes_x, sf_x, amax_ws, amax_h, lin2->scale, d, f,
-                                         sf_w2_rep, wait_limit(), fvq::error_word_ptr(), st);
+  //    (with x_amax given: a plain quantize of x with g_x from it, and the W2 scale copy, if
+  //    needed, as a launch of its own)
+  cudaError_t e = cudaSuccess;
+  if (ln != nullptr) {
+    e = fvq::launch_amax_quantize_ln(x, rows, d, ln->shift, ln->scale, ln->eps, ln->stats, g_x,
+                                     codes_x, sf_x, amax_ws, amax_h, lin2->scale, d, f, sf_w2_rep,
+                                     wait_limit(), fvq::error_word_ptr(), st);
+  } else if (x_amax != nullptr) {
+    e = fvq::launch_quantize(x, rows, d, nullptr, x_amax, g_x, codes_x, sf_x, amax_h, st);
+    if (e == cudaSuccess && sf_w2_rep != nullptr)
+      e = fvq::launch_replicate_w_scales(lin2->scale, d, f, sf_w2_rep, st);
+  } else {
+    e = fvq::launch_amax_quantize(x, rows, d, g_x, codes_x, sf_x, amax_ws, amax_h, lin2->scale, d,
+                                  f, sf_w2_rep, wait_limit(), fvq::error_word_ptr(), st);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "fvq_nvfp4_ffn quantize(x) launch");
   mark(1);
-  // 2. h = bf16(gelu(bf16(bf16(alpha1 * acc) + b1))), amax_h = max |h|
-  if (int rc = gemm_impl(codes_x, sf_x, g_x, lin1->qweight, lin1->scale, lin1->global_sf, nullptr,
-                         lin1->bias, h, rows, f, d, FVQ_EPI_GELU_AMAX, amax_h, st))
-    return rc;
+  // 2. h = bf16(gelu(bf16(bf16(alpha1 * acc) + b1))), amax_h = max |h|; y_amax zeroed for
+  //    step 4
+  {
+    fvq::QuantOut q;
+    q.zero_word = y_amax;
+    const char* why = nullptr;
+    e = fvq::launch_gemm(codes_x, sf_x, g_x, lin1->qweight, lin1->scale, lin1->global_sf, nullptr,
+                         lin1->bias, h, rows, f, d, FVQ_EPI_GELU_AMAX, amax_h, wait_limit(), st,
+                         &why, nullptr, nullptr, nullptr, &q);
+    if (e != cudaSuccess) {
+      if (why) return fail(FVQ_ECUDA, "fvq_nvfp4_ffn GEMM1: %s", why);
+      return cuda_fail(e, "fvq_nvfp4_ffn GEMM1 launch");
+    }
+  }
   mark(2);
   // 3. h -> NVFP4 with g_h = 2688 / max(amax_h, 1e-12); h is scratch, so its lines
   //    are dropped from L2 once read
@@ -407,7 +430,7 @@ int ffn_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const fvq_
   mark(3);
   // 4. y = bf16(bf16(alpha2 * acc) + b2)  [then bf16(residual + bf16(gate * y))]
   if (int rc = gemm_impl(codes_h, sf_h, g_h, lin2->qweight, lin2->scale, lin2->global_sf, nullptr,
-                         lin2->bias, y, rows, d, f, residual ? 2 : FVQ_EPI_BF16, nullptr, st,
+                         lin2->bias, y, rows, d, f, residual ? 2 : FVQ_EPI_BF16, y_amax, st,
                          sf_w2_rep, residual, gate))
     return rc;
   mark(4);
@@ -420,6 +443,21 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
                   uint16_t* y, void* workspace, size_t workspace_bytes, void* stream) {
   return ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes,
                   static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int fvq_nvfp4_ffn_chain(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                        const fvq_linear* lin2, uint16_t* y, const float* x_amax, float* y_amax,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (y_amax != nullptr && static_cast<const void*>(y_amax) == static_cast<const void*>(x_amax))
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_chain: y_amax must not alias x_amax (the call zeroes "
+                "y_amax while its first launch may still read x_amax)");
+  if (x_amax != nullptr && !aligned4(x_amax))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_ffn_chain: x_amax must be 4-byte aligned");
+  if (y_amax != nullptr && !aligned4(y_amax))
+    return fail(FVQ_EALIGN, "fvq_nvfp4_ffn_chain: y_amax must be 4-byte aligned");
+  return ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes,
+                  static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, nullptr, x_amax,
+                  y_amax);
 }
 
 size_t fvq_nvfp4_ffn_fused_workspace_bytes(int64_t rows, int64_t d_model, int64_t d_ff) {
@@ -608,10 +646,14 @@ int fvq_nvfp4_ffn_block(const uint16_t* x, int64_t rows, const uint16_t* shift,
   return ffn_impl(x, rows, lin1, lin2, out, workspace, ffn_bytes, st, nullptr, x, gate, &ln);
 }
 
-int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
-                          const fvq_linear* lin2, uint16_t* y, void* workspace,
-                          size_t workspace_bytes, void* stream, float* kernel_ms) {
+namespace {
+
+int ffn_profile_impl(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                     const fvq_linear* lin2, uint16_t* y, const float* x_amax, float* y_amax,
+                     void* workspace, size_t workspace_bytes, void* stream, float* kernel_ms) {
   if (kernel_ms == nullptr) return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_profile: kernel_ms is NULL");
+  if (y_amax != nullptr && static_cast<const void*>(y_amax) == static_cast<const void*>(x_amax))
+    return fail(FVQ_EINVAL, "fvq_nvfp4_ffn_chain_profile: y_amax must not alias x_amax");
   if (int rc = check_device()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaEvent_t ev[5];
@@ -623,7 +665,8 @@ int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin
   if (made < 5) {
     rc = fail(FVQ_ECUDA, "fvq_nvfp4_ffn_profile: cudaEventCreate failed");
   } else {
-    rc = ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes, st, ev);
+    rc = ffn_impl(x, rows, lin1, lin2, y, workspace, workspace_bytes, st, ev, nullptr, nullptr,
+                  nullptr, x_amax, y_amax);
     if (rc == FVQ_OK) {
       cudaError_t e = cudaEventSynchronize(ev[4]);
       for (int i = 0; e == cudaSuccess && i < 4; ++i)
@@ -633,6 +676,23 @@ int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin
   }
   for (int i = 0; i < made; ++i) cudaEventDestroy(ev[i]);
   return rc;
+}
+
+}  // namespace
+
+int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                          const fvq_linear* lin2, uint16_t* y, void* workspace,
+                          size_t workspace_bytes, void* stream, float* kernel_ms) {
+  return ffn_profile_impl(x, rows, lin1, lin2, y, nullptr, nullptr, workspace, workspace_bytes,
+                          stream, kernel_ms);
+}
+
+int fvq_nvfp4_ffn_chain_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                                const fvq_linear* lin2, uint16_t* y, const float* x_amax,
+                                float* y_amax, void* workspace, size_t workspace_bytes,
+                                void* stream, float* kernel_ms) {
+  return ffn_profile_impl(x, rows, lin1, lin2, y, x_amax, y_amax, workspace, workspace_bytes,
+                          stream, kernel_ms);
 }
 
 // ---------------------------------------------------------------- FP8 (W8A8) mode

@@ -26,6 +26,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "fvq_gelu.cuh"
 #include "fvq_internal.h"
 #include "fvq_ptx.cuh"
 
@@ -54,18 +55,6 @@ constexpr int kMaxResidentKSteps = (512 - 272) / 8;  // W scales of up to K = 19
 constexpr int kBarrierBytes = 256;
 constexpr int kStagingBytes = BM * BN * 2;       // bf16 tile staged for coalesced stores
 
-// GELU of a bf16 input is a function of 16 bits.  Inputs with exponent field
-// in [107, 130) (|x| in [2^-20, 8)) are tabulated per CTA in shared memory
-// (computed with the exact fp32 formula at kernel start); the rest take short
-// exact paths (gelu_bf16).  The range reaches down to 2^-20 because the
-// intermediate of a deep stack is small: its pre-activations shrink to a
-// standard deviation near 0.02, where 1% of them lie below 2^-12.  Entry
-// index: ((bits & 0x7FFF) - 0x3580) + sign * 2944, 2 x 2944 entries (11.5 KB).
-constexpr uint32_t kGeluTabLo = 107u << 7;       // 0x3580 = 2^-20
-constexpr uint32_t kGeluTabSpan = 23u << 7;      // 0xB80: magnitudes below 8.0
-constexpr int kGeluTabEntries = 2 * kGeluTabSpan;
-constexpr int kGeluTabBytes = kGeluTabEntries * 2;
-static_assert(kGeluTabBytes % 16 == 0, "table keeps what follows it 16-byte aligned");
 constexpr int kStageRowBytes = 128;              // one epilogue row: 64 bf16 columns
 constexpr int kWarpStagingBytes = 32 * kStageRowBytes;
 
@@ -82,9 +71,9 @@ template <int kEpi, bool kResident, bool kRepSfb = false>
 struct Plan {
   static constexpr int kStageBytes =
       kABytes + kBBytes + kSfaBytes + (kResident ? 0 : (kRepSfb ? kSfbRepBytes : kSfbBytes));
-  static constexpr int kStages =
-      kEpi == 3 ? (kResident ? 4 : 3) : (kEpi != 1 ? (kRepSfb ? 3 : 4) : (kResident ? 3 : 2));
   static constexpr bool kStaged = kEpi == 1;
+  static constexpr int kStages =
+      kEpi == 3 ? (kResident ? 4 : 3) : (!kStaged ? (kRepSfb ? 3 : 4) : (kResident ? 3 : 2));
   static constexpr bool kGelu = kEpi == 1 || kEpi == 3;
   static constexpr bool kPreloadInStage = kResident && !kStaged;
   static constexpr int kStagingOff = kStages * kStageBytes;
@@ -152,102 +141,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
-}
-
-// GELU, tanh approximation, evaluated in fp32 as torch does for bf16 inputs.
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float kBeta = 0.7978845608028654f;  // sqrt(2 / pi)
-  const float kKappa = 0.044715f;
-  const float x_cube = x * x * x;
-  const float inner = kBeta * (x + kKappa * x_cube);
-  return 0.5f * x * (1.0f + tanhf(inner));
-}
-
-__device__ __noinline__ uint32_t gelu_bf16_exact(uint32_t x_bits) {
-  return __bfloat16_as_ushort(__float2bfloat16_rn(gelu_tanh(__uint_as_float(x_bits << 16))));
-}
-
-__device__ __forceinline__ void gelu_table_init(uint16_t* tab, int tid, int nthreads) {
-  for (int i = tid; i < kGeluTabEntries; i += nthreads) {
-    const uint32_t neg = static_cast<uint32_t>(i) >= kGeluTabSpan ? 1u : 0u;
-    const uint32_t off = static_cast<uint32_t>(i) - neg * kGeluTabSpan;
-    tab[i] = static_cast<uint16_t>(gelu_bf16_exact((neg << 15) | (kGeluTabLo + off)));
-  }
-}
-
-// bf16(gelu(x)) for |x| < 2^-12 (zeros and subnormals included).  There the fp32
-// formula is 0.5x * (1 + t) with |t| = |tanh(sqrt(2/pi)(x + 0.044715x^3))| < 2^-12: for
-// a normal x, 0.5x is a bf16 value and the factor (1 + t) moves it by far less than
-// half a bf16 ulp, so the result rounds back to 0.5x; for a subnormal x, t is so small
-// that 1 + t == 1 in fp32.  Either way the result is bf16_rn(0.5x) (0.5x exact in
-// fp32, then one rounding).  The GPU test compares every bf16 input with torch.
-__device__ __forceinline__ uint32_t gelu_bf16_tiny(uint32_t x_bits) {
-  return __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn(__uint_as_float(x_bits << 16), 0.5f)));
-}
-
-// bf16(gelu(x)) for a bf16 input, bit-identical to the exact formula.  For
-// 8 <= |x| (finite, and +inf) the fp32 tanh saturates to +-1, so the formula
-// gives x itself for positive x and -0 for negative x; below 2^-12 see
-// gelu_bf16_tiny; only -inf and NaN evaluate the formula.
-__device__ __forceinline__ uint32_t gelu_bf16(uint32_t x_bits, const uint16_t* tab) {
-  const uint32_t mag = x_bits & 0x7FFFu;
-  const uint32_t off = mag - kGeluTabLo;
-  if (off < kGeluTabSpan) return tab[off + ((x_bits >> 15) & 1u) * kGeluTabSpan];
-  if (mag < kGeluTabLo) return gelu_bf16_tiny(x_bits);
-  if (mag < 0x7F80u) return (x_bits & 0x8000u) ? 0x8000u : x_bits;
-  if (x_bits == 0x7F80u) return x_bits;
-  return gelu_bf16_exact(x_bits);
-}
-
-__device__ __noinline__ uint32_t gelu_bf16x2_slow(uint32_t hv, const uint16_t* tab) {
-  return gelu_bf16(hv & 0xFFFFu, tab) | (gelu_bf16(hv >> 16, tab) << 16);
-}
-
-__device__ __forceinline__ uint32_t min_u16x2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("min.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
-  uint32_t r;
-  asm("ld.shared.u16 %0, [%1];" : "=r"(r) : "r"(addr));
-  return r;
-}
-
-// GELU of four bf16x2 words.  Per word both magnitude offsets are formed in one
-// 32-bit subtraction and clamped to the last entry in one min.u16x2, so the two
-// lookups stay inside the table whatever the input; a negative half adds the
-// table's span to its index.  There is no branch between the eight lookups, so all
-// can be in flight at once; a word with a half that was clamped (outside
-// [2^-20, 8), or a borrow from the low half) is redone through gelu_bf16 afterwards.  tab_base is the
-// table's shared-memory address.
-__device__ __forceinline__ void gelu_bf16x2_x4(uint32_t (&w)[4], uint32_t tab_base,
-                                               const uint16_t* tab) {
-  uint32_t res[4];
-  uint32_t slow = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t d = (w[j] & 0x7FFF7FFFu) - ((kGeluTabLo << 16) | kGeluTabLo);
-    const uint32_t c = min_u16x2(d, ((kGeluTabSpan - 1) << 16) | (kGeluTabSpan - 1));
-    const uint32_t off2 = (c + ((w[j] >> 15) & 0x00010001u) * kGeluTabSpan) << 1;
-    res[j] = __byte_perm(lds_u16(tab_base + (off2 & 0xFFFFu)), lds_u16(tab_base + (off2 >> 16)),
-                         0x5410);
-    slow |= static_cast<uint32_t>(c != d) << j;
-  }
-  if (slow != 0) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if ((slow >> j) & 1u) res[j] = gelu_bf16x2_slow(w[j], tab);
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) w[j] = res[j];
 }
 
 // alpha * (lo, hi) with one mul.rn.f32x2 (two IEEE products), rounded to a bf16x2 pair.
@@ -587,6 +480,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
     }
     grid_dependency_wait();
+    if (kEpi == 1 && qo.zero_word != nullptr && blockIdx.x == 0 && threadIdx.x == 64)
+      *qo.zero_word = 0.0f;
     // kEpi 3: the intermediate's provisional encode scale and its loop invariants
     float gq = 0.0f, r6 = 0.0f, rgq = 0.0f;
     uint32_t qflags = 0;
@@ -742,9 +637,19 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
             for (int j = 0; j < 4; ++j) o[j] = add_bf16x2(xw[j], mul_bf16x2(gw[j], o[j]));
           }
-          if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+          if (row < m) {
+            *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) amax2 = bmax2(amax2, o[j] & 0x7FFF7FFFu);
+          }
         }
       }
+    }
+    if ((kEpi == 0 || kEpi == 2) && amax_out != nullptr) {
+      // max |out| (NaN ignored, as the amax kernel takes it), for the next layer's quantizer
+      const uint32_t mag = max(amax2 & 0xFFFFu, amax2 >> 16);
+      const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, mag << 16);
+      if (lane == 0 && bits != 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), bits);
     }
     if (kEpi == 1 || kEpi == 3) {
       // the tensor stores must be complete before the CTA exits
@@ -798,6 +703,40 @@ static_assert(PairPlan<true>::kStages <= kPairMaxStages && PairPlan<false>::kSta
               "pair barrier arrays");
 constexpr uint32_t kIdescPair = (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
                                 (static_cast<uint32_t>(2 * BM >> 4) << 24);
+// N = 128 pair tile (a 256 x 128 half of a tile, see PairSeq): 64 W rows per CTA
+constexpr uint32_t kIdescPairHalf = (1u << 7) | (1u << 10) |
+                                    (static_cast<uint32_t>(BN / 2 >> 3) << 17) |
+                                    (static_cast<uint32_t>(2 * BM >> 4) << 24);
+constexpr int kPairQuarterBBytes = kPairBBytes / 2;  // 64 W rows per CTA
+
+// Tiles of one SM pair: tile t = pair + i * pairs, M pair-block fastest.  When the tiles
+// past the last full round number at most half the pairs, each of them is split into
+// two 256 x 128 halves, one per pair, so that the last round takes about half as long
+// (`half` is -1 for a whole tile, else 0 or 1).  Both CTAs of a pair compute the same
+// sequence.
+struct PairSeq {
+  int count, full_rounds, num_m_pairs;
+  bool split;
+  __device__ PairSeq(int tiles, int m_pairs) : num_m_pairs(m_pairs) {
+    const int pairs = gridDim.x / 2, pair = blockIdx.x / 2;
+    count = pair < tiles ? (tiles - 1 - pair) / pairs + 1 : 0;
+    const int rounds = tiles / pairs, rest = tiles - rounds * pairs;
+    split = rest > 0 && 2 * rest <= pairs;
+    full_rounds = rounds;
+    if (split) count = rounds + (pair < 2 * rest ? 1 : 0);
+  }
+  __device__ void at(int i, int& mbp, int& nb, int& half) const {
+    const int pairs = gridDim.x / 2, pair = blockIdx.x / 2;
+    int t = pair + i * pairs;
+    half = -1;
+    if (split && i == full_rounds) {
+      t = full_rounds * pairs + (pair >> 1);
+      half = pair & 1;
+    }
+    mbp = t % num_m_pairs;
+    nb = t / num_m_pairs;
+  }
+};
 
 struct PairBarriers {
   uint64_t full[kPairMaxStages];    // even CTA: both CTAs' stage landed
@@ -816,12 +755,13 @@ template <int kEpi, bool kRawSfb>
 __global__ void __launch_bounds__(kNumThreads, 1)
     nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                            const __grid_constant__ CUtensorMap tmap_b_half,
+                           const __grid_constant__ CUtensorMap tmap_b_quarter,
                            const __grid_constant__ CUtensorMap tmap_sfa,
                            const __grid_constant__ CUtensorMap tmap_sfb,
                            const float* __restrict__ g_a, const float* __restrict__ g_w,
                            const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int m,
                            int n, int k, uint64_t wait_limit, const uint16_t* __restrict__ residual,
-                           const uint16_t* __restrict__ gate) {
+                           const uint16_t* __restrict__ gate, float* amax_out) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
   if ((smem_u32(smem) & 1023u) != 0) {
@@ -836,15 +776,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool even = rank == 0;
-  const int pairs = gridDim.x / 2, pair = blockIdx.x / 2;
   // ragged m: the last pair tile may hold fewer than 256 rows; a CTA whose 128 rows lie
   // wholly past m loads the last valid row block instead (so every TMA box starts inside
   // A) and stores nothing
   const int num_m_pairs = (m + 2 * BM - 1) / (2 * BM);
   const int num_m_blocks = (m + BM - 1) / BM;
   const int num_n_blocks = n / BN;
-  const int tiles = num_m_pairs * num_n_blocks;
-  const int count = pair < tiles ? (tiles - 1 - pair) / pairs + 1 : 0;  // same in both CTAs
+  const PairSeq seq(num_m_pairs * num_n_blocks, num_m_pairs);  // same in both CTAs
+  const int count = seq.count;
   const int num_k_tiles = k / BK;
   const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
 
@@ -861,6 +800,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     fence_proxy_async_smem();
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_b_half);
+    prefetch_tmap(&tmap_b_quarter);
     prefetch_tmap(&tmap_sfa);
     prefetch_tmap(&tmap_sfb);
   }
@@ -887,9 +827,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int i = 0; i < count && !warp_aborted(bars); ++i) {
-        const int t = pair + i * pairs;
-        const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
+        int mbp, nb, half;
+        seq.at(i, mbp, nb, half);
         const int a_block = min(2 * mbp + static_cast<int>(rank), num_m_blocks - 1);  // its rows
+        // a half tile: this CTA's 64 of the half's 128 W rows, the same A and scale loads
+        const uint32_t stage_tx =
+            2u * static_cast<uint32_t>(half < 0 ? kPairStageBytes : kPairStageBytes - kPairQuarterBBytes);
         for (int kt = 0; kt < num_k_tiles; ++kt) {
           if (!warp_wait_cluster_bounded(&bars->empty[stage], phase ^ 1u, wait_limit)) {
             warp_flag_error(bars, kErrWaitProducer);
@@ -901,10 +844,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           uint8_t* ssfb = ssfa + kSfaBytes;
           const uint32_t bar = even_addr(&bars->full[stage]);
           if (elect_one()) {
-            if (even) mbar_arrive_expect_tx(&bars->full[stage], 2 * kPairStageBytes);
+            if (even) mbar_arrive_expect_tx(&bars->full[stage], stage_tx);
             tma_load_2d_pair(sa, &tmap_a, bar, kt * BKB, a_block * BM);
-            tma_load_2d_pair(sb, &tmap_b_half, bar, kt * BKB,
-                             nb * BN + static_cast<int>(rank) * (BN / 2));
+            if (half < 0)
+              tma_load_2d_pair(sb, &tmap_b_half, bar, kt * BKB,
+                               nb * BN + static_cast<int>(rank) * (BN / 2));
+            else
+              tma_load_2d_pair(sb, &tmap_b_quarter, bar, kt * BKB,
+                               nb * BN + half * (BN / 2) + static_cast<int>(rank) * (BN / 4));
             // A scales: atoms 4kt..4kt+3 of 128-row block a_block; W scales: the
             // same atoms of 128-row blocks 2nb and 2nb+1 (raw), or the 32
             // replicated atoms of K steps 4kt..4kt+3 of N block nb
@@ -940,6 +887,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       bool issued_any = false;
       bool ok = true;
       for (int i = 0; ok && i < count && !warp_aborted(bars); ++i) {
+        int mbp_unused, nb_unused, half;
+        seq.at(i, mbp_unused, nb_unused, half);
+        // a half tile: N = 128 MMAs on the first 64 W rows of each CTA's stage and the
+        // half's 4 of the 8 W-scale columns per K step
+        const uint32_t idesc = half < 0 ? kIdescPair : kIdescPairHalf;
+        const uint32_t sfb_off = half > 0 ? 4u : 0u;
         if (!warp_wait_cluster_bounded(&bars->acc_empty, (static_cast<uint32_t>(i) & 1u) ^ 1u,
                                        wait_limit)) {
           warp_flag_error(bars, kErrWaitMma);
@@ -978,8 +931,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               mma_nvf4_pair(tmem, adesc + static_cast<uint64_t>(2 * j),
-                            bdesc + static_cast<uint64_t>(2 * j), kIdescPair, tmem + kSfaCol + 4 * j,
-                            tmem + kSfbCol + 8 * j, (kt > 0 || j > 0) ? 1u : 0u);
+                            bdesc + static_cast<uint64_t>(2 * j), idesc, tmem + kSfaCol + 4 * j,
+                            tmem + kSfbCol + 8 * j + sfb_off, (kt > 0 || j > 0) ? 1u : 0u);
             }
             tc_commit_pair(smem_u32(&bars->empty[stage]));
             tc_commit_pair(empty_odd);
@@ -1017,14 +970,21 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     uint64_t alpha2;
     asm("mov.b64 %0, {%1, %1};" : "=l"(alpha2) : "f"(alpha));
     const uint32_t acc_empty_addr = even_addr(&bars->acc_empty);
+    uint32_t amax2 = 0;  // max |out| of the low and high columns (amax_out)
     for (int i = 0; i < count; ++i) {
       if (!mbar_wait_cluster_bounded(&bars->acc_full, static_cast<uint32_t>(i) & 1u, wait_limit)) {
         flag_error(bars, kErrWaitEpilogue);
         break;
       }
       tc_fence_after();
-      const int t = pair + i * pairs;
-      const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
+      int mbp, nb, half;
+      seq.at(i, mbp, nb, half);
+      if (half >= 0 && quarter >= 2) {
+        // a half tile has 128 accumulator columns: this warp's 64 are not part of it
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty_addr);
+        continue;
+      }
       uint32_t r[64];
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + col_base;
       tmem_ld_32x32b_x32(taddr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
@@ -1036,7 +996,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t y[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) y[j] = scale_pack_bf16x2(r[2 * j], r[2 * j + 1], alpha2);
-      const int col0 = nb * BN + col_base;
+      const int col0 = nb * BN + (half > 0 ? BN / 2 : 0) + col_base;
       const int row = mbp * 2 * BM + static_cast<int>(rank) * BM + trow;
       uint16_t* dst = out + static_cast<int64_t>(row) * n + col0;
 #pragma unroll
@@ -1062,8 +1022,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
           for (int j = 0; j < 4; ++j) o[j] = add_bf16x2(xw[j], mul_bf16x2(gw[j], o[j]));
         }
-        if (row < m) *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+        if (row < m) {
+          *reinterpret_cast<uint4*>(dst + c) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) amax2 = bmax2(amax2, o[j] & 0x7FFF7FFFu);
+        }
       }
+    }
+    if (amax_out != nullptr) {
+      // max |out| (NaN ignored, as the amax kernel takes it), for the next layer's quantizer
+      const uint32_t mag = max(amax2 & 0xFFFFu, amax2 >> 16);
+      const uint32_t bits = __reduce_max_sync(0xFFFFFFFFu, mag << 16);
+      if (lane == 0 && bits != 0) atomicMax(reinterpret_cast<unsigned int*>(amax_out), bits);
     }
   }
 
@@ -1810,11 +1780,13 @@ bool make_scale_maps(CUtensorMap* sfa, CUtensorMap* sfb, const uint8_t* a_sf, in
 
 template <int kEpi, bool kRawSfb>
 cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
+                             const CUtensorMap& mb_quarter,
                              const CUtensorMap& msfa, const CUtensorMap& msfb, const float* g_a,
                              const float* g_w,
                              const uint16_t* bias, uint16_t* out, int m, int n, int k,
                              uint64_t wait_limit, cudaStream_t st,
-                             const uint16_t* residual = nullptr, const uint16_t* gate = nullptr) {
+                             const uint16_t* residual = nullptr, const uint16_t* gate = nullptr,
+                             float* amax_out = nullptr) {
   static ContextCache attr_done;
   if (cudaError_t e = ensure_max_dynamic_smem(
           attr_done, reinterpret_cast<const void*>(nvfp4_gemm_pair_kernel<kEpi, kRawSfb>),
@@ -1822,7 +1794,7 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
     return e;
   const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * (n / BN);
   int pairs = sm_count() / 2;
-  if (pairs > tiles) pairs = tiles;
+  if (pairs > 2 * tiles) pairs = 2 * tiles;  // up to two pairs per tile: halves (PairSeq)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
   cfg.blockDim = dim3(kNumThreads);
@@ -1837,8 +1809,9 @@ cudaError_t launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb_half,
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, nvfp4_gemm_pair_kernel<kEpi, kRawSfb>, ma, mb_half, msfa, msfb,
-                            g_a, g_w, bias, out, m, n, k, wait_limit, residual, gate);
+  return cudaLaunchKernelEx(&cfg, nvfp4_gemm_pair_kernel<kEpi, kRawSfb>, ma, mb_half, mb_quarter,
+                            msfa, msfb,
+                            g_a, g_w, bias, out, m, n, k, wait_limit, residual, gate, amax_out);
 }
 
 template <int kEpi>
@@ -1975,11 +1948,13 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
   if (epilogue == 1) {
     // W scales stay in TMEM when they fit and every N block gets a CTA
     const bool resident = (k / 64) <= kMaxResidentKSteps && (n / BN) <= sm_count();
+    QuantOut q;
+    if (qo != nullptr) q.zero_word = qo->zero_word;
     if (resident)
       return launch_gemm_t<1, true>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
-                                    amax_out, wait_limit, st);
+                                    amax_out, wait_limit, st, nullptr, nullptr, q);
     return launch_gemm_t<1, false>(ma, mb, mo, a_sf, w_sf, g_a, g_w, alpha, bias, out, mi, ni, ki,
-                                   amax_out, wait_limit, st);
+                                   amax_out, wait_limit, st, nullptr, nullptr, q);
   }
   if (epilogue == 2) {
     if (residual == nullptr || gate == nullptr) {
@@ -1988,15 +1963,17 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
     }
     if (gemm_pairs_raw_scales(m) && alpha == nullptr && w_sf != nullptr) {
       alignas(64) CUtensorMap mb_half;
+      alignas(64) CUtensorMap mb_quarter;
       alignas(64) CUtensorMap msfa;
       alignas(64) CUtensorMap msfb;
       if (!make_code_map(&mb_half, w_codes, n, k, BN / 2) ||
+          !make_code_map(&mb_quarter, w_codes, n, k, BN / 4) ||
           !make_scale_maps(&msfa, &msfb, a_sf, (m + BM - 1) / BM, w_sf, false, n, k)) {
         if (why) *why = "cuTensorMapEncodeTiled failed for the SM-pair GEMM";
         return cudaErrorInvalidValue;
       }
-      return launch_gemm_pair<2, true>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
-                                       wait_limit, st, residual, gate);
+      return launch_gemm_pair<2, true>(ma, mb_half, mb_quarter, msfa, msfb, g_a, g_w, bias, out, mi,
+                                       ni, ki, wait_limit, st, residual, gate, amax_out);
     }
     if (w_sf_rep == nullptr) {
       if (why) *why = "the one-SM gated-residual epilogue needs replicated W scales";
@@ -2012,19 +1989,21 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
   const bool pair_rep = have_rep && (g_pairing == 2 || !have_raw);
   if (gemm_pairs(m, epilogue) && alpha == nullptr && (have_raw || have_rep)) {
     alignas(64) CUtensorMap mb_half;
+    alignas(64) CUtensorMap mb_quarter;
     alignas(64) CUtensorMap msfa;
     alignas(64) CUtensorMap msfb;
     if (!make_code_map(&mb_half, w_codes, n, k, BN / 2) ||
+        !make_code_map(&mb_quarter, w_codes, n, k, BN / 4) ||
         !make_scale_maps(&msfa, &msfb, a_sf, (m + BM - 1) / BM, pair_rep ? w_sf_rep : w_sf, pair_rep,
                          n, k)) {
       if (why) *why = "cuTensorMapEncodeTiled failed for the SM-pair GEMM";
       return cudaErrorInvalidValue;
     }
     if (pair_rep)
-      return launch_gemm_pair<0, false>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
-                                        wait_limit, st);
-    return launch_gemm_pair<0, true>(ma, mb_half, msfa, msfb, g_a, g_w, bias, out, mi, ni, ki,
-                                     wait_limit, st);
+      return launch_gemm_pair<0, false>(ma, mb_half, mb_quarter, msfa, msfb, g_a, g_w, bias, out, mi,
+                                        ni, ki, wait_limit, st, nullptr, nullptr, amax_out);
+    return launch_gemm_pair<0, true>(ma, mb_half, mb_quarter, msfa, msfb, g_a, g_w, bias, out, mi,
+                                     ni, ki, wait_limit, st, nullptr, nullptr, amax_out);
   }
   if (w_sf_rep != nullptr)
     return launch_gemm_t<0, false, true>(ma, mb, mo, a_sf, w_sf_rep, g_a, g_w, alpha, bias, out, mi,

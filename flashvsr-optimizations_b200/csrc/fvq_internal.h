@@ -134,6 +134,7 @@ struct QuantOut {
   int headroom_log2 = 0;
   float* g_used = nullptr;
   uint32_t* flags = nullptr;
+  float* zero_word = nullptr;  // epilogue 1: set to 0 before any tile (a later GEMM's amax target)
 };
 cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float* g_a,
                         const uint8_t* w_codes, const uint8_t* w_sf, const float* g_w,
@@ -144,6 +145,10 @@ cudaError_t launch_gemm(const uint8_t* a_codes, const uint8_t* a_sf, const float
                         const QuantOut* qo = nullptr);
 // epilogue 2 (replicated W scales only): out = bf16(residual + bf16(gate[n] * y)), y the
 // epilogue-0 result -- the gated residual of a DiT block around its FFN.
+// Epilogues 0 and 2 with amax_out: max |out| over the real rows (bf16 magnitudes, NaN
+// ignored, as launch_amax takes it) is maxed into *amax_out, which must start at 0;
+// epilogue 1 with qo->zero_word: that word is set to 0 before any tile (so that a later
+// GEMM of the same sequence can max into it).
 // FVQ_EPI_BF16 GEMMs with replicated W scales, alpha from the global scales and
 // m % 256 == 0 run on SM pairs (nvfp4_gemm_pair_kernel) when enabled.
 void set_gemm_pairing(int mode);  // 0 off, 1 pairs (raw W scales), 2 pairs (replicated)

@@ -214,6 +214,18 @@ class NVFP4FFN(torch.nn.Sequential):
                     self._h_state[self._h_turn:self._h_turn + 1].copy_(amax_h)
         return y.reshape(*shape[:-1], l2.out_features)
 
+    def chained(self, x: torch.Tensor, x_amax: torch.Tensor | None = None):
+        """(self(x), max |self(x)|) for a stack of FFNs that feed each other directly:
+        x_amax, max |x| as the previous FFN's ``chained`` returned it, spares this call its
+        own pass over x for the global scale (fvq_nvfp4_ffn_chain).  The exact h scaling
+        only; the output equals ``self(x)`` bit for bit."""
+        l1, l2 = self[0], self[2]
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        y, y_amax = ops.nvfp4_ffn_chain(x2, l1.qweight, l1.scale, l1.global_sf, l1.bias,
+                                        l2.qweight, l2.scale, l2.global_sf, l2.bias, x_amax)
+        return y.reshape(*shape[:-1], l2.out_features), y_amax
+
     def modulated(self, x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
                   gate: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
         """The DiT block's FFN step around this module: x + gate * self(LN(x) * (1 + scale) +
@@ -226,6 +238,20 @@ class NVFP4FFN(torch.nn.Sequential):
         y = ops.nvfp4_ffn_block(x2, shift, scale, gate, eps, l1.qweight, l1.scale, l1.global_sf,
                                 l1.bias, l2.qweight, l2.scale, l2.global_sf, l2.bias)
         return y.reshape(shape)
+
+
+class NVFP4FFNStack(torch.nn.ModuleList):
+    """FFNs applied one after another, y = ffn_L(...ffn_1(x)), each NVFP4FFN handing the
+    next the max |y| its second GEMM's epilogue already computed (``NVFP4FFN.chained``), so
+    only the first quantizes its input with a separate amax pass.  The output equals running
+    the modules one by one, bit for bit.  The FFN-only stack of the 30-layer benchmark
+    workloads; the DiT pipeline itself puts attention between its FFNs."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        amax = None
+        for ffn in self:
+            x, amax = ffn.chained(x, amax)
+        return x
 
 
 class FP8FFN(torch.nn.Sequential):

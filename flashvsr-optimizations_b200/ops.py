@@ -291,6 +291,39 @@ def _(x, q1, s1, g1, b1, q2, s2, g2, b2):
     return x.new_empty(x.shape, dtype=torch.bfloat16)
 
 
+@torch.library.custom_op("fvq::nvfp4_ffn_chain", mutates_args=())
+def nvfp4_ffn_chain(x: torch.Tensor, q1: torch.Tensor, s1: torch.Tensor, g1: torch.Tensor,
+                    b1: torch.Tensor | None, q2: torch.Tensor, s2: torch.Tensor, g2: torch.Tensor,
+                    b2: torch.Tensor | None, x_amax: torch.Tensor | None = None
+                    ) -> tuple[torch.Tensor, torch.Tensor]:
+    """nvfp4_ffn for FFNs that feed each other directly (fvq_nvfp4_ffn_chain): returns
+    (y, max |y|), and takes max |x| from the previous call when given, so that x is
+    quantized without its own amax pass.  y equals nvfp4_ffn(x, ...) bit for bit."""
+    _check_cuda("nvfp4_ffn_chain", x, q1, s1, g1, b1, q2, s2, g2, b2, x_amax)
+    _check_bf16("nvfp4_ffn_chain", x)
+    m, d = x.shape
+    f = q1.shape[0]
+    if m == 0:
+        raise RuntimeError("nvfp4_ffn_chain: empty input (the reference's global_scale fails on it)")
+    x = _aligned32(x)
+    y = torch.empty((m, d), dtype=torch.bfloat16, device=x.device)
+    y_amax = torch.empty(1, dtype=torch.float32, device=x.device)
+    if x_amax is not None:
+        x_amax = x_amax.to(torch.float32).reshape(1).contiguous()
+    lib = _lib.load()
+    ws = workspace(x.device, lib.fvq_nvfp4_ffn_workspace_bytes(m, d, f))
+    l1 = _linear_struct(q1, s1, g1, b1, d, f)
+    l2 = _linear_struct(q2, s2, g2, b2, f, d)
+    _lib.call("fvq_nvfp4_ffn_chain", _ptr(x), m, ctypes.byref(l1), ctypes.byref(l2), _ptr(y),
+              _ptr(x_amax), _ptr(y_amax), _ptr(ws), ws.numel(), _stream(x))
+    return y, y_amax
+
+
+@nvfp4_ffn_chain.register_fake
+def _(x, q1, s1, g1, b1, q2, s2, g2, b2, x_amax=None):
+    return x.new_empty(x.shape, dtype=torch.bfloat16), x.new_empty(1, dtype=torch.float32)
+
+
 @torch.library.custom_op("fvq::nvfp4_ffn_fused", mutates_args=("amax_seen", "flags"))
 def nvfp4_ffn_fused(x: torch.Tensor, q1: torch.Tensor, s1: torch.Tensor, g1: torch.Tensor,
                     b1: torch.Tensor | None, q2: torch.Tensor, s2: torch.Tensor, g2: torch.Tensor,

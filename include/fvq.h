@@ -189,6 +189,21 @@ int fvq_nvfp4_ffn(const uint16_t* x, int64_t rows, const fvq_linear* lin1, const
                   uint16_t* y, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * No counterpart in the reference (whose DiT blocks put attention between two
+ * FFNs): fvq_nvfp4_ffn for a stack of FFNs that feed each other directly, each
+ * call handing the next the max |y| it already knows.  x_amax (NULL: computed
+ * as fvq_nvfp4_ffn does) is max |x| as the previous call's y_amax gave it;
+ * then the first launch quantizes x without its own pass over x.  y_amax
+ * (NULL: not produced) receives max |y| (bf16 magnitudes, NaN ignored, as
+ * fvq_amax takes them) from the second GEMM's epilogue; the call sets it to 0
+ * itself, after its first launch.  y_amax must not alias x_amax.  Same
+ * workspace as fvq_nvfp4_ffn; the output equals fvq_nvfp4_ffn's bit for bit.
+ */
+int fvq_nvfp4_ffn_chain(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                        const fvq_linear* lin2, uint16_t* y, const float* x_amax, float* y_amax,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * The FFN with the intermediate never stored in bf16: GEMM1's epilogue applies bias and
  * GELU and quantizes h to NVFP4 itself (codes and 128x4-swizzled E4M3 scales, the
  * activation quantizer's exact per-block recipe), with a provisional encode scale
@@ -259,6 +274,11 @@ int fvq_nvfp4_ffn_block(const uint16_t* x, int64_t rows, const uint16_t* shift,
 int fvq_nvfp4_ffn_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
                           const fvq_linear* lin2, uint16_t* y, void* workspace,
                           size_t workspace_bytes, void* stream, float* kernel_ms);
+/* The same instrumentation around fvq_nvfp4_ffn_chain. */
+int fvq_nvfp4_ffn_chain_profile(const uint16_t* x, int64_t rows, const fvq_linear* lin1,
+                                const fvq_linear* lin2, uint16_t* y, const float* x_amax,
+                                float* y_amax, void* workspace, size_t workspace_bytes,
+                                void* stream, float* kernel_ms);
 
 /*
  * ---------------------------------------------------------------------------
@@ -391,7 +411,7 @@ int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream);
 
 /*
  * Test support: out[i] = bf16(gelu_tanh(in[i])) through the GEMM epilogue's
- * GELU path (a per-CTA table over |x| in [2^-12, 8) plus the exact fp32
+ * GELU path (a per-CTA table over |x| in [2^-20, 8) plus the exact fp32
  * formula elsewhere), so it can be compared with torch over all 65536 inputs.
  */
 int fvq_gelu_bf16_probe(const uint16_t* in, uint16_t* out, int64_t count, void* stream);

@@ -198,12 +198,14 @@ def test_ffn_profile_entry_point_same_output_and_times(ffn_layer):
     assert all(t > 0 for t in ms), list(ms)
 
 
-@pytest.mark.parametrize("mode,m", [(1, 7680), (2, 7680), (1, 300), (2, 300), (1, 1920), (1, 8100)])
+@pytest.mark.parametrize("mode,m", [(1, 7680), (2, 7680), (1, 300), (2, 300), (1, 1920), (1, 8100),
+                                    (1, 3840), (2, 3840)])
 def test_ffn_same_bits_with_and_without_sm_pairs(ffn_layer, mode, m):
     """With fvq_set_gemm_pairing(1 or 2), GEMM2 of the FFN runs on SM pairs (raw or
     replicated W scales), ragged row counts included (300, 1920 and 8100 rows leave the
-    last 256-row pair tile partly or, for one CTA, wholly past m); the output bits equal
-    the one-SM kernel's."""
+    last 256-row pair tile partly or, for one CTA, wholly past m), and with the last
+    partial round split into 256 x 128 halves (7680 and 3840 rows: 180 and 90 tiles on 74
+    pairs; 300 rows: 12 tiles, all split); the output bits equal the one-SM kernel's."""
     from flashvsr_optimizations_b200 import _lib
     ffn, _ = ffn_layer
     x = bits_to_dev(W.student_t(m, W.D_MODEL, seed=9))
