@@ -1173,8 +1173,17 @@ def shard_case(torch, dist, ops, lib, dev, stream, wl, shard_of, steps, warmup) 
     run.x = run.x[:run.rows].contiguous()
     run.bufs = [b[:run.rows] for b in run.bufs]
     ms = timed_steps(torch, dist, dev, stream, 1, lambda i: run.layers(), steps, warmup) / steps
+    # host time to issue one stack's 120 launches (the device is idle when each issue starts)
+    host = []
+    for _ in range(5):
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        run.layers()
+        host.append((time.perf_counter() - t0) * 1e3)
+    torch.cuda.synchronize(dev)
     kt = stack_kernel_timing(torch, dist, dev, 1, run, passes=2)
     return {"workload": wl["name"], "shard_of": shard_of, "rows": run.rows, "ms_per_stack": ms,
+            "host_issue_ms_per_stack": statistics.median(host),
             "tokens_per_s": run.rows / (ms * 1e-3),
             "tflops": run.rows * LAYERS * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12, "kernels_ms": kt}
 
