@@ -709,15 +709,17 @@ constexpr uint32_t kIdescPairHalf = (1u << 7) | (1u << 10) |
                                     (static_cast<uint32_t>(2 * BM >> 4) << 24);
 constexpr int kPairQuarterBBytes = kPairBBytes / 2;  // 64 W rows per CTA
 
-// Tiles of one SM pair: tile t = pair + i * pairs, M pair-block fastest.  When the tiles
-// past the last full round number at most half the pairs, each of them is split into
-// two 256 x 128 halves, one per pair, so that the last round takes about half as long
-// (`half` is -1 for a whole tile, else 0 or 1).  Both CTAs of a pair compute the same
-// sequence.
+// Tiles of one SM pair: tile t = pair + i * pairs, N block fastest, so that the pairs
+// working at one time share few 256-row blocks of A (each is read from HBM once and then
+// from L2 by the N blocks' pairs; with M fastest, an A larger than L2 -- H codes at 15360
+// rows are 69 MB -- went to HBM once per N block).  When the tiles past the last full
+// round number at most half the pairs, each of them is split into two 256 x 128 halves,
+// one per pair, so that the last round takes about half as long (`half` is -1 for a
+// whole tile, else 0 or 1).  Both CTAs of a pair compute the same sequence.
 struct PairSeq {
-  int count, full_rounds, num_m_pairs;
+  int count, full_rounds, num_n_blocks;
   bool split;
-  __device__ PairSeq(int tiles, int m_pairs) : num_m_pairs(m_pairs) {
+  __device__ PairSeq(int tiles, int n_blocks) : num_n_blocks(n_blocks) {
     const int pairs = gridDim.x / 2, pair = blockIdx.x / 2;
     count = pair < tiles ? (tiles - 1 - pair) / pairs + 1 : 0;
     const int rounds = tiles / pairs, rest = tiles - rounds * pairs;
@@ -733,8 +735,8 @@ struct PairSeq {
       t = full_rounds * pairs + (pair >> 1);
       half = pair & 1;
     }
-    mbp = t % num_m_pairs;
-    nb = t / num_m_pairs;
+    nb = t % num_n_blocks;
+    mbp = t / num_n_blocks;
   }
 };
 
@@ -782,7 +784,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int num_m_pairs = (m + 2 * BM - 1) / (2 * BM);
   const int num_m_blocks = (m + BM - 1) / BM;
   const int num_n_blocks = n / BN;
-  const PairSeq seq(num_m_pairs * num_n_blocks, num_m_pairs);  // same in both CTAs
+  const PairSeq seq(num_m_pairs * num_n_blocks, num_n_blocks);  // same in both CTAs
   const int count = seq.count;
   const int num_k_tiles = k / BK;
   const uint64_t teardown_limit = wait_limit > kDefaultWaitLimit ? wait_limit : kDefaultWaitLimit;
