@@ -705,14 +705,14 @@ def quantize_sweep(torch, lib, dev, stream, hbm_peak) -> list:
     return out
 
 
-def fp4_library_sustained(torch, dev, seconds=2.0) -> dict | None:
-    """cuBLASLt NVFP4 (torch._scaled_mm) on the layer's two GEMM shapes, each run back to
-    back for `seconds` so that it sits under the same power cap as the layer: the library's
-    sustained TFLOP/s next to which the layer's GEMMs can be read."""
+def fp4_library_sustained(torch, dev, seconds=2.0, rows=TOKENS) -> dict | None:
+    """cuBLASLt NVFP4 (torch._scaled_mm) on the layer's two GEMM shapes at `rows` rows, each
+    run back to back for `seconds` so that it sits under the same power cap as the layer: the
+    library's sustained TFLOP/s next to which the layer's GEMMs can be read."""
     try:
         out = {}
-        for name, (m, n, k) in (("gemm1_7680x8960x1536", (TOKENS, D_FF, D_MODEL)),
-                                ("gemm2_7680x1536x8960", (TOKENS, D_MODEL, D_FF))):
+        for name, (m, n, k) in ((f"gemm1_{rows}x8960x1536", (rows, D_FF, D_MODEL)),
+                                (f"gemm2_{rows}x1536x8960", (rows, D_MODEL, D_FF))):
             a = torch.randint(0, 256, (m, k // 2), dtype=torch.uint8, device=dev).view(torch.float4_e2m1fn_x2)
             b = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev).view(torch.float4_e2m1fn_x2)
             sa = torch.full((m * k // 16,), 0x38, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
@@ -1272,6 +1272,9 @@ def main():
         except ValueError:
             traffic = None
 
+    # ---- the vendor library (cuBLASLt NVFP4, no epilogue) on this rank's two GEMM shapes
+    lib_shapes = fp4_library_sustained(torch, dev, seconds=1.0, rows=run.rows)
+
     # ---- end to end through the public module API with host buffers
     e2e = stack_e2e(torch, dist, weights, run, dev, world, rank, args.steps, args.warmup)
 
@@ -1294,7 +1297,11 @@ def main():
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": peak_src,
                      "frac_of_sustained": achieved / peak_sus,
-                     "algorithmic_flop_per_launch_pair": gemm_flop},
+                     "algorithmic_flop_per_launch_pair": gemm_flop,
+                     **({"cublaslt_same_shapes_us": {k: v["us"] for k, v in lib_shapes.items()},
+                         "frac_of_cublaslt_same_shapes":
+                             (sum(v["us"] for v in lib_shapes.values()) * 1e-3) / kt["gemm_ms"]}
+                        if lib_shapes else {})},
         "quantize": {"kernel": f"quantize_kernel on the {run.rows}x{D_FF} intermediate",
                      "GBps": kt["quant_h_GBps"], "peak_GBps": hbm, "frac": kt["quant_h_GBps"] / hbm,
                      "ms": kt["quant_h_ms"]},
