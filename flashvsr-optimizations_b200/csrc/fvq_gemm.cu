@@ -1445,7 +1445,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t phase = 0;
       for (int i = 0; i < count && !warp_aborted(bars); ++i) {
         const int t = pair + i * pairs;
-        const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
+        const int nb = t % num_n_blocks, mbp = t / num_n_blocks;  // N block fastest (A reuse in L2)
         // this CTA's 128 rows; a block wholly past the last row loads the last
         // block instead (its rows are never stored), so every box starts inside A
         const int a_row = min((2 * mbp + static_cast<int>(rank)) * BM, ((m - 1) / BM) * BM);
@@ -1554,7 +1554,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const uint32_t acc_empty_addr = even_addr(&bars->acc_empty);
     for (int i = 0; i < count; ++i) {
       const int t = pair + i * pairs;
-      const int mbp = t % num_m_pairs, nb = t / num_m_pairs;
+      const int nb = t % num_n_blocks, mbp = t / num_n_blocks;  // N block fastest (A reuse in L2)
       const int row0 = mbp * 2 * BM + static_cast<int>(rank) * BM;  // this CTA's first row
       const int row = row0 + trow;
       const float sa = row < m ? __ldg(sa_rows + row) : 0.0f;
