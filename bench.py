@@ -87,12 +87,15 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0,
                     help="wall-time budget of the CPU baseline sample")
     ap.add_argument("--case", choices=("stack", "shard", "layer", "layer_fused", "fp8_ffn",
-                                       "pil_resize", "dit_block"),
+                                       "pil_resize", "dit_block", "sustained"),
                     default="stack",
                     help="stack: the benchmark (default); shard: the stack on rank 0's row block "
                          "of a --shard-of N split, on this GPU alone (no collective); layer / "
                          "layer_fused: one fvq_nvfp4_ffn / fvq_nvfp4_ffn_fused layer over --tokens "
-                         "rows, --steps calls (e.g. under a profiler); fp8_ffn / "
+                         "rows, --steps calls (e.g. under a profiler); sustained: each of the "
+                         "layer's launches, cuBLASLt on the same operands and the stack step over "
+                         "--tokens rows, each back to back for seconds under the power cap, with "
+                         "clock, power and energy per launch; fp8_ffn / "
                          "pil_resize / dit_block: only that separate measurement, one JSON line")
     ap.add_argument("--shard-of", type=int, default=8,
                     help="--case shard: the number of ranks whose first row block is run")
@@ -1188,6 +1191,98 @@ def shard_case(torch, dist, ops, lib, dev, stream, wl, shard_of, steps, warmup) 
             "tflops": run.rows * LAYERS * FLOP_PER_TOKEN / (ms * 1e-3) / 1e12, "kernels_ms": kt}
 
 
+def sustained_case(torch, ops, lib, dev, stream, rows, seconds=2.0) -> dict:
+    """Each of the layer's launches, and the whole stack step, run back to back for
+    `seconds` after 1.5 s at load (so the power cap has settled), with NVML sampling the SM
+    clock and power draw: the sustained time per launch, its median clock and power, and
+    the energy per launch.  cuBLASLt NVFP4 (torch._scaled_mm, no epilogue) runs on the same
+    codes and scales for comparison.  Under the cap, time per launch follows energy."""
+    from flashvsr_optimizations_b200 import workloads as W
+    d, f, m = D_MODEL, D_FF, rows
+    x = to_dev(torch, stack_input_rows(STACK_WORKLOADS["c4"], 0, m), dev) if m <= 15360 else \
+        torch.randn(m, d, device=dev, generator=torch.Generator(device=dev).manual_seed(0)).to(torch.bfloat16)
+    w1, b1, w2, b2 = (to_dev(torch, a, dev) for a in W.stack_layer_params(0))
+    gx, g1, g2 = ops.global_scale(x), ops.global_scale(w1), ops.global_scale(w2)
+    qx, sx = ops.nvfp4_quantize(x, gx)
+    q1, s1 = ops.nvfp4_quantize(w1, g1)
+    q2, s2 = ops.nvfp4_quantize(w2, g2)
+    h = torch.empty(m, f, dtype=torch.bfloat16, device=dev)
+    amax = torch.zeros(1, dtype=torch.float32, device=dev)
+    sp = stream.cuda_stream
+
+    def gemm1():
+        lib.fvq_nvfp4_gemm(qx.data_ptr(), sx.data_ptr(), gx.data_ptr(), q1.data_ptr(), s1.data_ptr(),
+                           g1.data_ptr(), b1.data_ptr(), h.data_ptr(), m, f, d, 1, amax.data_ptr(), sp)
+    gemm1()
+    torch.cuda.synchronize(dev)
+    gh = ops.global_scale(h)
+    qh, sh = ops.nvfp4_quantize(h, gh)
+    y = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
+
+    def gemm2():
+        lib.fvq_nvfp4_gemm(qh.data_ptr(), sh.data_ptr(), gh.data_ptr(), q2.data_ptr(), s2.data_ptr(),
+                           g2.data_ptr(), b2.data_ptr(), y.data_ptr(), m, d, f, 0, None, sp)
+
+    def quant_h():
+        ops.nvfp4_quantize(h, gh)
+
+    def lt(a, sa, b, sb):
+        av, bv = a.view(torch.float4_e2m1fn_x2), b.view(torch.float4_e2m1fn_x2)
+        sav, sbv = sa.view(torch.float8_e4m3fn).reshape(-1), sb.view(torch.float8_e4m3fn).reshape(-1)
+        return lambda: torch._scaled_mm(av, bv.t(), sav, sbv, out_dtype=torch.bfloat16)
+    cases = {"gemm1_bias_gelu_amax": gemm1, "quantize_h": quant_h, "gemm2_bias": gemm2}
+    try:
+        cases["cublaslt_gemm1_no_epilogue"] = lt(qx, sx, q1, s1)
+        cases["cublaslt_gemm2_no_epilogue"] = lt(qh, sh, q2, s2)
+    except (AttributeError, RuntimeError):
+        pass
+    weights = StackWeights(torch, ops, dev)
+    run = StackRun(torch, lib, dev, stream, weights, STACK_WORKLOADS["c4"], 1, 0)
+    run.rows = m
+    run.x = run.x[:m].contiguous()
+    run.bufs = [b[:m] for b in run.bufs]
+    cases["stack_step_30_layers"] = run.layers
+    gpu_uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    out = {}
+    for name, fn in cases.items():
+        reps_per_check = 2 if name.startswith("stack") else 20
+        try:
+            for _ in range(reps_per_check):
+                fn()
+            torch.cuda.synchronize(dev)
+        except RuntimeError as e:   # e.g. a torch without NVFP4 _scaled_mm
+            out[name] = {"unavailable": str(e).splitlines()[0][:120]}
+            continue
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < 1.5:
+            for _ in range(reps_per_check):
+                fn()
+            torch.cuda.synchronize(dev)
+        sampler = clock_sampler(gpu_uuid)
+        sampler.start()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 0
+        t1 = time.perf_counter()
+        s_ev.record(stream)
+        while time.perf_counter() - t1 < seconds:
+            for _ in range(reps_per_check):
+                fn()
+            reps += reps_per_check
+            torch.cuda.synchronize(dev)
+        e_ev.record(stream)
+        e_ev.synchronize()
+        clk = sampler.stop()
+        samples = getattr(sampler, "samples", [])
+        power = statistics.median(pw for _, pw, _ in samples) if samples else None
+        us = s_ev.elapsed_time(e_ev) / reps * 1e3
+        out[name] = {"us_per_launch": round(us, 2), "launches": reps, "sm_mhz_median": clk.get("sm_mhz"),
+                     "power_w_median": power, "reasons": clk.get("reasons"),
+                     "energy_mj_per_launch": round(us * 1e-3 * power, 2) if power else None}
+        time.sleep(1.0)
+    return {"rows": m, "seconds_timed": seconds, "note": "1.5 s at load before each timed loop; "
+            "stack_step_30_layers is one fvq_nvfp4_ffn_chain pass over the 30 layers", "cases": out}
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -1224,6 +1319,8 @@ def main():
         elif args.case == "fp8_ffn":
             peak8 = 2.0 * (peaks.get("bf16_tflops_sustained") or 1400.0)
             out = fp8_mode_timing(torch, ops, lib, dev, stream, args.tokens, peak8, steps=args.steps)
+        elif args.case == "sustained":
+            out = sustained_case(torch, ops, lib, dev, stream, args.tokens)
         elif args.case == "dit_block":
             out = dit_block_timing(torch, lib, dev, stream, make_sets(torch, ops, dev, args.tokens, rank)[:4],
                                    args.tokens, hbm, steps=args.steps)
