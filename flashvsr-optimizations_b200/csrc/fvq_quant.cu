@@ -456,10 +456,12 @@ cudaError_t launch_quantize(const uint16_t* x, int64_t rows, int64_t k, const fl
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  // read from the end: an input the previous kernel just wrote (the intermediate, or the
+  // previous layer's output in a stack) has its last-written lines still in L2
   if (scratch_input && (reinterpret_cast<uintptr_t>(x) & 127) == 0)
     return cudaLaunchKernelEx(&cfg, quantize_kernel<true, true>, x, r, bpr, g, amax, g_out, codes,
                               sf, zero_word, div);
-  return cudaLaunchKernelEx(&cfg, quantize_kernel<false, false>, x, r, bpr, g, amax, g_out, codes,
+  return cudaLaunchKernelEx(&cfg, quantize_kernel<true, false>, x, r, bpr, g, amax, g_out, codes,
                             sf, zero_word, div);
 }
 
