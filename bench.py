@@ -12,7 +12,8 @@ latent frames, N(0,1), seed 3), split into N contiguous row blocks of 15360/N ro
 (strong scaling: the total work is fixed as N grows).  Each rank runs the 30 layers on
 its rows with replicated weights (layer l: W ~ N(0, 0.02), bias ~ N(0, 0.01), seeded,
 ``workloads.stack_layer_params(l)``), then one NCCL all-gather over NVLink assembles the
-[15360, 1536] output on every rank; the all-gather is inside the step.  `--workload c5`
+[15360, 1536] output on every rank; the all-gather is inside the step.  The 30 layers' 120
+kernel launches are captured once into a CUDA graph and each step replays it.  `--workload c5`
 runs the 4K-stream batch instead: 64800 tokens (two 135x240 frames, Student-t(4) x 0.5,
 seed 4).  The weights alone (464 MB) and each layer's intermediate are far larger than
 the 126 MB L2, so no step finds its operands in L2.
@@ -292,6 +293,7 @@ class StackRun:
         self.out = (torch.empty(self.total, D_MODEL, dtype=torch.bfloat16, device=dev)
                     if world > 1 else None)
         self.lib, self.sptr, self.structs, self.world = lib, stream.cuda_stream, weights.structs, world
+        self.dev, self.graph, self.graph_out = dev, None, None
 
     def layers(self, profile: list | None = None):
         """The 30 layers on this rank's rows; with `profile`, each layer runs through
@@ -317,8 +319,30 @@ class StackRun:
             cur = out
         return cur
 
+    def capture(self, torch):
+        """The 30 layers' 120 launches captured once into a CUDA graph, which step() then
+        replays on the current stream (the same kernels on the same buffers, no host work per
+        layer).  Warm-up passes run on the capture stream first."""
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        sptr, self.sptr = self.sptr, side.cuda_stream
+        try:
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self.layers()
+            torch.cuda.current_stream(self.dev).wait_stream(side)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=side):
+                self.graph_out = self.layers()
+        finally:
+            self.sptr = sptr
+
     def step(self):
-        y = self.layers()
+        if self.graph is not None:
+            self.graph.replay()
+            y = self.graph_out
+        else:
+            y = self.layers()
         if self.world > 1:
             from flashvsr_optimizations_b200.sharding import gather_rows
             return gather_rows(y, self.total, out=self.out)
@@ -384,15 +408,17 @@ def stack_kernel_timing(torch, dist, dev, world, run, passes) -> dict:
 def stack_e2e(torch, dist, weights, run, dev, world, rank, steps, warmup) -> dict:
     """The stack through the public API with host buffers: per step every rank uploads its
     rows from pinned host memory, runs the 30 NVFP4FFN modules as an NVFP4FFNStack (torch
-    custom op fvq::nvfp4_ffn_chain), all-gathers with sharding.gather_rows, and rank 0 copies
-    the gathered [total, 1536] output to pinned host memory.  Uploads, compute and the
+    custom op fvq::nvfp4_ffn_chain) replayed from a CUDA graph (GraphedFFNStack, one per
+    input buffer), all-gathers with sharding.gather_rows, and rank 0 copies the gathered
+    [total, 1536] output to pinned host memory.  Uploads, compute and the
     download run on three streams, double-buffered, so one step's copies overlap its
     neighbours' compute."""
     from flashvsr_optimizations_b200.ffn_quantization import NVFP4FFNStack
     from flashvsr_optimizations_b200.sharding import gather_rows
     stack = NVFP4FFNStack(weights.modules(torch))
     xh = run.x.cpu().pin_memory()
-    xd = [torch.empty_like(run.x) for _ in range(2)]
+    xd = [run.x.clone() for _ in range(2)]
+    graphs = [stack.graphed(b) for b in xd]   # the stack over each input buffer, one CUDA graph
     out_rows = run.total if world > 1 else run.rows
     outs = ([torch.empty(run.total, D_MODEL, dtype=torch.bfloat16, device=dev) for _ in range(2)]
             if world > 1 else None)
@@ -415,17 +441,15 @@ def stack_e2e(torch, dist, weights, run, dev, world, rank, steps, warmup) -> dic
             up.record(s_up)
         with torch.cuda.stream(s_cmp):
             s_cmp.wait_event(up)
-            y = stack(xd[b])
+            s_cmp.wait_event(done_down[b])   # graph b's output (or outs[b]) has been read out
+            y = graphs[b]()
             if world > 1:
-                s_cmp.wait_event(done_down[b])
                 y = gather_rows(y, run.total, out=outs[b])
             done_cmp[b].record(s_cmp)
         with torch.cuda.stream(s_down):
             s_down.wait_event(done_cmp[b])
             if rank == 0:
                 yh[b].copy_(y, non_blocking=True)
-            if world == 1:
-                y.record_stream(s_down)
             done_down[b].record(s_down)
 
     with torch.no_grad():
@@ -449,7 +473,8 @@ def stack_e2e(torch, dist, weights, run, dev, world, rank, steps, warmup) -> dic
     return {"value": run.total * steps / (ms * 1e-3), "unit": "tokens/s",
             "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
             "steps": steps, "ms_per_step": ms / steps,
-            "api": "NVFP4FFNStack of 30 NVFP4FFN modules (torch custom op fvq::nvfp4_ffn_chain) + "
+            "api": "NVFP4FFNStack of 30 NVFP4FFN modules (torch custom op fvq::nvfp4_ffn_chain), "
+                   "replayed as GraphedFFNStack (one CUDA graph per input buffer) + "
                    "sharding.gather_rows; "
                    "each rank uploads its rows, rank 0 downloads the gathered output; "
                    "three streams, double-buffered"}
@@ -1175,7 +1200,8 @@ def shard_case(torch, dist, ops, lib, dev, stream, wl, shard_of, steps, warmup) 
     run.rows = r1 - r0
     run.x = run.x[:run.rows].contiguous()
     run.bufs = [b[:run.rows] for b in run.bufs]
-    ms = timed_steps(torch, dist, dev, stream, 1, lambda i: run.layers(), steps, warmup) / steps
+    run.capture(torch)   # as the N-GPU benchmark's ranks run it: one CUDA graph replay per stack
+    ms = timed_steps(torch, dist, dev, stream, 1, lambda i: run.step(), steps, warmup) / steps
     # host time to issue one stack's 120 launches (the device is idle when each issue starts)
     host = []
     for _ in range(5):
@@ -1338,7 +1364,8 @@ def main():
     weights = StackWeights(torch, ops, dev, keep_bf16=extras_here and world == 1)
     run = StackRun(torch, lib, dev, stream, weights, wl, world, rank)
 
-    # ---- the timed steps: 30 layers on this rank's rows + the all-gather
+    # ---- the timed steps: 30 layers on this rank's rows (one CUDA graph replay) + the all-gather
+    run.capture(torch)
     gpu_uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     sampler = clock_sampler(gpu_uuid)
     ms = timed_steps(torch, dist, dev, stream, world, lambda i: run.step(), args.steps, args.warmup,

@@ -6,10 +6,10 @@ operators in :mod:`.ops`.  The compute runs in ``libfvq.so`` (C ABI in
 ``include/fvq.h``), hand-written CUDA for sm_100a; there is no CPU fallback.
 """
 from ._lib import FvqError, LIB_PATH, load as load_library
-from .ffn_quantization import (FP8FFN, NVFP4FFN, NVFP4FFNStack, QuantLinear, global_scale, install_ffn,
-                               row_quant)
+from .ffn_quantization import (FP8FFN, NVFP4FFN, NVFP4FFNStack, GraphedFFNStack, QuantLinear, global_scale,
+                               install_ffn, row_quant)
 from . import ops
 
-__all__ = ["install_ffn", "QuantLinear", "NVFP4FFN", "NVFP4FFNStack", "FP8FFN", "global_scale", "row_quant", "ops",
+__all__ = ["install_ffn", "QuantLinear", "NVFP4FFN", "NVFP4FFNStack", "GraphedFFNStack", "FP8FFN", "global_scale", "row_quant", "ops",
            "FvqError",
            "LIB_PATH", "load_library"]

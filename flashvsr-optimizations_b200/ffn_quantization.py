@@ -29,8 +29,10 @@ from __future__ import annotations
 import torch
 
 from . import ops
+from ._lib import load as load_library
 
-__all__ = ["global_scale", "row_quant", "QuantLinear", "NVFP4FFN", "FP8FFN", "install_ffn"]
+__all__ = ["global_scale", "row_quant", "QuantLinear", "NVFP4FFN", "NVFP4FFNStack", "GraphedFFNStack",
+           "FP8FFN", "install_ffn"]
 
 
 def global_scale(x: torch.Tensor) -> torch.Tensor:
@@ -252,6 +254,49 @@ class NVFP4FFNStack(torch.nn.ModuleList):
         for ffn in self:
             x, amax = ffn.chained(x, amax)
         return x
+
+    def graphed(self, x: torch.Tensor) -> "GraphedFFNStack":
+        """This stack over the tensor ``x`` (a fixed buffer the caller refills), captured once
+        into a CUDA graph: see :class:`GraphedFFNStack`."""
+        return GraphedFFNStack(self, x)
+
+
+class GraphedFFNStack:
+    """An :class:`NVFP4FFNStack` over one input buffer, its launches (four per FFN) captured
+    once into a CUDA graph and replayed: ``g()`` runs every layer on the current contents of
+    the buffer given at capture, on the current CUDA stream, and returns the output tensor
+    (the same tensor each time, overwritten by each replay).  No host work per layer, and
+    the programmatic-dependent launches keep their overlap inside the graph; the output
+    equals ``stack(x)`` bit for bit.  The buffer, the weights and the library workspace the
+    capture used stay referenced while this object lives.  Shapes are fixed: a new row count
+    needs a new capture."""
+
+    def __init__(self, stack: NVFP4FFNStack, x: torch.Tensor):
+        if not x.is_cuda or x.dtype != torch.bfloat16 or not x.is_contiguous():
+            raise ValueError("GraphedFFNStack: x must be a contiguous bf16 CUDA tensor")
+        self.stack, self.x = stack, x
+        dev = x.device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.no_grad(), torch.cuda.stream(side):
+            # warm-up on the capture stream: per-context kernel attributes and symbol
+            # addresses are looked up once, and the library workspace of this stream is
+            # allocated outside the capture (it must outlive the graph)
+            for _ in range(2):
+                stack(x)
+            m = x.numel() // x.shape[-1]
+            lin1 = stack[0][0]
+            nbytes = load_library().fvq_nvfp4_ffn_workspace_bytes(m, lin1.in_features,
+                                                                   lin1.out_features)
+            self.workspace = ops.workspace(dev, nbytes)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph, stream=side):
+            self.out = stack(x)
+
+    def __call__(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out
 
 
 class FP8FFN(torch.nn.Sequential):

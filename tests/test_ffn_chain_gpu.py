@@ -91,3 +91,21 @@ def test_chain_rejects_aliased_maxima(ffns):
                                  torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.FVQ_EINVAL
     assert b"alias" in lib.fvq_last_error()
+
+
+@pytest.mark.parametrize("m", [300, 1920])
+def test_graphed_stack_equals_eager(ffns, m):
+    """GraphedFFNStack: the stack's launches captured into one CUDA graph over a fixed input
+    buffer; each replay recomputes from the buffer's current contents, bit-identical to the
+    eager stack."""
+    stack = NVFP4FFNStack(ffns)
+    x = bits_to_dev(W.gaussian(m, W.D_MODEL, seed=7))
+    buf = x.clone()
+    g = stack.graphed(buf)
+    assert torch.equal(g(), stack(x))
+    x2 = bits_to_dev(W.student_t(m, W.D_MODEL, seed=8))
+    buf.copy_(x2)
+    got = g()
+    assert torch.equal(got, stack(x2))
+    assert g() is got                     # the same output tensor, overwritten per replay
+    assert ops.read_device_error() == 0

@@ -87,3 +87,12 @@ def test_fp8_custom_ops_have_fake_kernels():
         z = torch.empty(2, 16, 8, 8, dtype=torch.bfloat16).to(memory_format=torch.channels_last)
         qz, sz = torch.ops.fvq.fp8_quantize_activation(z)
         assert qz.shape == z.shape and qz.stride() == z.stride() and sz.shape == (1,)
+
+
+def test_graphed_stack_rejects_host_and_non_bf16_buffers():
+    """GraphedFFNStack captures over a CUDA bf16 buffer only; there is no host path."""
+    stack = fvq.NVFP4FFNStack([])
+    with pytest.raises(ValueError):
+        fvq.GraphedFFNStack(stack, torch.zeros(4, 8, dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        stack.graphed(torch.zeros(4, 8))
