@@ -1,6 +1,6 @@
 """Whole NVFP4 FFN (QuantLinear -> GELU-tanh -> QuantLinear) on the GPU.
 
-Tolerance: the north-star bar, Frobenius-relative error <= 5e-3 against the
+Tolerance: Frobenius-relative error <= 5e-3 (the bar this path is held to) against the
 reference's own NVFP4 FFN (golden outputs of FlashInfer's kernels on a B200)
 and against the CPU oracle.
 """

@@ -12,7 +12,7 @@ cooperative X quantizer on small grids.
 Checked here, per block:
 * against the reference's own NVFP4 FFN (golden rows made by tests/golden/make_golden.py
   with FlashInfer's kernels on a B200): the 64 seeded rows bit for bit, the output's
-  Frobenius norm within the north-star tolerance, and the global scale of x;
+  Frobenius norm within the 5e-3 relative tolerance, and the global scale of x;
 * against the CPU oracle with this GPU's measured reciprocals, decomposed so that each
   half is pinned on its own: X quantization bit-exact on sampled rows; GEMM1 + bias +
   GELU rows (the sampled rows and the row holding max |h|) within the GEMM tolerance;
@@ -30,7 +30,7 @@ from oracle import nvfp4_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-FFN_TOL = 5e-3    # the north-star bar against the reference FFN
+FFN_TOL = 5e-3    # Frobenius-relative bar against the reference FFN
 GEMM_TOL = 2e-3   # GEMM vs the float64 oracle, Frobenius-relative
 ULPS = 2          # and per element, in bf16 units of the larger magnitude
 
