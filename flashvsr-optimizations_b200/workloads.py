@@ -4,7 +4,7 @@ reference's FFN workloads (Wan-1.3B FFN: d_model 1536, d_ff 8960).
 The reference measures on real video activations and downloaded weights
 (fetch_assets.py), which are not available here; these generators stand in
 for them.  numpy generators are deterministic across machines, so a CPU
-checker and a GPU run see identical bf16 bit patterns.
+oracle and a GPU run see identical bf16 bit patterns.
 """
 from __future__ import annotations
 
@@ -15,7 +15,7 @@ D_FF = 8960
 LAYERS = 30
 FLOP_PER_TOKEN = 2 * D_MODEL * D_FF * 2  # two GEMMs per FFN layer: 55,050,240
 
-# BASELINE workloads (token counts)
+# benchmark workloads (token counts)
 M_CPU_CASE = 1024          # reference torch emulation on CPU, seed 0
 M_ONE_LAYER = 7680         # one layer on one GPU (2 latent frames of 48x80), seed 1
 M_STACK = 15360            # 30-layer stack (4 frames of 48x80), seed 3

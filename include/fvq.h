@@ -405,7 +405,7 @@ int fvq_div_full_probe(const float* a, const float* b, float* out, int64_t n, vo
 
 /*
  * Test support: out[i] = rcp.approx.ftz.f32(in[i]) on the device, the
- * reciprocal the quantizer uses (so a CPU checker can use measured values).
+ * reciprocal the quantizer uses (so a CPU oracle can use measured values).
  */
 int fvq_rcp_approx_probe(const float* in, float* out, int64_t n, void* stream);
 

@@ -1,6 +1,6 @@
 """CPU oracle for the FP8 (E4M3, W8A8) paths (TEST INFRASTRUCTURE ONLY).
 
-This module is the checker, never the product: only ``tests/``,
+This module is a test oracle, never the product: only ``tests/``,
 ``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl reference``
 legs of ``bench.py`` may import it.  The CUDA extension never calls into it.
 

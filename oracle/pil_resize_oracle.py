@@ -1,6 +1,6 @@
 """CPU oracle for the Pillow-exact bicubic resize (TEST INFRASTRUCTURE ONLY).
 
-This module is the checker, never the product: only ``tests/``,
+This module is a test oracle, never the product: only ``tests/``,
 ``__graft_entry__.smoke()`` and the CPU legs of ``bench.py`` may import it.
 
 The reference resizes 426x240 RGB frames to 1704x960, crops 1664x896 and maps
