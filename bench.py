@@ -110,7 +110,7 @@ def env_rank():
 
 # ---------------------------------------------------------------- clocks
 class NvmlClockSampler:
-    """SM clock, power and clock-event reasons read through NVML every 5 ms from a
+    """SM clock, power and clock-event reasons read through NVML every 2 ms from a
     thread of this process, so that even a timed region of a few tens of
     milliseconds is sampled (nvidia-smi takes longer than that to start)."""
 
@@ -134,7 +134,7 @@ class NvmlClockSampler:
                 self.samples.append((sm, pw, rs))
             except nv.NVMLError:
                 pass
-            self._stop.wait(0.005)
+            self._stop.wait(0.002)
 
     def start(self):
         self._t = threading.Thread(target=self._run, daemon=True)
